@@ -1,0 +1,136 @@
+"""The CPU oracle against the reference's own known answers and fixtures.
+
+KATs follow the reference's tests/test_cpu_lightspark.py (int4 packing
+:59-64, SDOT GEMV vs integer reference :71-99, GQA vs einsum :101-122,
+argmax :36-39); ``tests/golden/tiny_decode.npz`` holds logits produced by the
+reference's ``LiteSparkQwen.forward_token`` (see ``tests/golden/make_golden.py``).
+"""
+import hashlib
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+from harsh4b_b200.cache import pack_int4, unpack_int4
+from harsh4b_b200.synthetic import synthetic_checkpoint
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "tiny_decode.npz"
+
+
+def test_int4_packing_known_answer():
+    weights = np.array([[-7, -1, 0, 7], [6, -6, 3, -3]], dtype=np.int8)
+    expected = np.array([[0xF9, 0x70], [0xA6, 0xD3]], dtype=np.uint8)
+    np.testing.assert_array_equal(pack_int4(weights), expected)
+    np.testing.assert_array_equal(unpack_int4(expected), weights)
+    with pytest.raises(ValueError, match=r"\[-7,\+7\]"):
+        pack_int4(np.array([[8, 0]], dtype=np.int8))
+
+
+def _seed41_gemv_case():
+    rng = np.random.default_rng(41)
+    weights = rng.integers(-7, 8, size=(67, 128), dtype=np.int8)
+    activation = rng.integers(-127, 128, size=128, dtype=np.int8)
+    scales = rng.random(67, dtype=np.float32)
+    return rng, weights, activation, scales
+
+
+@pytest.mark.parametrize("scalar", [True, False])
+def test_gemv_matches_integer_reference(scalar):
+    _, weights, activation, scales = _seed41_gemv_case()
+    integer = weights.astype(np.int32) @ activation.astype(np.int32)
+    expected = integer.astype(np.float32) * scales * np.float32(0.007)
+    out, acc = oracle.int4_gemv(activation, pack_int4(weights), scales, 0.007, scalar=scalar)
+    np.testing.assert_array_equal(acc, integer)
+    np.testing.assert_allclose(out, expected, rtol=2e-6, atol=2e-5)
+    # The epilogue order of litespark_int4.cpp:73-74 makes the result exact.
+    np.testing.assert_array_equal(out, integer.astype(np.float32) * np.float32(0.007) * scales)
+
+
+@pytest.mark.parametrize("rows,width", [(1, 2), (5, 34), (67, 136), (130, 1000)])
+def test_gemv_tails_and_odd_shapes(rows, width):
+    rng = np.random.default_rng(rows * 1000 + width)
+    weights = rng.integers(-7, 8, size=(rows, width), dtype=np.int8)
+    x = rng.integers(-127, 128, size=width, dtype=np.int8)
+    scales = rng.random(rows, dtype=np.float32)
+    packed = pack_int4(weights)
+    integer = weights.astype(np.int32) @ x.astype(np.int32)
+    for scalar in (True, False):
+        _, acc = oracle.int4_gemv(x, packed, scales, 1.0, scalar=scalar)
+        np.testing.assert_array_equal(acc, integer)
+
+
+def test_gqa_matches_einsum_reference():
+    rng, *_ = _seed41_gemv_case()
+    kv_heads, groups, context, capacity, head_dim = 2, 3, 7, 11, 16
+    query = rng.standard_normal((kv_heads * groups, head_dim), dtype=np.float32)
+    keys = rng.standard_normal((capacity, kv_heads, head_dim), dtype=np.float32)
+    values = rng.standard_normal((capacity, kv_heads, head_dim), dtype=np.float32)
+    scores = np.empty((kv_heads, groups, capacity), dtype=np.float32)
+    attended = np.empty_like(query)
+    oracle.gqa_decode(query, keys, values, scores, attended, context, kv_heads, groups, head_dim, capacity)
+    s = np.einsum("hgd,thd->hgt", query.reshape(kv_heads, groups, head_dim), keys[:context],
+                  dtype=np.float32) / np.sqrt(np.float32(head_dim))
+    p = np.exp(s - s.max(axis=-1, keepdims=True))
+    p /= p.sum(axis=-1, keepdims=True)
+    reference = np.einsum("hgt,thd->hgd", p, values[:context], dtype=np.float32)
+    np.testing.assert_allclose(attended, reference.reshape(kv_heads * groups, head_dim), rtol=2e-5, atol=2e-5)
+
+
+def test_argmax_known_answer():
+    logits = np.array([-1.0, 3.0, 2.0], dtype=np.float32)
+    assert oracle.sample_logits(logits, [], argmax=True) == 1
+
+
+def test_quantize_activation_contract():
+    x = np.array([0.5, -2.0, 1.0, 0.0, 1.99], dtype=np.float32)
+    q = np.empty(5, dtype=np.int8)
+    scale = oracle.quantize_activation(x, q)
+    assert scale == np.float32(2.0) / np.float32(127.0)
+    qs = np.float32(127.0) / np.float32(2.0)
+    np.testing.assert_array_equal(q, np.clip(np.rint(x * qs), -127, 127).astype(np.int8))
+    assert q[1] == -127
+    zeros = np.zeros(8, dtype=np.float32)
+    assert oracle.quantize_activation(zeros, np.empty(8, np.int8)) == np.float32(1e-5) / np.float32(127)
+    with pytest.raises(ValueError):
+        oracle.quantize_activation(x, np.empty(3, dtype=np.int8))
+
+
+def _digest(checkpoint):
+    digest = hashlib.sha256()
+    for name in sorted(checkpoint.projections):
+        for array in checkpoint.projections[name]:
+            digest.update(np.ascontiguousarray(array).tobytes())
+    digest.update(checkpoint.embedding.tobytes())
+    digest.update(checkpoint.embedding_scales.tobytes())
+    for name in sorted(checkpoint.norms):
+        digest.update(checkpoint.norms[name].tobytes())
+    return digest.hexdigest()
+
+
+def oracle_model(checkpoint, kv_dtype=np.float32):
+    config = checkpoint.config
+    layers = []
+    for index in range(int(config["num_hidden_layers"])):
+        parts = checkpoint.layer(index)
+        layers.append(oracle.OracleLayer(*[oracle.OracleProjection(*p) for p in parts[:4]], *parts[4:]))
+    return oracle.OracleQwen(config, layers, checkpoint.embedding, checkpoint.embedding_scales,
+                             checkpoint.norms["model.norm.weight"], kv_dtype=kv_dtype)
+
+
+def test_oracle_reproduces_reference_decode():
+    golden = np.load(GOLDEN)
+    config = json.loads(str(golden["config"]))
+    checkpoint = synthetic_checkpoint(config, seed=int(golden["seed"]))
+    assert _digest(checkpoint) == str(golden["digest"]), "synthetic generator drifted"
+    model = oracle_model(checkpoint)
+    prompt, tokens = list(golden["prompt"]), list(golden["tokens"])
+    state = model.new_state(len(prompt) + len(tokens))
+    logits = [model.forward_token(int(t), state).copy() for t in prompt]
+    generated = []
+    for step in range(len(tokens)):
+        generated.append(oracle.sample_logits(logits[-1], generated, argmax=True))
+        logits.append(model.forward_token(generated[-1], state).copy())
+    assert generated == tokens
+    np.testing.assert_allclose(np.stack(logits), golden["logits"], rtol=1e-4, atol=1e-5)
