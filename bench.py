@@ -1,0 +1,378 @@
+#!/usr/bin/env python3
+"""Batch-1 Qwen3-4B int4 decode benchmark on B200.
+
+A step is one decode token at batch 1 through the whole model (36 layers +
+LM head + greedy argmax), on the seeded synthetic checkpoint, after a
+128-token prompt. ``value`` times K steps with every input resident in HBM
+(one CUDA graph replay per token, the next token fed back on the device);
+``e2e`` times the same K steps through the public API with a host round trip
+per token (pinned H2D of the token id, D2H of the greedy result).
+
+Under torchrun each rank decodes its own sequence on its own GPU
+(independent replicas, no collective on the data path); ``value`` is the
+sum over ranks of tokens / max-over-ranks time.
+
+``--impl reference`` times the reference's CPU path instead: the oracle's
+restatement of cpu_lightspark.LiteSparkQwen.forward_token with the C GEMV
+(OpenMP over all host cores), since the reference's native kernel is ARM
+NEON only and its litespark-inference dependency is not installable.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "batch-1 decode tok/s Qwen3-4B int4; body-GEMV HBM GB/s vs ~8 TB/s"
+PROMPT = 128
+# dram__bytes_read.sum + dram__bytes_write.sum per body-GEMV launch from the
+# ncu capture summarised in profiles/gemv_body_config0.md (None until captured).
+NCU_TRAFFIC_PER_BYTE = None
+
+
+def parse_args():
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=64)
+    parser.add_argument("--warmup", type=int, default=8)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--kv-dtype", choices=("float16", "float32"), default="float16")
+    parser.add_argument("--seed", type=int, default=0)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    return parser.parse_args()
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML in a thread."""
+
+    def __init__(self, index: int):
+        self.index, self.samples, self.reasons = index, [], set()
+        self._stop = threading.Event()
+        self._thread = None
+        self.max_mhz = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # NVML missing: report no clocks rather than fail
+            self._nvml = None
+            self.error = str(exc)
+            return self
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def _run(self):
+        n = self._nvml
+        names = {
+            "hw_slowdown": getattr(n, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "hw_thermal_slowdown": getattr(n, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "sw_thermal_slowdown": getattr(n, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "sw_power_cap": getattr(n, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_power_brake_slowdown": getattr(n, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self._handle, n.NVML_CLOCK_SM))
+                mask = n.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                self.reasons.update(name for name, bit in names.items() if mask & bit)
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def body_gemv_roofline(torch, model, state, peak_gbs) -> dict:
+    """Average duration of the body GEMV kernel over all 144 launches of a
+    token, each launched alone (no programmatic overlap) and timed with CUDA
+    events on the stream they run on, after a sleep kernel so the host has
+    queued every launch before the first event."""
+    import ctypes
+
+    from harsh4b_b200._lib import check, lib
+
+    stream = state.stream
+    body_bytes = sum(t.numel() * t.element_size() for t in (
+        model.w_qkv, model.s_qkv, model.w_o, model.s_o, model.w_gate_up, model.s_gate_up, model.w_down,
+        model.s_down))
+    head_bytes = model.embedding.numel() + model.embedding_scales.numel() * 4
+    start, mid, end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(50_000_000)
+        start.record(stream)
+        for layer in range(model.n_layers):
+            for stage in (1, 3, 4, 5):
+                check(lib().h4b_decode_stage(ctypes.byref(model.desc), ctypes.byref(state.desc), stage, layer,
+                                             stream.cuda_stream), "h4b_decode_stage")
+        mid.record(stream)
+        check(lib().h4b_decode_stage(ctypes.byref(model.desc), ctypes.byref(state.desc), 6, 0,
+                                     stream.cuda_stream), "h4b_decode_stage")
+        end.record(stream)
+    stream.synchronize()
+    body_s = start.elapsed_time(mid) / 1000.0
+    head_s = mid.elapsed_time(end) / 1000.0
+    launches = 4 * model.n_layers
+    achieved = body_bytes / body_s / 1e9
+    traffic = None
+    if NCU_TRAFFIC_PER_BYTE is not None:
+        traffic = round(body_bytes / launches * NCU_TRAFFIC_PER_BYTE)
+    return {"bound": "hbm", "kernel": "gemv_kernel (body: qkv, o, gate/up, down)",
+            "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s", "frac": round(achieved / peak_gbs, 4),
+            "traffic": traffic, "bytes_per_launch": round(body_bytes / launches),
+            "avg_launch_us": round(body_s / launches * 1e6, 3), "launches": launches,
+            "lm_head_gbs": round(head_bytes / head_s / 1e9, 1), "lm_head_us": round(head_s * 1e6, 2)}
+
+
+def cpu_baseline(checkpoint, prompt, budget_s=20.0) -> dict:
+    """The oracle (restated reference CPU path) on this host's cores: decode
+    tokens after a short prefill until ~budget_s of decode work is done."""
+    import oracle
+
+    threads = oracle.configure_threads(os.cpu_count())
+    sys.path.insert(0, str(ROOT / "tests"))
+    from _models import oracle_model
+
+    model = oracle_model(checkpoint)
+    prefill = 8
+    state = model.new_state(prefill + 256)
+    for token in prompt[:prefill]:
+        logits = model.forward_token(int(token), state)
+    token = int(logits.argmax())
+    # two untimed decode tokens (the reference excludes warm-up tokens too)
+    for _ in range(2):
+        token = int(model.forward_token(token, state).argmax())
+    times = []
+    started = time.perf_counter()
+    while time.perf_counter() - started < budget_s and len(times) < 200:
+        t0 = time.perf_counter()
+        token = int(model.forward_token(token, state).argmax())
+        times.append(time.perf_counter() - t0)
+    value = len(times) / sum(times)
+    return {"value": round(value, 3), "unit": "tok/s", "cores": oracle.max_threads(), "kind": "port",
+            "sample": f"{len(times)} greedy decode tokens at batch 1 after an {prefill}-token prefill "
+                      f"(context {prefill + 3}..{prefill + 2 + len(times)}), config-0 weights, "
+                      f"{threads} OpenMP threads", "cpu": cpu_model()}
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args, rank) -> int:
+    if rank != 0:
+        return 0
+    from harsh4b_b200.synthetic import qwen3_4b_config, synthetic_checkpoint, synthetic_prompt
+
+    import oracle
+
+    oracle.configure_threads(os.cpu_count())
+    sys.path.insert(0, str(ROOT / "tests"))
+    from _models import oracle_model
+
+    config = qwen3_4b_config()
+    checkpoint = synthetic_checkpoint(config, seed=args.seed)
+    prompt = synthetic_prompt(config, PROMPT, seed=args.seed)
+    model = oracle_model(checkpoint)
+    state = model.new_state(PROMPT + args.warmup + args.steps + 1)
+    # Bound the untimed prefill: all 128 prompt tokens unless that would take
+    # more than ~90 s on this host (then the context starts shorter).
+    t0 = time.perf_counter()
+    logits = model.forward_token(int(prompt[0]), state)
+    per_token = time.perf_counter() - t0
+    prefill = min(PROMPT, max(1, int(90.0 / max(per_token, 1e-3))))
+    for token in prompt[1:prefill]:
+        logits = model.forward_token(int(token), state)
+    token = int(logits.argmax())
+    for _ in range(args.warmup):
+        token = int(model.forward_token(token, state).argmax())
+    started = time.perf_counter()
+    for _ in range(args.steps):
+        token = int(model.forward_token(token, state).argmax())
+    elapsed = time.perf_counter() - started
+    value = args.steps / elapsed
+    sample = (f"{args.steps} greedy decode tokens at batch 1 after a {prefill}-token prefill and "
+              f"{args.warmup} warm-up tokens, config-0 weights (seed {args.seed})")
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1000, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int4xint8", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "config0: Qwen3-4B int4 synthetic checkpoint, 128-token random prompt, "
+                               "batch-1 greedy decode", "prompt": prefill, "kv_dtype": "float32",
+                   "parallelism": "replicas"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": oracle.max_threads(), "kind": "port",
+                         "sample": sample, "cpu": cpu_model()},
+        "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, rank, world, local_rank, dist) -> int:
+    import torch
+
+    from harsh4b_b200.model import CudaQwen
+    from harsh4b_b200.synthetic import qwen3_4b_config, synthetic_checkpoint, synthetic_prompt
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    config = qwen3_4b_config()
+    checkpoint = synthetic_checkpoint(config, seed=args.seed)
+    # every replica decodes its own random prompt
+    prompt = synthetic_prompt(config, PROMPT, seed=args.seed + rank)
+    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype=args.kv_dtype, device=device)
+    capacity = PROMPT + args.warmup + args.steps + 1
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+
+    # ---- value: device-resident decode ----
+    state = model.new_state(capacity)
+    for token in prompt:
+        model.forward_token(token, state)
+    first = state.next_token_host()
+    model.generate_greedy(first, state, args.warmup)
+    token = state.next_token_host()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        with torch.cuda.stream(state.stream):
+            start.record(state.stream)
+        model.generate_greedy(token, state, args.steps)
+        with torch.cuda.stream(state.stream):
+            end.record(state.stream)
+        torch.cuda.synchronize()
+    barrier()
+    elapsed = start.elapsed_time(end) / 1000.0
+    last_token = state.next_token_host()
+    status = model.status()
+
+    # ---- e2e: host round trip per token through forward_token ----
+    e2e_state = model.new_state(capacity)
+    for token_id in prompt:
+        model.forward_token(token_id, e2e_state)
+    token = e2e_state.next_token_host()
+    for _ in range(args.warmup):
+        model.forward_token(token, e2e_state)
+        token = e2e_state.next_token_host()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e_start.record(e2e_state.stream)
+    for _ in range(args.steps):
+        model.forward_token(token, e2e_state)
+        token = e2e_state.next_token_host()
+    e_end.record(e2e_state.stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_elapsed = e_start.elapsed_time(e_end) / 1000.0
+
+    # ---- roofline of the dominant kernel ----
+    peaks = measured_peaks()
+    roof_state = model.new_state(capacity)
+    for token_id in prompt[:4]:
+        model.forward_token(token_id, roof_state)
+    roofline = body_gemv_roofline(torch, model, roof_state, peaks["hbm_gbs"])
+    roofline["peak_source"] = peaks["source"]
+    state.close(); e2e_state.close(); roof_state.close()
+
+    times = torch.tensor([elapsed, e2e_elapsed], dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    elapsed, e2e_elapsed = float(times[0]), float(times[1])
+    if rank != 0:
+        return 0
+    value = world * args.steps / elapsed
+    bytes_per_token = model.weight_bytes + model.n_layers * 2 * model.kv_size * 2 * (PROMPT + args.warmup + args.steps // 2)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1000, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int4xint8", "data": "synthetic",
+        "config": {"workload": "config0: Qwen3-4B int4 synthetic checkpoint (seed 0), 128-token random prompt, "
+                               "batch-1 greedy decode", "prompt": PROMPT, "kv_dtype": args.kv_dtype,
+                   "context": [PROMPT + args.warmup, PROMPT + args.warmup + args.steps],
+                   "l2": "inputs larger than L2 (1.82 GB of weights streamed per token)",
+                   "parallelism": f"replicas x{world}"},
+        "e2e": {"value": round(world * args.steps / e2e_elapsed, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": args.steps * (5 * model.n_layers + 3),
+        "step_roofline": {"bytes_per_token": bytes_per_token,
+                          "achieved_gbs": round(bytes_per_token * args.steps / elapsed / 1e9, 1),
+                          "frac": round(bytes_per_token * args.steps / elapsed / 1e9 / peaks["hbm_gbs"], 4)},
+        "roofline": roofline,
+        "clocks": clocks.summary(),
+        "device_status": status,
+        "last_token": last_token,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(checkpoint, prompt)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as torch_dist
+
+        torch.cuda.set_device(local_rank)
+        torch_dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                      device_id=torch.device("cuda", local_rank))
+        dist = torch_dist
+    try:
+        return run_ours(args, rank, world, local_rank, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,178 @@
+// Shared device helpers for the sm_100a decode kernels: status reporting,
+// mbarrier + bulk-copy (TMA engine) primitives, programmatic dependent
+// launch, and block reductions.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/harsh4b_b200.h"
+
+namespace h4b {
+
+// ---- status ------------------------------------------------------------
+// Kernels never trap. A bounded wait that gives up ORs a code into this
+// word; h4b_get_status() reads and clears it from the host. (The library is
+// one translation unit, harsh4b_b200.cu, so this is its only definition.)
+__device__ int g_status = 0;
+
+constexpr int kStatusWaitTimeout = 1;     // an mbarrier wait ran out of time
+constexpr int kStatusBadToken = 2;        // token id outside the vocabulary
+constexpr int kStatusBadPosition = 4;     // decode position beyond capacity
+
+__device__ __forceinline__ void report(int code) { atomicOr(&g_status, code); }
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// A wait gives up after this long; normal waits last microseconds.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+// True once any kernel has given up on a wait: later kernels then skip their
+// work, so a failure costs one wait limit instead of one per launch.
+__device__ __forceinline__ bool wait_failed_before() {
+    return (*reinterpret_cast<volatile int*>(&g_status) & kStatusWaitTimeout) != 0;
+}
+
+// ---- programmatic dependent launch ---------------------------------------
+// Everything before pdl_wait() may only touch data no earlier kernel in the
+// stream writes (weights, scales, tables). pdl_trigger() lets the next
+// kernel's CTAs start their own weight prefetch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---- mbarrier ---------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}"
+                 :: "r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
+                 :: "r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(done) : "r"(smem_addr(bar)), "r"(parity) : "memory");
+    return done != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete. Returns
+// false (and reports) when the time limit passes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - start > limit_ns) {
+            report(kStatusWaitTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
+// 1-D bulk copy global -> shared through the TMA engine, completing on the
+// mbarrier's transaction count. dst, src and bytes must be 16-byte multiples.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
+}
+
+// ---- named barrier among a subset of warps ------------------------------------
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(threads) : "memory");
+}
+
+// ---- reductions -------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Sum over `warps` warps (threads 0 .. 32*warps-1) synchronised with named
+// barrier `bar`; every participating thread gets the total. `scratch` holds
+// at least 32 floats. The order is fixed, so the result is deterministic.
+__device__ __forceinline__ float group_sum(float v, float* scratch, int warps, int bar) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
+    if (lane == 0) scratch[warp] = v;
+    named_sync(bar, warps * 32);
+    float total = 0.f;
+    for (int w = 0; w < warps; ++w) total += scratch[w];
+    named_sync(bar, warps * 32);
+    return total;
+}
+
+__device__ __forceinline__ float group_max(float v, float* scratch, int warps, int bar) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_max(v);
+    if (lane == 0) scratch[warp] = v;
+    named_sync(bar, warps * 32);
+    float total = scratch[0];
+    for (int w = 1; w < warps; ++w) total = fmaxf(total, scratch[w]);
+    named_sync(bar, warps * 32);
+    return total;
+}
+
+// Non-negative floats order like their bit patterns, so an unsigned
+// atomicMax on the bits is an exact, order-independent float max.
+__device__ __forceinline__ void atomic_max_nonneg(float* slot, float value) {
+    atomicMax(reinterpret_cast<unsigned int*>(slot), __float_as_uint(value));
+}
+
+// Per-token absmax int8 quantisation contract (shared with the oracle):
+//   m = max(absmax, 1e-5); qs = 127 / m; q = clamp(rint(v * qs), -127, 127);
+//   dequant scale = m / 127.
+__device__ __forceinline__ float quant_multiplier(float absmax) {
+    return __fdiv_rn(127.0f, fmaxf(absmax, 1e-5f));
+}
+__device__ __forceinline__ float dequant_scale(float absmax) {
+    return __fdiv_rn(fmaxf(absmax, 1e-5f), 127.0f);
+}
+__device__ __forceinline__ int quantize_one(float v, float qs) {
+    int q = __float2int_rn(__fmul_rn(v, qs));
+    return max(-127, min(127, q));
+}
+
+// Argmax key: larger value wins, ties go to the smaller index (numpy's
+// first-occurrence rule). Values are mapped to an order-preserving uint.
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {
+    uint32_t b = __float_as_uint(v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return (static_cast<unsigned long long>(b) << 32) | (0xFFFFFFFFu - index);
+}
+
+}  // namespace h4b
+
+#define H4B_CUDA_TRY(expr)                                   \
+    do {                                                     \
+        cudaError_t _e = (expr);                             \
+        if (_e != cudaSuccess) return static_cast<int>(_e);  \
+    } while (0)

@@ -1,0 +1,520 @@
+// Packed signed-int4 x int8 GEMV for batch-1 decode on sm_100a.
+//
+// Computes, for each weight row r (reference: cpu_kernels/litespark_int4.cpp:22-76),
+//   acc[r] = sum_k w4[r,k] * x8[k]                       (exact int32)
+//   out[r] = float(acc[r]) * act_scale * w_scale[r]       (left to right)
+// with the int8 activation produced inside the kernel (fused prologue) and
+// the consumer of out fused into the epilogue.
+//
+// Data movement: one CTA per SM owns a contiguous range of rows. Its rows
+// are one contiguous byte range of the row-major weight matrix, so a
+// producer warp streams them with 1-D bulk copies (the TMA engine) into a
+// ring of shared-memory stages tracked by mbarriers. The first ring's worth
+// is issued before griddepcontrol.wait: weights do not depend on the
+// previous kernel, so under programmatic dependent launch each GEMV's weight
+// stream overlaps the previous kernel's tail.
+//
+// Math: a lane owns a fixed set of 16-byte weight chunks (32 codes) of
+// every row, so its 32-byte slice of the quantised activation lives in
+// registers for the whole kernel. Each 4-byte weight word holds 8 codes;
+// reading a nibble n as u = n ^ 8 = s + 8 (0..15) turns the even and odd
+// codes into two dp4a operands with no sign extension, and the bias
+// 8 * sum(x) is folded into the lane's starting accumulator.
+#include "common.cuh"
+
+namespace h4b {
+
+enum { PRO_INT8 = 0, PRO_QUANT = 1, PRO_QUANT_ABSMAX = 2, PRO_RMSNORM = 3 };
+enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
+
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kGemvThreads = kConsumers + 32;
+constexpr int kMaxStages = 16;
+constexpr int kMaxSlots = 6;
+constexpr int kSwigluBlock = 4;  // gate/up interleave block (rows)
+constexpr int kRingBytes = 96 * 1024;
+constexpr int kStageTarget = 16 * 1024;
+
+struct GemvArgs {
+    const uint8_t* w;
+    const float* wscale;
+    int rows, width;
+    int row_align;      // rows per partition unit (2 * kSwigluBlock for SwiGLU)
+    int kgroups;        // warps sharing one row (each takes a K segment)
+    int tile_rows;      // rows per ring stage
+    int stages;         // ring depth
+    int rows_cap;       // smem rows reserved per CTA (multiple of 32)
+    const int8_t* x8;   // PRO_INT8 input
+    const float* xin;   // fp32 input
+    const float* gamma; // PRO_RMSNORM weight
+    const float* absmax_in;  // PRO_QUANT_ABSMAX
+    float act_scale;    // PRO_INT8
+    float eps;
+    float* out;
+    int32_t* acc_out;
+    float* act_scale_out;
+    float* absmax_out;
+    unsigned long long* argmax_out;
+};
+
+struct SmemLayout {
+    int red, xq, acc, scale, ring, total;
+};
+
+__host__ __device__ inline SmemLayout smem_layout(int width, int rows_cap, int stages, int stage_bytes) {
+    SmemLayout s;
+    s.red = 2 * kMaxStages * 8;               // barriers first
+    s.xq = s.red + 64 * 4;                    // 32 floats + flags
+    s.acc = s.xq + ((width + 127) & ~127);
+    s.scale = s.acc + rows_cap * 4;
+    s.ring = (s.scale + rows_cap * 4 + 127) & ~127;
+    s.total = s.ring + stages * stage_bytes;
+    return s;
+}
+
+__device__ __forceinline__ int dot_chunk(const uint4 w, const uint4 xa, const uint4 xb, int acc) {
+    // word j of the chunk pairs with activation words (even, odd) = x[2j], x[2j+1]
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    const uint32_t xe[4] = {xa.x, xa.z, xb.x, xb.z};
+    const uint32_t xo[4] = {xa.y, xa.w, xb.y, xb.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t lo = (ww[j] & 0x0F0F0F0Fu) ^ 0x08080808u;
+        const uint32_t hi = ((ww[j] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+        acc = __dp4a(static_cast<int>(lo), static_cast<int>(xe[j]), acc);
+        acc = __dp4a(static_cast<int>(hi), static_cast<int>(xo[j]), acc);
+    }
+    return acc;
+}
+
+// Writes the 8 quantised values of group g (columns 8g..8g+7) as
+// [x0 x2 x4 x6][x1 x3 x5 x7] at xq + 8g.
+__device__ __forceinline__ void store_group(int8_t* xq, int g, const int q[8]) {
+    const uint32_t even = (q[0] & 0xFF) | ((q[2] & 0xFF) << 8) | ((q[4] & 0xFF) << 16) | ((uint32_t)(q[6] & 0xFF) << 24);
+    const uint32_t odd = (q[1] & 0xFF) | ((q[3] & 0xFF) << 8) | ((q[5] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+    *reinterpret_cast<uint2*>(xq + 8 * g) = make_uint2(even, odd);
+}
+
+__device__ __forceinline__ void load8(const float* p, float v[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// Builds the permuted int8 activation in shared memory; returns the dequant
+// scale. Runs on the consumer warps only (named barrier 1).
+template <int PRO>
+__device__ float gemv_prologue(const GemvArgs& a, int8_t* xq, float* red) {
+    const int tid = threadIdx.x;
+    const int groups = a.width >> 3;
+    if constexpr (PRO == PRO_INT8) {
+        for (int g = tid; g < groups; g += kConsumers) {
+            const uint2 raw = *reinterpret_cast<const uint2*>(a.x8 + 8 * g);
+            int q[8];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                q[e] = static_cast<int8_t>((raw.x >> (8 * e)) & 0xFF);
+                q[4 + e] = static_cast<int8_t>((raw.y >> (8 * e)) & 0xFF);
+            }
+            store_group(xq, g, q);
+        }
+        return a.act_scale;
+    } else {
+        float inv = 1.0f;
+        if constexpr (PRO == PRO_RMSNORM) {
+            float ss = 0.f;
+            for (int g = tid; g < groups; g += kConsumers) {
+                float v[8];
+                load8(a.xin + 8 * g, v);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ss = __fmaf_rn(v[e], v[e], ss);
+            }
+            ss = group_sum(ss, red, kConsumerWarps, 1);
+            const float mean = __fdiv_rn(ss, static_cast<float>(a.width));
+            inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+        }
+        float m;
+        if constexpr (PRO == PRO_QUANT_ABSMAX) {
+            m = *a.absmax_in;
+        } else {
+            float local = 0.f;
+            for (int g = tid; g < groups; g += kConsumers) {
+                float v[8], gm[8];
+                load8(a.xin + 8 * g, v);
+                if constexpr (PRO == PRO_RMSNORM) load8(a.gamma + 8 * g, gm);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float n = (PRO == PRO_RMSNORM) ? __fmul_rn(__fmul_rn(v[e], inv), gm[e]) : v[e];
+                    local = fmaxf(local, fabsf(n));
+                }
+            }
+            m = group_max(local, red, kConsumerWarps, 1);
+        }
+        const float qs = quant_multiplier(m);
+        for (int g = tid; g < groups; g += kConsumers) {
+            float v[8], gm[8];
+            int q[8];
+            load8(a.xin + 8 * g, v);
+            if constexpr (PRO == PRO_RMSNORM) load8(a.gamma + 8 * g, gm);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float n = (PRO == PRO_RMSNORM) ? __fmul_rn(__fmul_rn(v[e], inv), gm[e]) : v[e];
+                q[e] = quantize_one(n, qs);
+            }
+            store_group(xq, g, q);
+        }
+        return dequant_scale(m);
+    }
+}
+
+template <int PRO, int EPI, int SLOTS>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int kb = a.width >> 1;
+    const uint32_t stage_bytes = static_cast<uint32_t>(a.tile_rows) * kb;
+    const SmemLayout L = smem_layout(a.width, a.rows_cap, a.stages, stage_bytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kMaxStages;
+    float* red = reinterpret_cast<float*>(smem + L.red);
+    int* flags = reinterpret_cast<int*>(red + 32);  // [0] error, [1] act scale bits, [2] skip
+    int8_t* xq = reinterpret_cast<int8_t*>(smem + L.xq);
+    int32_t* acc_s = reinterpret_cast<int32_t*>(smem + L.acc);
+    float* sc_s = reinterpret_cast<float*>(smem + L.scale);
+    uint8_t* ring = smem + L.ring;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int units = a.rows / a.row_align;
+    const int u0 = static_cast<int>(static_cast<long long>(blockIdx.x) * units / gridDim.x);
+    const int u1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * units / gridDim.x);
+    const int r0 = u0 * a.row_align;
+    const int nrows = (u1 - u0) * a.row_align;
+    const int ntiles = (nrows + a.tile_rows - 1) / a.tile_rows;
+
+    if (tid == 0) {
+        for (int s = 0; s < a.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        flags[0] = 0;
+        flags[2] = wait_failed_before();
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+    if (flags[2]) return;  // before any bulk copy is issued
+
+    if (warp == kConsumerWarps) {
+        // ---------------- producer warp ----------------
+        int issued = 0;
+        auto issue = [&](int t) {
+            const int s = t % a.stages;
+            const int rows_t = min(a.tile_rows, nrows - t * a.tile_rows);
+            const uint32_t bytes = static_cast<uint32_t>(rows_t) * kb;
+            mbar_arrive_expect_tx(&full[s], bytes);
+            bulk_g2s(ring + static_cast<size_t>(s) * stage_bytes,
+                     a.w + static_cast<size_t>(r0 + t * a.tile_rows) * kb, bytes, &full[s]);
+        };
+        if (lane == 0) {
+            const int first = min(a.stages, ntiles);
+            for (int t = 0; t < first; ++t) issue(t);
+            issued = first;
+        }
+        // Row scales are weights too: fetch them before any dependency wait.
+        for (int i = lane; i < nrows; i += 32) sc_s[i] = __ldg(a.wscale + r0 + i);
+        if (lane == 0) {
+            for (int t = a.stages; t < ntiles; ++t) {
+                const int s = t % a.stages;
+                if (!mbar_wait(&empty[s], ((t / a.stages) - 1) & 1)) {
+                    atomicOr(&flags[0], 1);
+                    break;
+                }
+                issue(t);
+                issued = t + 1;
+            }
+            // Never leave the CTA with bulk copies in flight.
+            for (int t = max(0, issued - a.stages); t < issued; ++t)
+                mbar_wait(&full[t % a.stages], (t / a.stages) & 1, 100000000ull);
+        }
+    } else {
+        // ---------------- consumer warps ----------------
+        pdl_wait();
+        if (a.kgroups > 1)
+            for (int i = tid; i < nrows; i += kConsumers) acc_s[i] = 0;
+        const float act_scale = gemv_prologue<(PRO)>(a, xq, red);
+        if (tid == 0) flags[1] = __float_as_int(act_scale);
+        named_sync(1, kConsumers);
+
+        const int chunks = a.width >> 5;
+        const int G = a.kgroups;
+        const int kg = warp % G, rg = warp / G, nrg = kConsumerWarps / G;
+        const int c_begin = kg * chunks / G, c_end = (kg + 1) * chunks / G;
+        uint4 xa[SLOTS], xb[SLOTS];
+        int bias = 0;
+#pragma unroll
+        for (int j = 0; j < SLOTS; ++j) {
+            const int c = c_begin + lane + 32 * j;
+            if (c < c_end) {
+                xa[j] = *reinterpret_cast<const uint4*>(xq + 32 * c);
+                xb[j] = *reinterpret_cast<const uint4*>(xq + 32 * c + 16);
+                const uint32_t words[8] = {xa[j].x, xa[j].y, xa[j].z, xa[j].w, xb[j].x, xb[j].y, xb[j].z, xb[j].w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) bias = __dp4a(static_cast<int>(words[e]), 0x01010101, bias);
+            } else {
+                xa[j] = make_uint4(0, 0, 0, 0);
+                xb[j] = make_uint4(0, 0, 0, 0);
+            }
+        }
+        bias *= -8;
+
+        for (int t = 0; t < ntiles; ++t) {
+            const int s = t % a.stages;
+            if (!mbar_wait(&full[s], (t / a.stages) & 1)) {
+                atomicOr(&flags[0], 1);
+                break;
+            }
+            const uint8_t* tile = ring + static_cast<size_t>(s) * stage_bytes;
+            const int trows = min(a.tile_rows, nrows - t * a.tile_rows);
+            for (int lr = rg; lr < trows; lr += nrg) {
+                const uint8_t* row = tile + static_cast<size_t>(lr) * kb;
+                int acc0 = bias, acc1 = 0;
+#pragma unroll
+                for (int j = 0; j < SLOTS; ++j) {
+                    const int c = c_begin + lane + 32 * j;
+                    if (c < c_end) {
+                        const uint4 w = *reinterpret_cast<const uint4*>(row + 16 * c);
+                        if (j & 1) acc1 = dot_chunk(w, xa[j], xb[j], acc1);
+                        else acc0 = dot_chunk(w, xa[j], xb[j], acc0);
+                    }
+                }
+                const int total = __reduce_add_sync(0xffffffffu, acc0 + acc1);
+                if (lane == 0) {
+                    const int i = t * a.tile_rows + lr;
+                    if (G == 1) acc_s[i] = total;
+                    else atomicAdd(&acc_s[i], total);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+    }
+    __syncthreads();
+    if (flags[0]) return;
+
+    // ---------------- epilogue (all threads) ----------------
+    const float act_scale = __int_as_float(flags[1]);
+    auto value = [&](int i) {
+        return __fmul_rn(__fmul_rn(static_cast<float>(acc_s[i]), act_scale), sc_s[i]);
+    };
+    if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
+        for (int i = tid; i < nrows; i += kGemvThreads) {
+            const float v = value(i);
+            if constexpr (EPI == EPI_STORE) a.out[r0 + i] = v;
+            else a.out[r0 + i] = __fadd_rn(a.out[r0 + i], v);
+            if (a.acc_out) a.acc_out[r0 + i] = acc_s[i];
+        }
+        if (a.act_scale_out && blockIdx.x == 0 && tid == 0) *a.act_scale_out = act_scale;
+    } else if constexpr (EPI == EPI_SWIGLU) {
+        float local = 0.f;
+        const int pairs = nrows >> 1;
+        for (int p = tid; p < pairs; p += kGemvThreads) {
+            const int b = p / kSwigluBlock, j = p % kSwigluBlock;
+            const int gi = 2 * kSwigluBlock * b + j;
+            const float g = value(gi), u = value(gi + kSwigluBlock);
+            // cpu_lightspark.py:451-455: gate / (1 + exp(-gate)) * up
+            const float act = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+            a.out[(r0 >> 1) + p] = act;
+            local = fmaxf(local, fabsf(act));
+        }
+        local = warp_max(local);
+        if (lane == 0) red[warp] = local;
+        __syncthreads();
+        if (tid == 0) {
+            float m = red[0];
+            for (int w = 1; w < kGemvThreads / 32; ++w) m = fmaxf(m, red[w]);
+            atomic_max_nonneg(a.absmax_out, m);
+        }
+    } else {  // EPI_ARGMAX
+        unsigned long long best = 0ull;
+        for (int i = tid; i < nrows; i += kGemvThreads) {
+            const float v = value(i);
+            a.out[r0 + i] = v;
+            const unsigned long long k = argmax_key(v, static_cast<uint32_t>(r0 + i));
+            best = k > best ? k : best;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
+        }
+        unsigned long long* keys = reinterpret_cast<unsigned long long*>(acc_s);
+        __syncthreads();  // acc_s is free now
+        if (lane == 0) keys[warp] = best;
+        __syncthreads();
+        if (tid == 0) {
+            for (int w = 1; w < kGemvThreads / 32; ++w) best = keys[w] > best ? keys[w] : best;
+            best = keys[0] > best ? keys[0] : best;
+            atomicMax(a.argmax_out, best);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host-side planning and launch.
+
+struct GemvPlan {
+    int grid, kgroups, slots, tile_rows, stages, rows_cap, smem;
+};
+
+static int g_sm_count = 0;
+
+int sm_count() {
+    if (g_sm_count == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
+        if (g_sm_count <= 0) g_sm_count = 148;
+    }
+    return g_sm_count;
+}
+
+int plan_gemv(int rows, int width, int row_align, GemvPlan* p) {
+    if (rows <= 0 || width <= 0 || (width & 31) || rows % row_align) return H4B_EINVAL;
+    const int chunks = width >> 5;
+    int G = 1;
+    while ((chunks + 32 * G - 1) / (32 * G) > kMaxSlots && G < kConsumerWarps) G *= 2;
+    const int seg = (chunks + G - 1) / G;
+    const int slots = (seg + 31) / 32;
+    if (slots > kMaxSlots) return H4B_EUNSUPPORTED;
+    const int nrg = kConsumerWarps / G;
+    const int kb = width >> 1;
+    const int m = max(1, kStageTarget / (kb * nrg));
+    const int tile_rows = nrg * m;
+    const int stage_bytes = tile_rows * kb;
+    if (stage_bytes > 64 * 1024) return H4B_EUNSUPPORTED;
+    const int stages = max(2, min(kMaxStages, kRingBytes / stage_bytes));
+    const int units = rows / row_align;
+    const int grid = max(1, min(sm_count(), units));
+    const int rows_cap = (((units + grid - 1) / grid) * row_align + 31) & ~31;
+    const SmemLayout L = smem_layout(width, rows_cap, stages, stage_bytes);
+    if (L.total > 227 * 1024) return H4B_EUNSUPPORTED;
+    *p = GemvPlan{grid, G, slots, tile_rows, stages, rows_cap, L.total};
+    return 0;
+}
+
+template <int PRO, int EPI, int SLOTS>
+static int set_smem_limit() {
+    H4B_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel<PRO, EPI, SLOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      227 * 1024));
+    return 0;
+}
+
+template <int PRO, int EPI>
+static int set_smem_limits() {
+    int r = 0;
+    if ((r = set_smem_limit<PRO, EPI, 1>()) || (r = set_smem_limit<PRO, EPI, 2>()) ||
+        (r = set_smem_limit<PRO, EPI, 3>()) || (r = set_smem_limit<PRO, EPI, 4>()) ||
+        (r = set_smem_limit<PRO, EPI, 5>()) || (r = set_smem_limit<PRO, EPI, 6>()))
+        return r;
+    return 0;
+}
+
+static bool g_prepared = false;
+
+// Raises every GEMV instantiation's dynamic shared-memory limit. Runs once,
+// outside any stream capture.
+int prepare_kernels() {
+    if (g_prepared) return 0;
+    int r = 0;
+    if ((r = set_smem_limits<PRO_INT8, EPI_STORE>()) || (r = set_smem_limits<PRO_QUANT, EPI_STORE>()) ||
+        (r = set_smem_limits<PRO_RMSNORM, EPI_STORE>()) || (r = set_smem_limits<PRO_QUANT_ABSMAX, EPI_RESIDUAL>()) ||
+        (r = set_smem_limits<PRO_RMSNORM, EPI_SWIGLU>()) || (r = set_smem_limits<PRO_RMSNORM, EPI_ARGMAX>()))
+        return r;
+    sm_count();
+    g_prepared = true;
+    return 0;
+}
+
+template <int PRO, int EPI, int SLOTS>
+static int launch_t(const GemvArgs& a, const GemvPlan& p, cudaStream_t stream, bool pdl) {
+    auto kernel = gemv_kernel<PRO, EPI, SLOTS>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    H4B_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, a));
+    return 0;
+}
+
+template <int PRO, int EPI>
+static int launch_slots(const GemvArgs& a, const GemvPlan& p, cudaStream_t s, bool pdl) {
+    switch (p.slots) {
+        case 1: return launch_t<PRO, EPI, 1>(a, p, s, pdl);
+        case 2: return launch_t<PRO, EPI, 2>(a, p, s, pdl);
+        case 3: return launch_t<PRO, EPI, 3>(a, p, s, pdl);
+        case 4: return launch_t<PRO, EPI, 4>(a, p, s, pdl);
+        case 5: return launch_t<PRO, EPI, 5>(a, p, s, pdl);
+        case 6: return launch_t<PRO, EPI, 6>(a, p, s, pdl);
+        default: return H4B_EUNSUPPORTED;
+    }
+}
+
+// The (prologue, epilogue) pairs the decode path and the C ABI use.
+int launch_gemv(int pro, int epi, GemvArgs a, cudaStream_t stream, bool pdl) {
+    if (!g_prepared) {
+        const int prc = prepare_kernels();
+        if (prc) return prc;
+    }
+    const int align = (epi == EPI_SWIGLU) ? 2 * kSwigluBlock : 1;
+    GemvPlan p;
+    const int rc = plan_gemv(a.rows, a.width, align, &p);
+    if (rc) return rc;
+    if (reinterpret_cast<uintptr_t>(a.w) & 15) return H4B_EINVAL;
+    a.row_align = align;
+    a.kgroups = p.kgroups;
+    a.tile_rows = p.tile_rows;
+    a.stages = p.stages;
+    a.rows_cap = p.rows_cap;
+    if (pro == PRO_INT8 && epi == EPI_STORE) return launch_slots<PRO_INT8, EPI_STORE>(a, p, stream, pdl);
+    if (pro == PRO_QUANT && epi == EPI_STORE) return launch_slots<PRO_QUANT, EPI_STORE>(a, p, stream, pdl);
+    if (pro == PRO_RMSNORM && epi == EPI_STORE) return launch_slots<PRO_RMSNORM, EPI_STORE>(a, p, stream, pdl);
+    if (pro == PRO_QUANT_ABSMAX && epi == EPI_RESIDUAL)
+        return launch_slots<PRO_QUANT_ABSMAX, EPI_RESIDUAL>(a, p, stream, pdl);
+    if (pro == PRO_RMSNORM && epi == EPI_SWIGLU) return launch_slots<PRO_RMSNORM, EPI_SWIGLU>(a, p, stream, pdl);
+    if (pro == PRO_RMSNORM && epi == EPI_ARGMAX) return launch_slots<PRO_RMSNORM, EPI_ARGMAX>(a, p, stream, pdl);
+    return H4B_EUNSUPPORTED;
+}
+
+}  // namespace h4b
+
+// ---------------------------------------------------------------------------
+// C ABI (declared in include/harsh4b_b200.h)
+
+extern "C" int h4b_int4_i8_gemv(const int8_t* x, const uint8_t* weights, const float* scales,
+                                float activation_scale, float* output, int32_t* acc, int rows, int width,
+                                void* stream) {
+    if (!x || !weights || !scales || !output) return H4B_EINVAL;
+    if (reinterpret_cast<uintptr_t>(x) & 7) return H4B_EINVAL;
+    h4b::GemvArgs a = {};
+    a.w = weights; a.wscale = scales; a.rows = rows; a.width = width;
+    a.x8 = x; a.act_scale = activation_scale; a.out = output; a.acc_out = acc;
+    return h4b::launch_gemv(h4b::PRO_INT8, h4b::EPI_STORE, a, static_cast<cudaStream_t>(stream), false);
+}
+
+extern "C" int h4b_int4_gemv_fused_quant(const float* values, const uint8_t* weights, const float* scales,
+                                         float* output, int32_t* acc, float* act_scale_out, int rows,
+                                         int width, void* stream) {
+    if (!values || !weights || !scales || !output) return H4B_EINVAL;
+    if (reinterpret_cast<uintptr_t>(values) & 15) return H4B_EINVAL;
+    h4b::GemvArgs a = {};
+    a.w = weights; a.wscale = scales; a.rows = rows; a.width = width;
+    a.xin = values; a.out = output; a.acc_out = acc; a.act_scale_out = act_scale_out;
+    return h4b::launch_gemv(h4b::PRO_QUANT, h4b::EPI_STORE, a, static_cast<cudaStream_t>(stream), false);
+}

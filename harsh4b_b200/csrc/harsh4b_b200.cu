@@ -1,0 +1,5 @@
+// Single translation unit for libharsh4b_b200.so: the kernels share device
+// globals (the status word) without relocatable device code.
+#include "gemv.cu"
+#include "attention.cu"
+#include "decode.cu"

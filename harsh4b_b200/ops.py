@@ -1,0 +1,106 @@
+"""Operator-level wrappers over the C ABI, on torch CUDA tensors.
+
+Each function mirrors one call the reference's CPU path makes (the C ABI
+declarations in include/harsh4b_b200.h cite the reference lines). Inputs
+must already be CUDA tensors; nothing here copies to or from the host.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._lib import check, lib, stream_handle
+
+
+def _dev(tensor: torch.Tensor, dtype: torch.dtype, name: str) -> int:
+    if not isinstance(tensor, torch.Tensor) or not tensor.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if tensor.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {tensor.dtype}")
+    if not tensor.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return tensor.data_ptr()
+
+
+def int4_i8_gemv(x8: torch.Tensor, weights: torch.Tensor, scales: torch.Tensor, activation_scale: float,
+                 *, out: torch.Tensor | None = None, acc: torch.Tensor | None = None):
+    """litespark_int4_i8_gemv on the GPU: returns (fp32 out[rows], int32 acc[rows] or None)."""
+    rows, packed = weights.shape
+    out = torch.empty(rows, dtype=torch.float32, device=weights.device) if out is None else out
+    check(lib().h4b_int4_i8_gemv(_dev(x8, torch.int8, "x8"), _dev(weights, torch.uint8, "weights"),
+                                 _dev(scales, torch.float32, "scales"), float(activation_scale),
+                                 _dev(out, torch.float32, "out"),
+                                 _dev(acc, torch.int32, "acc") if acc is not None else None,
+                                 rows, 2 * packed, stream_handle()), "h4b_int4_i8_gemv")
+    return out, acc
+
+
+def int4_gemv_fused_quant(values: torch.Tensor, weights: torch.Tensor, scales: torch.Tensor,
+                          *, out: torch.Tensor | None = None, acc: torch.Tensor | None = None):
+    """quantize_activation + int4 GEMV in one kernel: returns (out, acc, act_scale tensor[1])."""
+    rows, packed = weights.shape
+    out = torch.empty(rows, dtype=torch.float32, device=weights.device) if out is None else out
+    scale = torch.empty(1, dtype=torch.float32, device=weights.device)
+    check(lib().h4b_int4_gemv_fused_quant(_dev(values, torch.float32, "values"),
+                                          _dev(weights, torch.uint8, "weights"),
+                                          _dev(scales, torch.float32, "scales"), _dev(out, torch.float32, "out"),
+                                          _dev(acc, torch.int32, "acc") if acc is not None else None,
+                                          scale.data_ptr(), rows, 2 * packed, stream_handle()),
+          "h4b_int4_gemv_fused_quant")
+    return out, acc, scale
+
+
+def quantize_activation(values: torch.Tensor, quantized: torch.Tensor | None = None):
+    """Returns (int8 tensor, dequant scale tensor[1])."""
+    quantized = torch.empty(values.numel(), dtype=torch.int8, device=values.device) if quantized is None else quantized
+    if quantized.numel() < values.numel():
+        raise ValueError("int8 output buffer is smaller than the activation")
+    scale = torch.empty(1, dtype=torch.float32, device=values.device)
+    check(lib().h4b_quantize_activation(_dev(values, torch.float32, "values"),
+                                        _dev(quantized, torch.int8, "quantized"), scale.data_ptr(),
+                                        values.numel(), stream_handle()), "h4b_quantize_activation")
+    return quantized, scale
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    out = torch.empty_like(x) if out is None else out
+    check(lib().h4b_rmsnorm(_dev(x, torch.float32, "x"), _dev(weight, torch.float32, "weight"),
+                            _dev(out, torch.float32, "out"), x.numel(), float(eps), stream_handle()), "h4b_rmsnorm")
+    return out
+
+
+def add_inplace(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    check(lib().h4b_add_inplace(_dev(x, torch.float32, "x"), _dev(y, torch.float32, "y"), x.numel(),
+                                stream_handle()), "h4b_add_inplace")
+    return x
+
+
+def gqa_decode(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, context: int,
+               kv_heads: int, groups: int, *, scores: torch.Tensor | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """litespark_gqa_decode on the GPU; keys/values fp32 [capacity, kv_heads, head_dim]."""
+    capacity, _, head_dim = keys.shape
+    q_heads = kv_heads * groups
+    scores = torch.empty(q_heads * capacity, dtype=torch.float32, device=query.device) if scores is None else scores
+    out = torch.empty(q_heads, head_dim, dtype=torch.float32, device=query.device) if out is None else out
+    check(lib().h4b_gqa_decode(_dev(query, torch.float32, "query"), _dev(keys, torch.float32, "keys"),
+                               _dev(values, torch.float32, "values"), _dev(scores, torch.float32, "scores"),
+                               _dev(out, torch.float32, "out"), context, kv_heads, groups, head_dim, capacity,
+                               stream_handle()), "h4b_gqa_decode")
+    return out
+
+
+def embedding(token: torch.Tensor, table: torch.Tensor, scales: torch.Tensor,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    vocab, packed = table.shape
+    out = torch.empty(2 * packed, dtype=torch.float32, device=table.device) if out is None else out
+    check(lib().h4b_embedding(_dev(token, torch.int32, "token"), _dev(table, torch.uint8, "table"),
+                              _dev(scales, torch.float32, "scales"), _dev(out, torch.float32, "out"), vocab,
+                              2 * packed, stream_handle()), "h4b_embedding")
+    return out
+
+
+def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    out = torch.empty(1, dtype=torch.int32, device=logits.device) if out is None else out
+    check(lib().h4b_argmax(_dev(logits, torch.float32, "logits"), logits.numel(), _dev(out, torch.int32, "out"),
+                           stream_handle()), "h4b_argmax")
+    return out

@@ -1,0 +1,163 @@
+/*
+ * harsh4b_b200 -- C ABI of the B200 (sm_100a) decode backend for the
+ * Qwen3-4B packed int4 model.
+ *
+ * Conventions (following the reference's native ABI,
+ * cpu_kernels/litespark_int4.cpp:78-81): extern "C", raw pointers and int
+ * sizes, the caller owns every buffer, outputs land in caller memory, and
+ * nothing allocates on the hot path. Unlike the reference (which returns
+ * void), every entry point returns an int status: 0 on success, a positive
+ * cudaError_t value for a CUDA failure, or a negative H4B_E* code for a
+ * rejected argument. All data pointers are DEVICE pointers unless named
+ * host_*; `stream` is a cudaStream_t (NULL = legacy default stream).
+ *
+ * Weight layout (the reference's packed cache, cpu_lightspark.py:139-146,
+ * :571-676): uint8[rows, width/2], row-major, two signed int4 codes per
+ * byte, low nibble = even column, codes in [-7, +7]; float32 row scales.
+ */
+#ifndef HARSH4B_B200_H
+#define HARSH4B_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define H4B_EINVAL (-1)       /* bad size, alignment or pointer */
+#define H4B_EUNSUPPORTED (-2) /* shape outside what the kernels implement */
+
+/* Device-side status word (bit 1: a bounded wait gave up; bit 2: token id
+ * out of range; bit 4: position beyond capacity). Reads and clears it; the
+ * read synchronises with the device. */
+int h4b_get_status(int *host_status);
+
+/* One-time set-up of the current device (kernel shared-memory limits).
+ * Call it before capturing any graph; other entry points call it lazily. */
+int h4b_prepare(void);
+
+/* Number of SMs and the device's compute capability (for tests). */
+int h4b_device_info(int *host_sm_count, int *host_cc_major, int *host_cc_minor);
+
+/* ---- operator level ------------------------------------------------------ */
+
+/* Replaces litespark_int4_i8_gemv (cpu_kernels/litespark_int4.cpp:78-84):
+ *   output[r] = float(sum_k w[r,k] * x[k]) * activation_scale * scales[r]
+ * evaluated left to right as the reference does (litespark_int4.cpp:73-74).
+ * x: int8[width]; width a positive multiple of 32, weights 16-byte aligned.
+ * acc (may be NULL) receives the int32 accumulators. */
+int h4b_int4_i8_gemv(const int8_t *x, const uint8_t *weights, const float *scales,
+                     float activation_scale, float *output, int32_t *acc,
+                     int rows, int width, void *stream);
+
+/* Replaces the pair kernel.quantize_activation + litespark_int4_i8_gemv that
+ * cpu_lightspark.LiteSparkQwen._projection runs (cpu_lightspark.py:433-434,
+ * :351-371), fused: the fp32 input is absmax-quantised to int8 inside the
+ * kernel. act_scale_out (may be NULL) receives the dequant scale. */
+int h4b_int4_gemv_fused_quant(const float *values, const uint8_t *weights, const float *scales,
+                              float *output, int32_t *acc, float *act_scale_out,
+                              int rows, int width, void *stream);
+
+/* Replaces kernel.quantize_activation (third-party, called at
+ * cpu_lightspark.py:433): q = clamp(rint(v * 127/m), -127, 127) with
+ * m = max(absmax(v), 1e-5); *scale_out = m / 127. */
+int h4b_quantize_activation(const float *values, int8_t *quantized, float *scale_out, int n,
+                            void *stream);
+
+/* Replaces kernel.rmsnorm_into (third-party, cpu_lightspark.py:431):
+ * out = (x * (1 / sqrt(mean(x^2) + eps))) * weight. */
+int h4b_rmsnorm(const float *x, const float *weight, float *out, int n, float eps, void *stream);
+
+/* Replaces kernel.add_inplace (third-party, cpu_lightspark.py:445): x += y. */
+int h4b_add_inplace(float *x, const float *y, int n, void *stream);
+
+/* Replaces litespark_gqa_decode (cpu_kernels/litespark_int4.cpp:160-171):
+ * single-token grouped-query attention, fp32, keys/values laid out
+ * [time, kv_heads, head_dim], query/output heads [kv_head, group, head_dim].
+ * scores: caller scratch of q_heads * score_stride floats (as in the
+ * reference); the kernel keeps its split partials there. head_dim = 128. */
+int h4b_gqa_decode(const float *query, const float *keys, const float *values, float *scores,
+                   float *output, int context, int kv_heads, int groups, int head_dim,
+                   int score_stride, void *stream);
+
+/* Replaces LiteSparkQwen._embedding_into (cpu_lightspark.py:341-349):
+ * out[k] = int4(embedding[token, k]) * scales[token]. The token id is read
+ * from device memory; an out-of-range id sets status bit 2 and writes 0. */
+int h4b_embedding(const int32_t *token, const uint8_t *embedding, const float *scales,
+                  float *out, int vocab, int hidden, void *stream);
+
+/* Greedy selection (cpu_lightspark.py:704-705): first index of the maximum
+ * of logits[n], written to *token_out (device int32). */
+int h4b_argmax(const float *logits, int n, int32_t *token_out, void *stream);
+
+/* ---- model level ----------------------------------------------------------- */
+
+/* Device-resident Qwen3 model. Every weight kind is one buffer covering all
+ * layers: w_qkv [L][q+2kv][H/2] (q, k, v rows concatenated as
+ * cpu_lightspark.py:638-661 combines them); w_o [L][H][q/2]; w_gate_up
+ * [L][2I][H/2] with gate and up rows interleaved in blocks of 4 (rows
+ * 8b..8b+3 = gate 4b..4b+3, rows 8b+4..8b+7 = up 4b..4b+3); w_down
+ * [L][H][I/2]; scales alongside. Norm vectors: norm_in/norm_post [L][H],
+ * norm_q/norm_k [L][head_dim]. rope_cos/rope_sin: [max_pos][head_dim/2] fp32
+ * tables (cpu_lightspark.py:329-336). */
+typedef struct h4b_model {
+    int layers, hidden, intermediate, heads, kv_heads, head_dim, vocab, max_pos;
+    float eps;
+    const uint8_t *w_qkv;     const float *s_qkv;
+    const uint8_t *w_o;       const float *s_o;
+    const uint8_t *w_gate_up; const float *s_gate_up;
+    const uint8_t *w_down;    const float *s_down;
+    const uint8_t *w_embed;   const float *s_embed;
+    const float *norm_in, *norm_post, *norm_q, *norm_k, *norm_final;
+    const float *rope_cos, *rope_sin;
+} h4b_model;
+
+/* One decode session (QwenDecodeState, cpu_lightspark.py:275-309), all
+ * buffers caller-allocated on the device. k_cache/v_cache:
+ * [L][kv_heads][capacity][head_dim] in kv_dtype (0 = fp32, 1 = fp16).
+ * position/token/next_token: device int32 scalars; the step reads token and
+ * position, writes next_token (greedy) and advances position by one.
+ * Scratch: x[H], qkv[q+2kv], attended[q], act[I], logits[V]; absmax[2L]
+ * floats and argmax_key[1] are rewritten every step; attn_partials holds
+ * kv_heads * attn_splits * groups * (head_dim + 4) floats; attn_counters
+ * holds kv_heads ints and must be zero when the session is created. */
+typedef struct h4b_state {
+    int capacity, kv_dtype, attn_splits;
+    void *k_cache, *v_cache;
+    int32_t *position, *token, *next_token;
+    float *x, *qkv, *attended, *act, *logits;
+    float *absmax;
+    unsigned long long *argmax_key;
+    float *attn_partials;
+    int *attn_counters;
+} h4b_state;
+
+/* Checks the shapes/pointers of a model + state pair against what the
+ * kernels implement. */
+int h4b_validate(const h4b_model *model, const h4b_state *state);
+
+/* One full decode token (LiteSparkQwen.forward_token,
+ * cpu_lightspark.py:424-468) as a chain of kernel launches on `stream`:
+ * embedding, 36 x (qkv GEMV, attention, o GEMV, gate/up GEMV, down GEMV),
+ * LM head + argmax, position += 1. Capturable in a CUDA graph. */
+int h4b_decode_step(const h4b_model *model, const h4b_state *state, void *stream);
+
+/* Launches one stage of h4b_decode_step without programmatic launch, for
+ * per-category timing (LiteSparkQwen.profile_forward_token,
+ * cpu_lightspark.py:470-553). stage: 0 embedding, 1 qkv GEMV, 2 attention,
+ * 3 o GEMV, 4 gate/up GEMV, 5 down GEMV (1-5 take `layer`), 6 LM head +
+ * argmax, 7 finalize (next_token, position += 1). */
+int h4b_decode_stage(const h4b_model *model, const h4b_state *state, int stage, int layer, void *stream);
+
+/* Captures h4b_decode_step into a CUDA graph bound to (model, state) and
+ * instantiates it; *graph_out is an opaque handle. */
+int h4b_graph_create(const h4b_model *model, const h4b_state *state, void *stream, void **graph_out);
+int h4b_graph_launch(void *graph, void *stream);
+int h4b_graph_destroy(void *graph);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HARSH4B_B200_H */

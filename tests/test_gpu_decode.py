@@ -1,0 +1,128 @@
+"""Model-level parity of the device decode against the CPU oracle.
+
+Contract (north star): final logits within 1e-2 max-abs and the same greedy
+token at every step of a 64-token decode, versus the reference CPU path
+(fp32 KV cache). The device keeps an fp16 KV cache by default; with an fp32
+cache it tracks the oracle to ~1e-5.
+"""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from _models import cuda_decode, oracle_decode, oracle_model, top2_margin  # noqa: E402
+from harsh4b_b200.model import CudaQwen  # noqa: E402
+from harsh4b_b200.synthetic import qwen3_4b_config, synthetic_checkpoint, synthetic_prompt, tiny_config  # noqa: E402
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "tiny_decode.npz"
+LOGIT_TOL = 1e-2  # max-abs, from the north star
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    checkpoint = synthetic_checkpoint(tiny_config(), seed=11)
+    return checkpoint, synthetic_prompt(checkpoint.config, 16, seed=11)
+
+
+def test_tiny_fp32_kv_tracks_oracle(tiny):
+    checkpoint, prompt = tiny
+    want, greedy = oracle_decode(oracle_model(checkpoint), prompt, 24)
+    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float32")
+    got, got_greedy = cuda_decode(model, prompt, 24)
+    assert got_greedy == greedy
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=2e-5)
+    assert model.status() == 0
+
+
+@pytest.mark.parametrize("splits", [1, 3, 16])
+def test_tiny_fp16_kv_matches_fp16_oracle(tiny, splits):
+    checkpoint, prompt = tiny
+    want16, greedy16 = oracle_decode(oracle_model(checkpoint, kv_dtype=np.float16), prompt, 24)
+    want32, greedy32 = oracle_decode(oracle_model(checkpoint), prompt, 24)
+    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float16")
+    got, got_greedy = cuda_decode(model, prompt, 24, attn_splits=splits)
+    assert got_greedy == greedy16
+    np.testing.assert_allclose(got, want16, rtol=1e-3, atol=1e-4)
+    assert np.abs(got - want32).max() <= LOGIT_TOL
+
+
+def test_device_side_greedy_loop_matches_host_loop(tiny):
+    checkpoint, prompt = tiny
+    model = CudaQwen.from_checkpoint(checkpoint)
+    _, greedy = cuda_decode(model, prompt, 12)
+    state = model.new_state(len(prompt) + 12)
+    for token in prompt[:-1]:
+        model.forward_token(token, state)
+    tokens = []
+    model.forward_token(prompt[-1], state)
+    tokens.append(state.next_token_host())
+    model.generate_greedy(tokens[-1], state, 11)
+    tokens.append(state.next_token_host())
+    # generate_greedy ran 11 steps; its last greedy token must equal the host loop's 12th.
+    assert tokens[0] == greedy[0] and tokens[-1] == greedy[11]
+    assert state.position == len(prompt) + 11
+
+
+def test_reference_golden_decode_on_device():
+    """Logits recorded from the reference's own LiteSparkQwen.forward_token."""
+    golden = np.load(GOLDEN)
+    config = json.loads(str(golden["config"]))
+    checkpoint = synthetic_checkpoint(config, seed=int(golden["seed"]))
+    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float32")
+    prompt, tokens = list(golden["prompt"]), list(golden["tokens"])
+    got, greedy = cuda_decode(model, prompt, len(tokens), teacher=tokens)
+    assert greedy == tokens
+    np.testing.assert_allclose(got, golden["logits"], rtol=1e-4, atol=2e-5)
+
+
+def test_profile_categories_and_counts(tiny):
+    checkpoint, prompt = tiny
+    model = CudaQwen.from_checkpoint(checkpoint)
+    state = model.new_state(8)
+    model.forward_token(prompt[0], state)
+    logits, timings, counts, total = model.profile_forward_token(prompt[1], state)
+    layers = checkpoint.config["num_hidden_layers"]
+    assert counts["ternary/int4 GEMV"] == 4 * layers
+    assert counts["attention"] == layers
+    assert counts["embedding / LM head"] == 2
+    assert total > 0 and all(v >= 0 for v in timings.values())
+    after = model.forward_token(prompt[2], state).cpu().numpy()
+    assert np.isfinite(after).all() and state.position == 3
+
+
+def test_host_side_errors(tiny):
+    checkpoint, _ = tiny
+    model = CudaQwen.from_checkpoint(checkpoint)
+    state = model.new_state(2)
+    with pytest.raises(ValueError, match="outside the vocabulary"):
+        model.forward_token(checkpoint.config["vocab_size"], state)
+    model.forward_token(1, state)
+    model.forward_token(2, state)
+    with pytest.raises(ValueError, match="capacity exhausted"):
+        model.forward_token(3, state)
+    assert model.status() == 0
+
+
+@pytest.fixture(scope="module")
+def full():
+    config = qwen3_4b_config()
+    return synthetic_checkpoint(config, seed=0), synthetic_prompt(config, 128, seed=0)
+
+
+def test_config0_64_greedy_tokens_match_reference_path(full):
+    """128 random prompt ids, 64 greedy tokens, batch 1."""
+    checkpoint, prompt = full
+    want, greedy = oracle_decode(oracle_model(checkpoint), prompt, 64)
+    model = CudaQwen.from_checkpoint(checkpoint)  # fp16 KV, the production setting
+    got, got_greedy = cuda_decode(model, prompt, 64, teacher=greedy)
+    diff = np.abs(got - want).max(axis=1)
+    margins = top2_margin(want[len(prompt) - 1:])
+    report = {"max_abs_logit_diff": float(diff.max()), "min_top2_margin": float(margins.min())}
+    print(json.dumps(report))
+    assert diff.max() <= LOGIT_TOL, report
+    assert got_greedy == greedy, report
+    assert model.status() == 0
