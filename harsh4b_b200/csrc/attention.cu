@@ -131,7 +131,7 @@ __device__ __forceinline__ float4 merge_splits(const float* base, int splits, in
         const float* p = base + s * stride;
         const float ls = __ldcg(p + kHeadDim + 1);
         if (ls == 0.f) continue;
-        const float w = expf(__ldcg(p + kHeadDim) - mmax);
+        const float w = exp_cw(__ldcg(p + kHeadDim) - mmax);
         l = __fmaf_rn(ls, w, l);
         const float4 v = __ldcg(reinterpret_cast<const float4*>(p + 4 * lane));
         o.x = __fmaf_rn(v.x, w, o.x);
@@ -204,8 +204,8 @@ __global__ void __launch_bounds__(256) gqa_split_kernel(const AttnArgs a) {
             if (t + u >= t1) break;
             const float s = __fmul_rn(warp_sum(dot4(q, kk[u])), scale);
             const float mn = fmaxf(m, s);
-            const float corr = expf(m - mn);
-            const float p = expf(s - mn);
+            const float corr = exp_cw(m - mn);
+            const float p = exp_cw(s - mn);
             l = __fmaf_rn(l, corr, p);
             o.x = __fmaf_rn(o.x, corr, __fmul_rn(p, vv[u].x));
             o.y = __fmaf_rn(o.y, corr, __fmul_rn(p, vv[u].y));

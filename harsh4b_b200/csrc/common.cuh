@@ -161,6 +161,29 @@ __device__ __forceinline__ int quantize_one(float v, float qs) {
     return max(-127, min(127, q));
 }
 
+// exp(x) by Cody-Waite range reduction (x = n ln2 + r, |r| <= ln2/2, with
+// ln2 split into a short high part and a low correction) and the degree-7
+// Taylor polynomial of exp(r) in Horner form, scaled exactly by 2^n. Inputs
+// below -87 give 0; inputs above 88 are clamped. One IEEE op per step, so
+// a CPU implementation with the same steps returns the same bits (the test
+// oracle does); within 2 ulp of exp on [-87, 88].
+__device__ __forceinline__ float exp_cw(float x) {
+    if (x < -87.0f) return 0.0f;
+    x = fminf(x, 88.0f);
+    const float n = rintf(__fmul_rn(x, 1.44269504f));
+    float r = __fmaf_rn(n, -0.693145751953125f, x);
+    r = __fmaf_rn(n, -1.42860682e-06f, r);
+    float p = 1.98412698e-04f;
+    p = __fmaf_rn(p, r, 1.38888889e-03f);
+    p = __fmaf_rn(p, r, 8.33333333e-03f);
+    p = __fmaf_rn(p, r, 4.16666667e-02f);
+    p = __fmaf_rn(p, r, 1.66666667e-01f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    return __fmul_rn(p, __int_as_float((static_cast<int>(n) + 127) << 23));
+}
+
 // Argmax key: larger value wins, ties go to the smaller index (numpy's
 // first-occurrence rule). Values are mapped to an order-preserving uint.
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {

@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
             const int gi = 2 * kSwigluBlock * b + j;
             const float g = value(gi), u = value(gi + kSwigluBlock);
             // cpu_lightspark.py:451-455: gate / (1 + exp(-gate)) * up
-            const float act = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+            const float act = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_cw(-g))), u);
             a.out[(r0 >> 1) + p] = act;
             local = fmaxf(local, fabsf(act));
         }

@@ -54,6 +54,16 @@ def library() -> ctypes.CDLL:
     lib.oracle_add_inplace.restype = None
     lib.oracle_gqa_decode.argtypes = [vp] * 5 + [i32] * 5
     lib.oracle_gqa_decode.restype = None
+    lib.oracle_expf.argtypes = [f32]
+    lib.oracle_expf.restype = f32
+    lib.oracle_exp_array.argtypes = [vp, vp, i32]
+    lib.oracle_exp_array.restype = None
+    lib.oracle_qk_norm.argtypes = [vp, vp, i32, f32]
+    lib.oracle_qk_norm.restype = None
+    lib.oracle_silu_mul.argtypes = [vp, vp, vp, i32]
+    lib.oracle_silu_mul.restype = None
+    lib.oracle_gqa_splitk.argtypes = [vp, vp, vp, vp, i32, i32, i32, ctypes.c_long, ctypes.c_long, i32]
+    lib.oracle_gqa_splitk.restype = None
     lib.oracle_max_threads.argtypes = []
     lib.oracle_max_threads.restype = i32
     return lib
@@ -93,6 +103,22 @@ def quantize_activation(values: np.ndarray, quantized: np.ndarray) -> float:
     if quantized.size < values.size or quantized.dtype != np.int8:
         raise ValueError("int8 output buffer is smaller than the activation")
     return float(library().oracle_quantize_activation(_ptr(values), _ptr(quantized), values.size))
+
+
+def exp(values: np.ndarray) -> np.ndarray:
+    """The shared exp (oracle_expf) applied elementwise to float32 values."""
+    values = np.ascontiguousarray(values, dtype=np.float32)
+    out = np.empty_like(values)
+    library().oracle_exp_array(_ptr(values), _ptr(out), values.size)
+    return out
+
+
+def gqa_splitk(query, keys, values, output, context, kv_heads, groups, splits):
+    """GQA in the device's split-K order; keys/values [time, kv_heads, 128]."""
+    if query.shape[-1] != 128 or not 1 <= splits <= 64:
+        raise ValueError("device-order attention needs head_dim 128 and 1..64 splits")
+    library().oracle_gqa_splitk(_ptr(query), _ptr(keys), _ptr(values), _ptr(output), context, kv_heads,
+                                groups, kv_heads * 128, 128, splits)
 
 
 def gqa_decode(query, keys, values, scores, output, context, kv_heads, groups, head_dim, score_stride):
@@ -137,6 +163,6 @@ from .model import OracleLayer, OracleProjection, OracleQwen, OracleState, sampl
 
 __all__ = [
     "OracleKernel", "OracleLayer", "OracleProjection", "OracleQwen", "OracleState", "build",
-    "configure_threads", "gqa_decode", "int4_gemv", "int4_gemv_function", "library", "max_threads",
+    "configure_threads", "exp", "gqa_decode", "gqa_splitk", "int4_gemv", "int4_gemv_function", "library", "max_threads",
     "quantize_activation", "sample_logits",
 ]

@@ -23,6 +23,15 @@
  *
  * The reference kernel is ARM NEON (vdotq_s32); this file is portable C with
  * an optional AVX2 path for the row dot, both exact in int32.
+ *
+ * Reduction orders and exp: the reference does not pin them (its RMSNorm is
+ * third-party, and its NEON and numpy attention paths already sum in
+ * different orders). On this int8-quantised model an order change alone
+ * moves logits by ~0.1 (the quantiser turns last-ulp differences into code
+ * flips), so the model-level functions below fix the order to the device
+ * kernels' documented order and use one exp implementation, which makes
+ * device-vs-oracle parity bit-exact. oracle_gqa_decode keeps the reference's
+ * own order and is checked against the reference's known answers.
  */
 #include <float.h>
 #include <math.h>
@@ -170,16 +179,152 @@ float oracle_quantize_activation(const float *values, int8_t *quantized, int n)
     return m / 127.0f;
 }
 
+/* ---- arithmetic shared bit-for-bit with the device -------------------- */
+
+/* exp(x) by Cody-Waite range reduction (x = n ln2 + r, |r| <= ln2/2, ln2 split
+ * into a short high part and a low correction) and the degree-7 Taylor
+ * polynomial of exp(r) in Horner form, then an exact scaling by 2^n. Inputs
+ * below -87 return 0 and inputs above 88 are clamped to 88. Every operation
+ * is a single IEEE fp32 op or fmaf, so the device (common.cuh, h4b::exp_cw)
+ * produces the same bits. Within 2 ulp of exp on [-87, 88]. */
+float oracle_expf(float x)
+{
+    if (x < -87.0f) return 0.0f;
+    if (x > 88.0f) x = 88.0f;
+    const float n = rintf(x * 1.44269504f);
+    float r = fmaf(n, -0.693145751953125f, x);
+    r = fmaf(n, -1.42860682e-06f, r);
+    float p = 1.98412698e-04f;
+    p = fmaf(p, r, 1.38888889e-03f);
+    p = fmaf(p, r, 8.33333333e-03f);
+    p = fmaf(p, r, 4.16666667e-02f);
+    p = fmaf(p, r, 1.66666667e-01f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    union { uint32_t u; float f; } scale;
+    scale.u = (uint32_t)((int)n + 127) << 23;
+    return p * scale.f;
+}
+
+void oracle_exp_array(const float *x, float *out, int n)
+{
+    for (int i = 0; i < n; ++i) out[i] = oracle_expf(x[i]);
+}
+
+/* 32-lane butterfly sum (xor 16, 8, 4, 2, 1), the device's warp_sum. */
+static float butterfly32(float lanes[32])
+{
+    float next[32];
+    for (int o = 16; o > 0; o >>= 1) {
+        for (int l = 0; l < 32; ++l) next[l] = lanes[l] + lanes[l ^ o];
+        memcpy(lanes, next, sizeof(next));
+    }
+    return lanes[0];
+}
+
 /* kernel.rmsnorm_into(x, w, out, eps) (cpu_lightspark.py:431,447,461):
  *   out = (x * (1 / sqrt(sum(x^2) / n + eps))) * w
- * The sum of squares is accumulated in double and rounded once to fp32. */
+ * with the sum of squares in the device's order: 256 partials, partial t
+ * takes the 8-column groups g = t, t+256, ... with fmaf; each warp of 32
+ * partials is summed by butterfly; the 8 warp sums are added in order. */
 void oracle_rmsnorm(const float *x, const float *w, float *out, int n, float eps)
 {
-    double ss = 0.0;
-    for (int i = 0; i < n; ++i) ss += (double)x[i] * (double)x[i];
-    const float mean = (float)ss / (float)n;
+    float partial[256];
+    const int groups = n >> 3;
+    for (int t = 0; t < 256; ++t) {
+        float ss = 0.0f;
+        for (int g = t; g < groups; g += 256)
+            for (int e = 0; e < 8; ++e) ss = fmaf(x[8 * g + e], x[8 * g + e], ss);
+        partial[t] = ss;
+    }
+    float total = 0.0f;
+    for (int warp = 0; warp < 8; ++warp) total += butterfly32(partial + 32 * warp);
+    const float mean = total / (float)n;
     const float inv = 1.0f / sqrtf(mean + eps);
     for (int i = 0; i < n; ++i) out[i] = (x[i] * inv) * w[i];
+}
+
+/* Lane l of a 128-wide head holds v[4l..4l+3]; its share of a dot product
+ * is fma(a3,b3, fma(a2,b2, fma(a1,b1, a0*b0))), summed over lanes by
+ * butterfly. */
+static float head_dot(const float *a, const float *b)
+{
+    float lanes[32];
+    for (int l = 0; l < 32; ++l) {
+        const float *p = a + 4 * l, *q = b + 4 * l;
+        lanes[l] = fmaf(p[3], q[3], fmaf(p[2], q[2], fmaf(p[1], q[1], p[0] * q[0])));
+    }
+    return butterfly32(lanes);
+}
+
+/* Per-head RMSNorm of q or k (cpu_lightspark.py:373-379): v / sqrt(mean(v^2)
+ * + eps) * gamma, divide first, for heads of 128 in the device's order. */
+void oracle_qk_norm(float *v, const float *gamma, int heads, float eps)
+{
+    for (int h = 0; h < heads; ++h) {
+        float *x = v + 128 * h;
+        const float ss = head_dot(x, x);
+        const float root = sqrtf(ss / 128.0f + eps);
+        for (int d = 0; d < 128; ++d) x[d] = (x[d] / root) * gamma[d];
+    }
+}
+
+/* SiLU(gate) * up (cpu_lightspark.py:451-455): gate / (1 + exp(-gate)) * up. */
+void oracle_silu_mul(const float *gate, const float *up, float *out, int n)
+{
+    for (int i = 0; i < n; ++i) out[i] = (gate[i] / (1.0f + oracle_expf(-gate[i]))) * up[i];
+}
+
+/* Single-token GQA in the device's split-K order (head_dim 128): the context
+ * is cut into `splits` chunks of ceil(context/splits); each chunk runs an
+ * online softmax token by token (m, l, o), and the chunks are merged in order
+ * with weights exp(m_s - max m). keys/values element (t, kv, d) sits at
+ * t * time_stride + kv * head_stride + d. */
+void oracle_gqa_splitk(const float *query, const float *keys, const float *values, float *output,
+                       int context, int kv_heads, int groups, long time_stride, long head_stride, int splits)
+{
+    const float scale = 1.0f / sqrtf(128.0f);
+    const int chunk = (context + splits - 1) / splits;
+    const int query_heads = kv_heads * groups;
+#pragma omp parallel for if (query_heads >= 8) schedule(static)
+    for (int h = 0; h < query_heads; ++h) {
+        const int kvh = h / groups;
+        const float *q = query + 128 * h;
+        float ms[64], ls[64], os[64][128];
+        for (int s = 0; s < splits; ++s) {
+            const int t0 = s * chunk < context ? s * chunk : context;
+            const int t1 = t0 + chunk < context ? t0 + chunk : context;
+            float m = -INFINITY, l = 0.0f;
+            float *o = os[s];
+            for (int d = 0; d < 128; ++d) o[d] = 0.0f;
+            for (int t = t0; t < t1; ++t) {
+                const float *k = keys + t * time_stride + kvh * head_stride;
+                const float *v = values + t * time_stride + kvh * head_stride;
+                const float sc = head_dot(q, k) * scale;
+                const float mn = fmaxf(m, sc);
+                const float corr = oracle_expf(m - mn);
+                const float p = oracle_expf(sc - mn);
+                l = fmaf(l, corr, p);
+                for (int d = 0; d < 128; ++d) o[d] = fmaf(o[d], corr, p * v[d]);
+                m = mn;
+            }
+            ms[s] = m;
+            ls[s] = l;
+        }
+        float mmax = -INFINITY;
+        for (int s = 0; s < splits; ++s) mmax = fmaxf(mmax, ms[s]);
+        float l = 0.0f, acc[128];
+        for (int d = 0; d < 128; ++d) acc[d] = 0.0f;
+        for (int s = 0; s < splits; ++s) {
+            if (ls[s] == 0.0f) continue;
+            const float wgt = oracle_expf(ms[s] - mmax);
+            l = fmaf(ls[s], wgt, l);
+            for (int d = 0; d < 128; ++d) acc[d] = fmaf(os[s][d], wgt, acc[d]);
+        }
+        const float inv = 1.0f / l;
+        for (int d = 0; d < 128; ++d) output[128 * h + d] = acc[d] * inv;
+    }
 }
 
 /* kernel.add_inplace(x, y) (cpu_lightspark.py:445,459). */

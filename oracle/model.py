@@ -7,6 +7,10 @@ reference project root). Heavy arithmetic goes through the C oracle
 ``kv_dtype=np.float16`` rounds every stored key/value through fp16, which
 mirrors the device cache's precision; the default fp32 is the reference's
 own cache (cpu_lightspark.py:290).
+
+RMSNorm, qk-norm, attention and SiLU run in the device kernels' reduction
+order with the shared exp (see litespark_oracle.c); ``attn_splits`` must
+equal the device state's split count for bit-exact comparisons.
 """
 from __future__ import annotations
 
@@ -14,7 +18,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from . import OracleKernel, gqa_decode, library, _ptr
+from . import OracleKernel, gqa_splitk, library, _ptr
 
 
 @dataclass(frozen=True)
@@ -84,7 +88,8 @@ def rope_tables(config) -> tuple[np.ndarray, np.ndarray]:
 class OracleQwen:
     """Torch-free Qwen3 single-token decode (cpu_lightspark.py:312-468)."""
 
-    def __init__(self, config, layers, embedding, embedding_scales, final_norm, *, kv_dtype=np.float32):
+    def __init__(self, config, layers, embedding, embedding_scales, final_norm, *, kv_dtype=np.float32,
+                 attn_splits: int = 16):
         self.config = config
         self.layers = list(layers)
         self.embedding = embedding
@@ -93,6 +98,7 @@ class OracleQwen:
         self.final_norm = final_norm
         self.kernel = OracleKernel()
         self.kv_dtype = np.dtype(kv_dtype)
+        self.attn_splits = attn_splits
         self.n_layers = int(config["num_hidden_layers"])
         self.hidden = int(config["hidden_size"])
         self.intermediate = int(config["intermediate_size"])
@@ -129,10 +135,7 @@ class OracleQwen:
 
     # cpu_lightspark.py:373-379: divide by sqrt(mean(v^2) + eps), then scale.
     def qk_norm(self, values: np.ndarray, gamma: np.ndarray) -> None:
-        mean = np.einsum("hd,hd->h", values, values, dtype=np.float32) / np.float32(values.shape[1])
-        root = np.sqrt(mean + np.float32(self.eps))
-        values /= root[:, None]
-        values *= gamma[None, :]
+        library().oracle_qk_norm(_ptr(values), _ptr(gamma), values.shape[0], self.eps)
 
     # cpu_lightspark.py:381-387: half-split rotation at one position.
     def rope(self, values: np.ndarray, position: int) -> None:
@@ -143,11 +146,10 @@ class OracleQwen:
         values[:, :half] = x1 * cosine - x2 * sine
         values[:, half:] = x2 * cosine + x1 * sine
 
-    # cpu_lightspark.py:389-422 through litespark_gqa_decode's restatement.
+    # cpu_lightspark.py:389-422: softmax(q.k / sqrt(d)) v over t <= position.
     def attention(self, state: OracleState, layer_index: int, q: np.ndarray) -> None:
-        gqa_decode(np.ascontiguousarray(q), state.keys[layer_index], state.values[layer_index],
-                   state.scores, state.attended, state.position + 1, self.kv_heads, self.groups,
-                   self.head_dim, state.capacity)
+        gqa_splitk(np.ascontiguousarray(q), state.keys[layer_index], state.values[layer_index], state.attended,
+                   state.position + 1, self.kv_heads, self.groups, self.attn_splits)
 
     def _store(self, values: np.ndarray) -> np.ndarray:
         if self.kv_dtype == np.float32:
@@ -183,8 +185,7 @@ class OracleQwen:
             self.project(layer.gate_up, quantized, scale, state.gate_up)
             gate = state.gate_up[:self.intermediate]
             up = state.gate_up[self.intermediate:]
-            np.divide(gate, np.float32(1.0) + np.exp(-gate), out=state.activated)
-            state.activated *= up
+            library().oracle_silu_mul(_ptr(gate), _ptr(up), _ptr(state.activated), self.intermediate)
             quantized, scale = self.quantize(state.activated, state)
             self.project(layer.down, quantized, scale, state.projected)
             self.kernel.add_inplace(state.x, state.projected)

@@ -119,6 +119,13 @@ def oracle_model(checkpoint, kv_dtype=np.float32):
                              checkpoint.norms["model.norm.weight"], kv_dtype=kv_dtype)
 
 
+# The oracle sums RMSNorm / qk-norm / attention in the device's order with the
+# shared exp; the reference sums in numpy's order. On this int8-quantised
+# model that difference alone moves logits by a few 1e-3 (see
+# test_reduction_order_sensitivity), well inside the 1e-2 contract.
+REFERENCE_ORDER_TOL = 5e-3
+
+
 def test_oracle_reproduces_reference_decode():
     golden = np.load(GOLDEN)
     config = json.loads(str(golden["config"]))
@@ -133,4 +140,31 @@ def test_oracle_reproduces_reference_decode():
         generated.append(oracle.sample_logits(logits[-1], generated, argmax=True))
         logits.append(model.forward_token(generated[-1], state).copy())
     assert generated == tokens
-    np.testing.assert_allclose(np.stack(logits), golden["logits"], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(np.stack(logits), golden["logits"], rtol=0, atol=REFERENCE_ORDER_TOL)
+
+
+def test_shared_exp_accuracy():
+    x = np.linspace(-87.0, 88.0, 1_000_001, dtype=np.float32)
+    y = oracle.exp(x).astype(np.float64)
+    exact = np.exp(x.astype(np.float64))
+    ulp = np.spacing(exact.astype(np.float32)).astype(np.float64)
+    assert (np.abs(y - exact) / ulp).max() < 2.0
+    assert oracle.exp(np.array([0.0, -np.inf, -90.0], dtype=np.float32)).tolist() == [1.0, 0.0, 0.0]
+
+
+def test_kv_precision_sensitivity():
+    """Why device parity is checked bit-exactly per KV precision rather than
+    with one tolerance: on this synthetic int8-quantised model, rounding the
+    KV cache to fp16 (the device's production setting) moves full-vocabulary
+    logits by more than the 1e-2 contract even in a 2-layer model on the CPU
+    oracle alone, because the per-token int8 quantiser turns small
+    differences into code flips."""
+    from harsh4b_b200.synthetic import qwen3_4b_config, synthetic_prompt
+
+    config = qwen3_4b_config(num_hidden_layers=2)
+    checkpoint = synthetic_checkpoint(config, seed=0)
+    prompt = synthetic_prompt(config, 16, seed=0)
+    a, b = oracle_model(checkpoint), oracle_model(checkpoint, kv_dtype=np.float16)
+    sa, sb = a.new_state(16), b.new_state(16)
+    drift = max(float(np.abs(a.forward_token(t, sa) - b.forward_token(t, sb)).max()) for t in prompt)
+    assert drift > 1e-2
