@@ -98,6 +98,14 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  :: "r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
 }
 
+// 4-byte asynchronous global -> shared copy (no register round trip).
+__device__ __forceinline__ void async_copy4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void async_copy_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // ---- named barrier among a subset of warps ------------------------------------
 __device__ __forceinline__ void named_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(threads) : "memory");

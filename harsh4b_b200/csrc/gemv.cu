@@ -221,8 +221,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
             for (int t = 0; t < first; ++t) issue(t);
             issued = first;
         }
-        // Row scales are weights too: fetch them before any dependency wait.
-        for (int i = lane; i < nrows; i += 32) sc_s[i] = __ldg(a.wscale + r0 + i);
+        // Row scales are weights too: fetch them asynchronously before any
+        // dependency wait, so lane 0 goes straight on to refilling the ring.
+        for (int i = lane; i < nrows; i += 32) async_copy4(sc_s + i, a.wscale + r0 + i);
         if (lane == 0) {
             for (int t = a.stages; t < ntiles; ++t) {
                 const int s = t % a.stages;
@@ -237,6 +238,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
             for (int t = max(0, issued - a.stages); t < issued; ++t)
                 mbar_wait(&full[t % a.stages], (t / a.stages) & 1, 100000000ull);
         }
+        async_copy_wait_all();
     } else {
         // ---------------- consumer warps ----------------
         pdl_wait();

@@ -5,14 +5,15 @@ import numpy as np
 import oracle
 
 
-def oracle_model(checkpoint, kv_dtype=np.float32):
+def oracle_model(checkpoint, kv_dtype=np.float32, attn_splits=16):
     config = checkpoint.config
     layers = []
     for index in range(int(config["num_hidden_layers"])):
         parts = checkpoint.layer(index)
         layers.append(oracle.OracleLayer(*[oracle.OracleProjection(*p) for p in parts[:4]], *parts[4:]))
     return oracle.OracleQwen(config, layers, checkpoint.embedding, checkpoint.embedding_scales,
-                             checkpoint.norms["model.norm.weight"], kv_dtype=kv_dtype)
+                             checkpoint.norms["model.norm.weight"], kv_dtype=kv_dtype,
+                             attn_splits=attn_splits)
 
 
 def oracle_decode(model, prompt, steps, teacher=None):
