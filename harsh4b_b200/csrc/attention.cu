@@ -5,11 +5,16 @@
 // softmax over t <= pos, o = sum_t p_t v_t; q head h reads kv head h / groups.
 //
 // Split-K ("flash decoding"): grid = (splits, kv_heads, batch). A CTA owns
-// one kv head and one slice of the context; each of its warps owns one q
-// head of the group, so every K/V row it streams serves `groups` heads.
-// Each warp keeps an online softmax (m, l, o) and the slices are merged
-// either by the last CTA to finish (decode path, self-resetting counters)
-// or by a second kernel (the reference-compatible entry point).
+// one kv head and one chunk of ceil(context / splits) tokens; each of its
+// warps owns one q head of the group, so every K/V row it stages serves
+// `groups` heads. The chunk is walked in sub-tiles of 64 tokens staged in
+// shared memory with one cooperative load each. Per sub-tile a warp scores
+// 32 tokens at a time (4 dims per lane, then a transpose-reduce that pairs
+// lanes exactly like a butterfly sum), takes a two-pass softmax, and
+// accumulates p * v in token order. Sub-tiles fold into the chunk's running
+// (m, l, o); chunks are merged either by the last CTA to finish (decode
+// path, self-resetting counters) or by a second kernel (the
+// reference-compatible entry point). The CPU oracle repeats this order.
 //
 // In the decode path the kernel also applies, before attending, what
 // cpu_lightspark.py:435-440 does between the qkv projection and attention:
@@ -25,6 +30,7 @@ constexpr int kHeadDim = 128;  // 4 values per lane
 // One split result per q head: o[128], m, l, 2 pad floats, so every float4
 // store stays 16-byte aligned.
 constexpr int kPartialStride = kHeadDim + 4;
+constexpr int kSubTile = 64;  // tokens staged per pass
 
 struct AttnArgs {
     const float* q;       // [batch][q_heads][d]  (qkv buffer in the decode path)
@@ -143,12 +149,32 @@ __device__ __forceinline__ float4 merge_splits(const float* base, int splits, in
     return make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
 }
 
+// Sum over lanes of 32 per-lane partials, one per token: afterwards lane l
+// holds the total for token l. Each step keeps half of the tokens and adds
+// the partner's value for them, so token t is summed over lanes in the same
+// pairing order as warp_sum's butterfly (identical bits).
+__device__ __forceinline__ float transpose_reduce32(float v[32], int lane) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < o; ++i) {
+            const float keep = upper ? v[i + o] : v[i];
+            const float send = upper ? v[i] : v[i + o];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    return v[0];
+}
+
 template <typename KV>
 __global__ void __launch_bounds__(256) gqa_split_kernel(const AttnArgs a) {
+    extern __shared__ __align__(16) uint8_t attn_smem[];
+    KV* ks = reinterpret_cast<KV*>(attn_smem);
+    KV* vs = ks + kSubTile * kHeadDim;
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = kvh * a.groups + warp;
-    const int q_heads = a.kv_heads * a.groups;
     __shared__ int last_flag;
     __shared__ float red[8];
 
@@ -171,48 +197,85 @@ __global__ void __launch_bounds__(256) gqa_split_kernel(const AttnArgs a) {
 
     KV* kc = static_cast<KV*>(a.kcache) + b * a.batch_stride + kvh * a.head_stride;
     KV* vc = static_cast<KV*>(a.vcache) + b * a.batch_stride + kvh * a.head_stride;
-    if (a.knew && t0 <= pos && pos < t1) {
-        // This CTA's slice holds the new position: append k (normed, roped) and v.
+    const bool owns_new = a.knew && t0 <= pos && pos < t1;
+    float4 k_new = make_float4(0.f, 0.f, 0.f, 0.f), v_new = k_new;
+    if (owns_new) {
+        // This CTA's chunk holds the new position: append k (normed, roped) and v.
         if (warp == 0) {
-            float4 k = *reinterpret_cast<const float4*>(a.knew + b * a.q_batch_stride +
-                                                         static_cast<long long>(kvh) * kHeadDim + 4 * lane);
-            k = norm_rope(k, a.k_norm, cs, sn, a.eps, lane);
-            store4<KV>(kc + static_cast<long long>(pos) * a.time_stride + 4 * lane, k);
+            k_new = *reinterpret_cast<const float4*>(a.knew + b * a.q_batch_stride +
+                                                     static_cast<long long>(kvh) * kHeadDim + 4 * lane);
+            k_new = norm_rope(k_new, a.k_norm, cs, sn, a.eps, lane);
+            store4<KV>(kc + static_cast<long long>(pos) * a.time_stride + 4 * lane, k_new);
         }
         if (warp == a.groups - 1) {
-            const float4 v = *reinterpret_cast<const float4*>(a.vnew + b * a.q_batch_stride +
-                                                               static_cast<long long>(kvh) * kHeadDim + 4 * lane);
-            store4<KV>(vc + static_cast<long long>(pos) * a.time_stride + 4 * lane, v);
+            v_new = *reinterpret_cast<const float4*>(a.vnew + b * a.q_batch_stride +
+                                                     static_cast<long long>(kvh) * kHeadDim + 4 * lane);
+            store4<KV>(vc + static_cast<long long>(pos) * a.time_stride + 4 * lane, v_new);
         }
-        __syncthreads();
     }
 
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(kHeadDim)));
+    constexpr int kRowVecs = kHeadDim * sizeof(KV) / 16;  // 16-byte pieces per row
     float m = -INFINITY, l = 0.f;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    constexpr int U = 4;
-    for (int t = t0; t < t1; t += U) {
-        float4 kk[U], vv[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int tt = min(t + u, t1 - 1);
-            kk[u] = load4<KV>(kc + static_cast<long long>(tt) * a.time_stride + 4 * lane);
-            vv[u] = load4<KV>(vc + static_cast<long long>(tt) * a.time_stride + 4 * lane);
+    for (int base = t0; base < t1; base += kSubTile) {
+        const int n = min(kSubTile, t1 - base);
+        __syncthreads();  // the previous sub-tile is consumed
+        for (int i = threadIdx.x; i < 2 * n * kRowVecs; i += blockDim.x) {
+            const int which = i / (n * kRowVecs), rest = i % (n * kRowVecs);
+            const int r = rest / kRowVecs, piece = rest % kRowVecs;
+            if (base + r == pos && owns_new) continue;  // filled from registers below
+            const KV* src = (which ? vc : kc) + static_cast<long long>(base + r) * a.time_stride;
+            reinterpret_cast<uint4*>((which ? vs : ks) + r * kHeadDim)[piece] =
+                __ldcg(reinterpret_cast<const uint4*>(src) + piece);
         }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (t + u >= t1) break;
-            const float s = __fmul_rn(warp_sum(dot4(q, kk[u])), scale);
-            const float mn = fmaxf(m, s);
-            const float corr = exp_cw(m - mn);
-            const float p = exp_cw(s - mn);
-            l = __fmaf_rn(l, corr, p);
-            o.x = __fmaf_rn(o.x, corr, __fmul_rn(p, vv[u].x));
-            o.y = __fmaf_rn(o.y, corr, __fmul_rn(p, vv[u].y));
-            o.z = __fmaf_rn(o.z, corr, __fmul_rn(p, vv[u].z));
-            o.w = __fmaf_rn(o.w, corr, __fmul_rn(p, vv[u].w));
-            m = mn;
+        if (owns_new && pos >= base && pos < base + n) {
+            if (warp == 0) store4<KV>(ks + (pos - base) * kHeadDim + 4 * lane, k_new);
+            if (warp == a.groups - 1) store4<KV>(vs + (pos - base) * kHeadDim + 4 * lane, v_new);
         }
+        __syncthreads();
+
+        // scores, 32 tokens per round; lane l ends with token (round * 32 + l)
+        float p_round[2];
+        float mt = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            if (32 * r >= n) {  // uniform: the sub-tile has no second round
+                p_round[r] = -INFINITY;
+                continue;
+            }
+            float part[32];
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+                const int tt = min(32 * r + t, n - 1);
+                part[t] = dot4(q, load4<KV>(ks + tt * kHeadDim + 4 * lane));
+            }
+            const float sc = __fmul_rn(transpose_reduce32(part, lane), scale);
+            const bool valid = 32 * r + lane < n;
+            p_round[r] = valid ? sc : -INFINITY;
+            mt = fmaxf(mt, p_round[r]);
+        }
+        mt = warp_max(mt);
+#pragma unroll
+        for (int r = 0; r < 2; ++r) p_round[r] = (32 * r + lane < n) ? exp_cw(p_round[r] - mt) : 0.f;
+        const float lt = warp_sum(p_round[0] + p_round[1]);
+        float4 ot = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int t = 0; t < n; ++t) {
+            const float p = __shfl_sync(0xffffffffu, p_round[t >> 5], t & 31);
+            const float4 v = load4<KV>(vs + t * kHeadDim + 4 * lane);
+            ot.x = __fmaf_rn(p, v.x, ot.x);
+            ot.y = __fmaf_rn(p, v.y, ot.y);
+            ot.z = __fmaf_rn(p, v.z, ot.z);
+            ot.w = __fmaf_rn(p, v.w, ot.w);
+        }
+        const float mn = fmaxf(m, mt);
+        const float c_old = exp_cw(m - mn), c_new = exp_cw(mt - mn);
+        l = __fmaf_rn(l, c_old, __fmul_rn(lt, c_new));
+        o.x = __fmaf_rn(o.x, c_old, __fmul_rn(ot.x, c_new));
+        o.y = __fmaf_rn(o.y, c_old, __fmul_rn(ot.y, c_new));
+        o.z = __fmaf_rn(o.z, c_old, __fmul_rn(ot.z, c_new));
+        o.w = __fmaf_rn(o.w, c_old, __fmul_rn(ot.w, c_new));
+        m = mn;
     }
 
     float* out_h = a.out + b * a.out_batch_stride + static_cast<long long>(h) * kHeadDim;
@@ -263,7 +326,7 @@ __global__ void __launch_bounds__(256) gqa_split_kernel(const AttnArgs a) {
             atomic_max_nonneg(a.absmax_out + b, t);
         }
     }
-    (void)q_heads;
+
 }
 
 __global__ void __launch_bounds__(256) gqa_merge_kernel(const AttnArgs a) {
@@ -284,6 +347,7 @@ int launch_attention(const AttnArgs& a, int kv_dtype, int batch, cudaStream_t st
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.splits, a.kv_heads, batch);
     cfg.blockDim = dim3(32 * a.groups);
+    cfg.dynamicSmemBytes = 2 * kSubTile * kHeadDim * (kv_dtype == 0 ? 4 : 2);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -294,6 +358,7 @@ int launch_attention(const AttnArgs& a, int kv_dtype, int batch, cudaStream_t st
     else H4B_CUDA_TRY(cudaLaunchKernelEx(&cfg, gqa_split_kernel<__half>, a));
     if (a.splits > 1 && !a.counters) {
         cfg.gridDim = dim3(1, a.kv_heads, batch);
+        cfg.dynamicSmemBytes = 0;
         H4B_CUDA_TRY(cudaLaunchKernelEx(&cfg, gqa_merge_kernel, a));
     }
     return 0;

@@ -232,6 +232,18 @@ int decode_step(const h4b_model* m, const h4b_state* s, cudaStream_t stream) {
     return launch_stage(m, s, STAGE_FINALIZE, 0, stream, true);
 }
 
+int prepare_other_kernels() {
+    int r = 0;
+    if ((r = cudaFuncSetAttribute(gqa_split_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  2 * kSubTile * kHeadDim * 4)))
+        return r;
+    if ((r = set_carveout(gqa_split_kernel<float>)) || (r = set_carveout(gqa_split_kernel<__half>)) ||
+        (r = set_carveout(gqa_merge_kernel)) || (r = set_carveout(embed_kernel)) ||
+        (r = set_carveout(finalize_kernel)))
+        return r;
+    return 0;
+}
+
 struct GraphHandle {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;

@@ -14,9 +14,15 @@
 // previous kernel, so under programmatic dependent launch each GEMV's weight
 // stream overlaps the previous kernel's tail.
 //
+// Work split: the consumer warps own ring tiles round-robin (tile t belongs
+// to warp t % 8) and process a tile's rows in batches with independent
+// accumulators, so the fixed per-tile latencies (barrier wait, the row
+// reductions) are paid once per batch, not once per row.
+//
 // Math: a lane owns a fixed set of 16-byte weight chunks (32 codes) of
-// every row, so its 32-byte slice of the quantised activation lives in
-// registers for the whole kernel. Each 4-byte weight word holds 8 codes;
+// every row, so up to K = 4096 its 32-byte activation slices live in
+// registers for the whole kernel (above that they are re-read from shared
+// memory). Each 4-byte weight word holds 8 codes;
 // reading a nibble n as u = n ^ 8 = s + 8 (0..15) turns the even and odd
 // codes into two dp4a operands with no sign extension, and the bias
 // 8 * sum(x) is folded into the lane's starting accumulator.
@@ -31,7 +37,8 @@ constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumers + 32;
 constexpr int kMaxStages = 16;
-constexpr int kMaxSlots = 6;
+constexpr int kMaxSlots = 16;       // K <= 16384
+constexpr int kMaxRegSlots = 4;     // activation in registers up to K = 4096
 constexpr int kSwigluBlock = 4;  // gate/up interleave block (rows)
 constexpr int kRingBytes = 96 * 1024;
 constexpr int kStageTarget = 16 * 1024;
@@ -41,7 +48,6 @@ struct GemvArgs {
     const float* wscale;
     int rows, width;
     int row_align;      // rows per partition unit (2 * kSwigluBlock for SwiGLU)
-    int kgroups;        // warps sharing one row (each takes a K segment)
     int tile_rows;      // rows per ring stage
     int stages;         // ring depth
     int rows_cap;       // smem rows reserved per CTA (multiple of 32)
@@ -59,22 +65,27 @@ struct GemvArgs {
 };
 
 struct SmemLayout {
-    int red, xq, acc, scale, ring, total;
+    int red, xq, gamma, acc, scale, ring, total;
 };
 
-__host__ __device__ inline SmemLayout smem_layout(int width, int rows_cap, int stages, int stage_bytes) {
+__host__ __device__ inline SmemLayout smem_layout(int width, int rows_cap, int stages, int stage_bytes,
+                                                  bool with_gamma) {
     SmemLayout s;
     s.red = 2 * kMaxStages * 8;               // barriers first
     s.xq = s.red + 64 * 4;                    // 32 floats + flags
-    s.acc = s.xq + ((width + 127) & ~127);
+    s.gamma = s.xq + ((width + 127) & ~127);  // RMSNorm weight (PRO_RMSNORM only)
+    s.acc = s.gamma + (with_gamma ? width * 4 : 0);
     s.scale = s.acc + rows_cap * 4;
     s.ring = (s.scale + rows_cap * 4 + 127) & ~127;
     s.total = s.ring + stages * stage_bytes;
     return s;
 }
 
-__device__ __forceinline__ int dot_chunk(const uint4 w, const uint4 xa, const uint4 xb, int acc) {
-    // word j of the chunk pairs with activation words (even, odd) = x[2j], x[2j+1]
+// One 16-byte weight chunk (32 codes) against the lane's 32 activation
+// bytes. Word j of the chunk pairs with the activation words (even, odd) of
+// column group j and feeds accumulator j, so the four dp4a chains are
+// independent.
+__device__ __forceinline__ void dot_chunk(const uint4 w, const uint4 xa, const uint4 xb, int acc[4]) {
     const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
     const uint32_t xe[4] = {xa.x, xa.z, xb.x, xb.z};
     const uint32_t xo[4] = {xa.y, xa.w, xb.y, xb.w};
@@ -82,10 +93,9 @@ __device__ __forceinline__ int dot_chunk(const uint4 w, const uint4 xa, const ui
     for (int j = 0; j < 4; ++j) {
         const uint32_t lo = (ww[j] & 0x0F0F0F0Fu) ^ 0x08080808u;
         const uint32_t hi = ((ww[j] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
-        acc = __dp4a(static_cast<int>(lo), static_cast<int>(xe[j]), acc);
-        acc = __dp4a(static_cast<int>(hi), static_cast<int>(xo[j]), acc);
+        acc[j] = __dp4a(static_cast<int>(lo), static_cast<int>(xe[j]), acc[j]);
+        acc[j] = __dp4a(static_cast<int>(hi), static_cast<int>(xo[j]), acc[j]);
     }
-    return acc;
 }
 
 // Writes the 8 quantised values of group g (columns 8g..8g+7) as
@@ -106,7 +116,7 @@ __device__ __forceinline__ void load8(const float* p, float v[8]) {
 // Builds the permuted int8 activation in shared memory; returns the dequant
 // scale. Runs on the consumer warps only (named barrier 1).
 template <int PRO>
-__device__ float gemv_prologue(const GemvArgs& a, int8_t* xq, float* red) {
+__device__ float gemv_prologue(const GemvArgs& a, int8_t* xq, float* red, const float* gamma_s) {
     const int tid = threadIdx.x;
     const int groups = a.width >> 3;
     if constexpr (PRO == PRO_INT8) {
@@ -143,7 +153,7 @@ __device__ float gemv_prologue(const GemvArgs& a, int8_t* xq, float* red) {
             for (int g = tid; g < groups; g += kConsumers) {
                 float v[8], gm[8];
                 load8(a.xin + 8 * g, v);
-                if constexpr (PRO == PRO_RMSNORM) load8(a.gamma + 8 * g, gm);
+                if constexpr (PRO == PRO_RMSNORM) load8(gamma_s + 8 * g, gm);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                     const float n = (PRO == PRO_RMSNORM) ? __fmul_rn(__fmul_rn(v[e], inv), gm[e]) : v[e];
@@ -153,11 +163,12 @@ __device__ float gemv_prologue(const GemvArgs& a, int8_t* xq, float* red) {
             m = group_max(local, red, kConsumerWarps, 1);
         }
         const float qs = quant_multiplier(m);
+#pragma unroll 2
         for (int g = tid; g < groups; g += kConsumers) {
             float v[8], gm[8];
             int q[8];
             load8(a.xin + 8 * g, v);
-            if constexpr (PRO == PRO_RMSNORM) load8(a.gamma + 8 * g, gm);
+            if constexpr (PRO == PRO_RMSNORM) load8(gamma_s + 8 * g, gm);
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
                 const float n = (PRO == PRO_RMSNORM) ? __fmul_rn(__fmul_rn(v[e], inv), gm[e]) : v[e];
@@ -174,7 +185,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int kb = a.width >> 1;
     const uint32_t stage_bytes = static_cast<uint32_t>(a.tile_rows) * kb;
-    const SmemLayout L = smem_layout(a.width, a.rows_cap, a.stages, stage_bytes);
+    const SmemLayout L = smem_layout(a.width, a.rows_cap, a.stages, stage_bytes, PRO == PRO_RMSNORM);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kMaxStages;
     float* red = reinterpret_cast<float*>(smem + L.red);
@@ -195,7 +206,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     if (tid == 0) {
         for (int s = 0; s < a.stages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
+            mbar_init(&empty[s], 1);  // released by the tile's owning warp
         }
         flags[0] = 0;
         flags[2] = wait_failed_before();
@@ -241,36 +252,44 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
         async_copy_wait_all();
     } else {
         // ---------------- consumer warps ----------------
+        float* gamma_s = reinterpret_cast<float*>(smem + L.gamma);
+        if constexpr (PRO == PRO_RMSNORM) {
+            // The norm weight is static: stage it before the dependency wait.
+            for (int i = tid; i < (a.width >> 2); i += kConsumers)
+                reinterpret_cast<float4*>(gamma_s)[i] = __ldg(reinterpret_cast<const float4*>(a.gamma) + i);
+        }
         pdl_wait();
-        if (a.kgroups > 1)
-            for (int i = tid; i < nrows; i += kConsumers) acc_s[i] = 0;
-        const float act_scale = gemv_prologue<(PRO)>(a, xq, red);
+        const float act_scale = gemv_prologue<(PRO)>(a, xq, red, gamma_s);
         if (tid == 0) flags[1] = __float_as_int(act_scale);
         named_sync(1, kConsumers);
 
         const int chunks = a.width >> 5;
-        const int G = a.kgroups;
-        const int kg = warp % G, rg = warp / G, nrg = kConsumerWarps / G;
-        const int c_begin = kg * chunks / G, c_end = (kg + 1) * chunks / G;
-        uint4 xa[SLOTS], xb[SLOTS];
+        constexpr bool kXReg = SLOTS <= kMaxRegSlots;
+        constexpr int kXSlots = kXReg ? SLOTS : 1;
+        constexpr int RB = SLOTS <= 3 ? 4 : (SLOTS <= 4 ? 3 : 2);  // rows per batch
+        uint4 xa[kXSlots], xb[kXSlots];
         int bias = 0;
 #pragma unroll
         for (int j = 0; j < SLOTS; ++j) {
-            const int c = c_begin + lane + 32 * j;
-            if (c < c_end) {
-                xa[j] = *reinterpret_cast<const uint4*>(xq + 32 * c);
-                xb[j] = *reinterpret_cast<const uint4*>(xq + 32 * c + 16);
-                const uint32_t words[8] = {xa[j].x, xa[j].y, xa[j].z, xa[j].w, xb[j].x, xb[j].y, xb[j].z, xb[j].w};
+            const int c = lane + 32 * j;
+            if (c < chunks) {
+                const uint4 va = *reinterpret_cast<const uint4*>(xq + 32 * c);
+                const uint4 vb = *reinterpret_cast<const uint4*>(xq + 32 * c + 16);
+                const uint32_t words[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
                 for (int e = 0; e < 8; ++e) bias = __dp4a(static_cast<int>(words[e]), 0x01010101, bias);
-            } else {
+                if constexpr (kXReg) {
+                    xa[j] = va;
+                    xb[j] = vb;
+                }
+            } else if constexpr (kXReg) {
                 xa[j] = make_uint4(0, 0, 0, 0);
                 xb[j] = make_uint4(0, 0, 0, 0);
             }
         }
         bias *= -8;
 
-        for (int t = 0; t < ntiles; ++t) {
+        for (int t = warp; t < ntiles; t += kConsumerWarps) {
             const int s = t % a.stages;
             if (!mbar_wait(&full[s], (t / a.stages) & 1)) {
                 atomicOr(&flags[0], 1);
@@ -278,23 +297,43 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
             }
             const uint8_t* tile = ring + static_cast<size_t>(s) * stage_bytes;
             const int trows = min(a.tile_rows, nrows - t * a.tile_rows);
-            for (int lr = rg; lr < trows; lr += nrg) {
-                const uint8_t* row = tile + static_cast<size_t>(lr) * kb;
-                int acc0 = bias, acc1 = 0;
+            for (int b0 = 0; b0 < trows; b0 += RB) {
+                int acc[RB][4];
+#pragma unroll
+                for (int i = 0; i < RB; ++i) {
+                    acc[i][0] = bias;
+                    acc[i][1] = acc[i][2] = acc[i][3] = 0;
+                }
 #pragma unroll
                 for (int j = 0; j < SLOTS; ++j) {
-                    const int c = c_begin + lane + 32 * j;
-                    if (c < c_end) {
-                        const uint4 w = *reinterpret_cast<const uint4*>(row + 16 * c);
-                        if (j & 1) acc1 = dot_chunk(w, xa[j], xb[j], acc1);
-                        else acc0 = dot_chunk(w, xa[j], xb[j], acc0);
+                    const int c = lane + 32 * j;
+                    if (c < chunks) {
+                        uint4 w[RB];
+#pragma unroll
+                        for (int i = 0; i < RB; ++i) {
+                            const int lr = min(b0 + i, trows - 1);  // a short batch repeats its last row
+                            w[i] = *reinterpret_cast<const uint4*>(tile + static_cast<size_t>(lr) * kb + 16 * c);
+                        }
+                        uint4 va, vb;
+                        if constexpr (kXReg) {
+                            va = xa[j];
+                            vb = xb[j];
+                        } else {
+                            va = *reinterpret_cast<const uint4*>(xq + 32 * c);
+                            vb = *reinterpret_cast<const uint4*>(xq + 32 * c + 16);
+                        }
+#pragma unroll
+                        for (int i = 0; i < RB; ++i) dot_chunk(w[i], va, vb, acc[i]);
                     }
                 }
-                const int total = __reduce_add_sync(0xffffffffu, acc0 + acc1);
+                int total[RB];
+#pragma unroll
+                for (int i = 0; i < RB; ++i)
+                    total[i] = __reduce_add_sync(0xffffffffu, (acc[i][0] + acc[i][1]) + (acc[i][2] + acc[i][3]));
                 if (lane == 0) {
-                    const int i = t * a.tile_rows + lr;
-                    if (G == 1) acc_s[i] = total;
-                    else atomicAdd(&acc_s[i], total);
+#pragma unroll
+                    for (int i = 0; i < RB; ++i)
+                        if (b0 + i < trows) acc_s[t * a.tile_rows + b0 + i] = total[i];
                 }
             }
             __syncwarp();
@@ -366,7 +405,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
 // Host-side planning and launch.
 
 struct GemvPlan {
-    int grid, kgroups, slots, tile_rows, stages, rows_cap, smem;
+    int grid, slots, tile_rows, stages, rows_cap, smem;
 };
 
 static int g_sm_count = 0;
@@ -381,27 +420,44 @@ int sm_count() {
     return g_sm_count;
 }
 
+// Slot counts that have kernel instantiations (a lane covers `slots` 16-byte
+// chunks of every row).
+static int instantiated_slots(int needed) {
+    static const int kSlots[] = {1, 2, 3, 4, 6, 8, 10, 12, 16};
+    for (int v : kSlots)
+        if (v >= needed) return v;
+    return 0;
+}
+
 int plan_gemv(int rows, int width, int row_align, GemvPlan* p) {
     if (rows <= 0 || width <= 0 || (width & 31) || rows % row_align) return H4B_EINVAL;
     const int chunks = width >> 5;
-    int G = 1;
-    while ((chunks + 32 * G - 1) / (32 * G) > kMaxSlots && G < kConsumerWarps) G *= 2;
-    const int seg = (chunks + G - 1) / G;
-    const int slots = (seg + 31) / 32;
-    if (slots > kMaxSlots) return H4B_EUNSUPPORTED;
-    const int nrg = kConsumerWarps / G;
+    const int slots = instantiated_slots((chunks + 31) / 32);
+    if (slots == 0) return H4B_EUNSUPPORTED;
     const int kb = width >> 1;
-    const int m = max(1, kStageTarget / (kb * nrg));
-    const int tile_rows = nrg * m;
+    const int units = rows / row_align;
+    const int grid = max(1, min(sm_count(), units));
+    const int per_cta = ((units + grid - 1) / grid) * row_align;
+    // Enough tiles per CTA for every consumer warp, at most 8 rows / 16 KB each.
+    int tile_rows = max(1, min(8, (per_cta + kConsumerWarps - 1) / kConsumerWarps));
+    tile_rows = max(1, min(tile_rows, kStageTarget / kb));
     const int stage_bytes = tile_rows * kb;
     if (stage_bytes > 64 * 1024) return H4B_EUNSUPPORTED;
     const int stages = max(2, min(kMaxStages, kRingBytes / stage_bytes));
-    const int units = rows / row_align;
-    const int grid = max(1, min(sm_count(), units));
-    const int rows_cap = (((units + grid - 1) / grid) * row_align + 31) & ~31;
-    const SmemLayout L = smem_layout(width, rows_cap, stages, stage_bytes);
+    const int rows_cap = (per_cta + 31) & ~31;
+    const SmemLayout L = smem_layout(width, rows_cap, stages, stage_bytes, true);
     if (L.total > 227 * 1024) return H4B_EUNSUPPORTED;
-    *p = GemvPlan{grid, G, slots, tile_rows, stages, rows_cap, L.total};
+    *p = GemvPlan{grid, slots, tile_rows, stages, rows_cap, L.total};
+    return 0;
+}
+
+// Every kernel of the decode chain asks for the same (maximal) shared-memory
+// carveout, so a kernel's CTAs can become resident next to its predecessor's
+// under programmatic dependent launch instead of waiting for an SM to drain.
+template <typename K>
+int set_carveout(K kernel) {
+    H4B_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      cudaSharedmemCarveoutMaxShared));
     return 0;
 }
 
@@ -409,7 +465,7 @@ template <int PRO, int EPI, int SLOTS>
 static int set_smem_limit() {
     H4B_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel<PRO, EPI, SLOTS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       227 * 1024));
-    return 0;
+    return set_carveout(gemv_kernel<PRO, EPI, SLOTS>);
 }
 
 template <int PRO, int EPI>
@@ -417,12 +473,15 @@ static int set_smem_limits() {
     int r = 0;
     if ((r = set_smem_limit<PRO, EPI, 1>()) || (r = set_smem_limit<PRO, EPI, 2>()) ||
         (r = set_smem_limit<PRO, EPI, 3>()) || (r = set_smem_limit<PRO, EPI, 4>()) ||
-        (r = set_smem_limit<PRO, EPI, 5>()) || (r = set_smem_limit<PRO, EPI, 6>()))
+        (r = set_smem_limit<PRO, EPI, 6>()) || (r = set_smem_limit<PRO, EPI, 8>()) ||
+        (r = set_smem_limit<PRO, EPI, 10>()) || (r = set_smem_limit<PRO, EPI, 12>()) ||
+        (r = set_smem_limit<PRO, EPI, 16>()))
         return r;
     return 0;
 }
 
 static bool g_prepared = false;
+int prepare_other_kernels();  // attention and the small kernels (defined after them)
 
 // Raises every GEMV instantiation's dynamic shared-memory limit. Runs once,
 // outside any stream capture.
@@ -433,6 +492,7 @@ int prepare_kernels() {
         (r = set_smem_limits<PRO_RMSNORM, EPI_STORE>()) || (r = set_smem_limits<PRO_QUANT_ABSMAX, EPI_RESIDUAL>()) ||
         (r = set_smem_limits<PRO_RMSNORM, EPI_SWIGLU>()) || (r = set_smem_limits<PRO_RMSNORM, EPI_ARGMAX>()))
         return r;
+    if ((r = prepare_other_kernels())) return r;
     sm_count();
     g_prepared = true;
     return 0;
@@ -462,8 +522,11 @@ static int launch_slots(const GemvArgs& a, const GemvPlan& p, cudaStream_t s, bo
         case 2: return launch_t<PRO, EPI, 2>(a, p, s, pdl);
         case 3: return launch_t<PRO, EPI, 3>(a, p, s, pdl);
         case 4: return launch_t<PRO, EPI, 4>(a, p, s, pdl);
-        case 5: return launch_t<PRO, EPI, 5>(a, p, s, pdl);
         case 6: return launch_t<PRO, EPI, 6>(a, p, s, pdl);
+        case 8: return launch_t<PRO, EPI, 8>(a, p, s, pdl);
+        case 10: return launch_t<PRO, EPI, 10>(a, p, s, pdl);
+        case 12: return launch_t<PRO, EPI, 12>(a, p, s, pdl);
+        case 16: return launch_t<PRO, EPI, 16>(a, p, s, pdl);
         default: return H4B_EUNSUPPORTED;
     }
 }
@@ -480,7 +543,6 @@ int launch_gemv(int pro, int epi, GemvArgs a, cudaStream_t stream, bool pdl) {
     if (rc) return rc;
     if (reinterpret_cast<uintptr_t>(a.w) & 15) return H4B_EINVAL;
     a.row_align = align;
-    a.kgroups = p.kgroups;
     a.tile_rows = p.tile_rows;
     a.stages = p.stages;
     a.rows_cap = p.rows_cap;

@@ -276,11 +276,15 @@ void oracle_silu_mul(const float *gate, const float *up, float *out, int n)
     for (int i = 0; i < n; ++i) out[i] = (gate[i] / (1.0f + oracle_expf(-gate[i]))) * up[i];
 }
 
-/* Single-token GQA in the device's split-K order (head_dim 128): the context
- * is cut into `splits` chunks of ceil(context/splits); each chunk runs an
- * online softmax token by token (m, l, o), and the chunks are merged in order
- * with weights exp(m_s - max m). keys/values element (t, kv, d) sits at
- * t * time_stride + kv * head_stride + d. */
+/* Single-token GQA in the device's split-K order (head_dim 128). The context
+ * is cut into `splits` chunks of ceil(context/splits) tokens, each chunk into
+ * sub-tiles of 64 tokens. Per sub-tile: scores s_t = head_dot(q, k_t) * scale,
+ * m = max s, p_t = exp(s_t - m), l = butterfly over lanes of (p_lane +
+ * p_lane+32), o[d] = sum_t p_t v_t[d] by fmaf in token order. Sub-tiles fold
+ * into the chunk's running (m, l, o) with weights exp(m_old - m_new) and
+ * exp(m_sub - m_new); chunks merge in order with weights exp(m_c - max m).
+ * keys/values element (t, kv, d) sits at t * time_stride + kv * head_stride + d. */
+#define SUBTILE 64
 void oracle_gqa_splitk(const float *query, const float *keys, const float *values, float *output,
                        int context, int kv_heads, int groups, long time_stride, long head_stride, int splits)
 {
@@ -292,35 +296,49 @@ void oracle_gqa_splitk(const float *query, const float *keys, const float *value
         const int kvh = h / groups;
         const float *q = query + 128 * h;
         float ms[64], ls[64], os[64][128];
-        for (int s = 0; s < splits; ++s) {
-            const int t0 = s * chunk < context ? s * chunk : context;
+        for (int c = 0; c < splits; ++c) {
+            const int t0 = c * chunk < context ? c * chunk : context;
             const int t1 = t0 + chunk < context ? t0 + chunk : context;
-            float m = -INFINITY, l = 0.0f;
-            float *o = os[s];
+            float m = -INFINITY, l = 0.0f, o[128];
             for (int d = 0; d < 128; ++d) o[d] = 0.0f;
-            for (int t = t0; t < t1; ++t) {
-                const float *k = keys + t * time_stride + kvh * head_stride;
-                const float *v = values + t * time_stride + kvh * head_stride;
-                const float sc = head_dot(q, k) * scale;
-                const float mn = fmaxf(m, sc);
-                const float corr = oracle_expf(m - mn);
-                const float p = oracle_expf(sc - mn);
-                l = fmaf(l, corr, p);
-                for (int d = 0; d < 128; ++d) o[d] = fmaf(o[d], corr, p * v[d]);
+            for (int base = t0; base < t1; base += SUBTILE) {
+                const int n = t1 - base < SUBTILE ? t1 - base : SUBTILE;
+                float sc[SUBTILE], p[SUBTILE];
+                float mt = -INFINITY;
+                for (int i = 0; i < n; ++i) {
+                    const float *k = keys + (long)(base + i) * time_stride + kvh * head_stride;
+                    sc[i] = head_dot(q, k) * scale;
+                    mt = fmaxf(mt, sc[i]);
+                }
+                for (int i = 0; i < SUBTILE; ++i) p[i] = i < n ? oracle_expf(sc[i] - mt) : 0.0f;
+                float lanes[32];
+                for (int ln = 0; ln < 32; ++ln) lanes[ln] = p[ln] + p[ln + 32];
+                const float lt = butterfly32(lanes);
+                float ot[128];
+                for (int d = 0; d < 128; ++d) ot[d] = 0.0f;
+                for (int i = 0; i < n; ++i) {
+                    const float *v = values + (long)(base + i) * time_stride + kvh * head_stride;
+                    for (int d = 0; d < 128; ++d) ot[d] = fmaf(p[i], v[d], ot[d]);
+                }
+                const float mn = fmaxf(m, mt);
+                const float c_old = oracle_expf(m - mn), c_new = oracle_expf(mt - mn);
+                l = fmaf(l, c_old, lt * c_new);
+                for (int d = 0; d < 128; ++d) o[d] = fmaf(o[d], c_old, ot[d] * c_new);
                 m = mn;
             }
-            ms[s] = m;
-            ls[s] = l;
+            ms[c] = m;
+            ls[c] = l;
+            memcpy(os[c], o, sizeof(o));
         }
         float mmax = -INFINITY;
-        for (int s = 0; s < splits; ++s) mmax = fmaxf(mmax, ms[s]);
+        for (int c = 0; c < splits; ++c) mmax = fmaxf(mmax, ms[c]);
         float l = 0.0f, acc[128];
         for (int d = 0; d < 128; ++d) acc[d] = 0.0f;
-        for (int s = 0; s < splits; ++s) {
-            if (ls[s] == 0.0f) continue;
-            const float wgt = oracle_expf(ms[s] - mmax);
-            l = fmaf(ls[s], wgt, l);
-            for (int d = 0; d < 128; ++d) acc[d] = fmaf(os[s][d], wgt, acc[d]);
+        for (int c = 0; c < splits; ++c) {
+            if (ls[c] == 0.0f) continue;
+            const float wgt = oracle_expf(ms[c] - mmax);
+            l = fmaf(ls[c], wgt, l);
+            for (int d = 0; d < 128; ++d) acc[d] = fmaf(os[c][d], wgt, acc[d]);
         }
         const float inv = 1.0f / l;
         for (int d = 0; d < 128; ++d) output[128 * h + d] = acc[d] * inv;
