@@ -13,6 +13,7 @@ LIBRARY = Path(__file__).resolve().parent / "libharsh4b_b200.so"
 
 H4B_EINVAL = -1
 H4B_EUNSUPPORTED = -2
+H4B_ETOOBIG = -3
 
 STATUS_WAIT_TIMEOUT = 1
 STATUS_BAD_TOKEN = 2
@@ -49,6 +50,7 @@ _SIGNATURES = {
     "h4b_rmsnorm": [_vp, _vp, _vp, _i32, _f32, _vp],
     "h4b_add_inplace": [_vp, _vp, _i32, _vp],
     "h4b_gqa_decode": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp],
+    "h4b_gqa_decode_noalloc": [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
     "h4b_embedding": [_vp, _vp, _vp, _vp, _i32, _i32, _vp],
     "h4b_argmax": [_vp, _i32, _vp, _vp],
     "h4b_validate": [ctypes.POINTER(ModelDesc), ctypes.POINTER(StateDesc)],
@@ -95,7 +97,9 @@ def lib() -> ctypes.CDLL:
 
 
 _MESSAGES = {H4B_EINVAL: "invalid argument (size, alignment or null pointer)",
-             H4B_EUNSUPPORTED: "shape not supported by the sm_100a kernels"}
+             H4B_EUNSUPPORTED: "shape not supported by the sm_100a kernels",
+             H4B_ETOOBIG: "request exceeds the library's static scratch (kv_heads * groups * (head_dim + 4) "
+                          "must be <= 262144 floats)"}
 
 
 def check(rc: int, what: str) -> None:

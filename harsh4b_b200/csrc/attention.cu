@@ -21,6 +21,7 @@
 // per-head RMSNorm of q and k (divide by sqrt(mean + eps), then scale),
 // half-split RoPE at the current position, and the KV-cache append.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -387,6 +388,68 @@ extern "C" int h4b_gqa_decode(const float* query, const float* keys, const float
     const int fit = score_stride / h4b::kPartialStride;
     a.splits = std::max(1, std::min({fit, 64, (context + 63) / 64}));
     a.partials = scores;
+    a.out = output;
+    return h4b::launch_attention(a, 0, 1, static_cast<cudaStream_t>(stream), false);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of h4b_gqa_decode.
+//
+// The split partials live in this file-scope array instead of caller
+// scratch. Every GPU that loads the library holds it (1 MiB) until the
+// process exits. Host code must not hand the array's name to a kernel: on
+// the host it is only a stand-in, so its device address is looked up once
+// per device with cudaGetSymbolAddress (with that device current) and cached.
+namespace h4b {
+
+constexpr int kNoAllocScratchFloats = 256 * 1024;  // 1 MiB
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocScratchFloats];
+
+constexpr int kMaxDevices = 64;
+static std::once_flag g_noalloc_once[kMaxDevices];
+static float* g_noalloc_ptr[kMaxDevices];
+static cudaError_t g_noalloc_err[kMaxDevices];
+
+static int noalloc_scratch(float** out) {
+    int dev = 0;
+    H4B_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return H4B_EUNSUPPORTED;
+    std::call_once(g_noalloc_once[dev], [dev] {
+        void* ptr = nullptr;
+        g_noalloc_err[dev] = cudaGetSymbolAddress(&ptr, g_noalloc_partials);
+        g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+    });
+    if (g_noalloc_err[dev] != cudaSuccess) return static_cast<int>(g_noalloc_err[dev]);
+    *out = g_noalloc_ptr[dev];
+    return 0;
+}
+
+}  // namespace h4b
+
+extern "C" int h4b_gqa_decode_noalloc(const float* query, const float* keys, const float* values, float* output,
+                                      int context, int kv_heads, int groups, int head_dim, void* stream) {
+    if (!query || !keys || !values || !output) return H4B_EINVAL;
+    if (head_dim != h4b::kHeadDim) return H4B_EUNSUPPORTED;
+    if (context < 1 || kv_heads < 1 || groups < 1 || groups > 8) return H4B_EINVAL;
+    const long long per_split = static_cast<long long>(kv_heads) * groups * h4b::kPartialStride;
+    if (per_split > h4b::kNoAllocScratchFloats) return H4B_ETOOBIG;
+    float* scratch = nullptr;
+    const int rc = h4b::noalloc_scratch(&scratch);
+    if (rc) return rc;
+    h4b::AttnArgs a = {};
+    a.q = query;
+    a.kcache = const_cast<float*>(keys);
+    a.vcache = const_cast<float*>(values);
+    a.head_stride = head_dim;
+    a.time_stride = static_cast<long long>(kv_heads) * head_dim;
+    a.context = context;
+    a.capacity = context;
+    a.groups = groups;
+    a.kv_heads = kv_heads;
+    // Same split rule as h4b_gqa_decode, with the static array as the room.
+    const int fit = static_cast<int>(h4b::kNoAllocScratchFloats / per_split);
+    a.splits = std::max(1, std::min({fit, 64, (context + 63) / 64}));
+    a.partials = scratch;  // every slot read is written earlier in the same call
     a.out = output;
     return h4b::launch_attention(a, 0, 1, static_cast<cudaStream_t>(stream), false);
 }

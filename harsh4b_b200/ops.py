@@ -89,6 +89,22 @@ def gqa_decode(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, co
     return out
 
 
+def gqa_decode_noalloc(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, context: int,
+                       kv_heads: int, groups: int, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """gqa_decode without a scratch buffer, for callers that cannot allocate
+    device memory when attention runs (see h4b_gqa_decode_noalloc in
+    include/harsh4b_b200.h): the split partials live in a fixed 1 MiB array
+    inside the library, so concurrent calls on different streams race."""
+    head_dim = keys.shape[-1]
+    if out is None:
+        raise ValueError("gqa_decode_noalloc allocates nothing: pass `out` (q_heads x head_dim fp32)")
+    check(lib().h4b_gqa_decode_noalloc(_dev(query, torch.float32, "query"), _dev(keys, torch.float32, "keys"),
+                                       _dev(values, torch.float32, "values"), _dev(out, torch.float32, "out"),
+                                       context, kv_heads, groups, head_dim, stream_handle()),
+          "h4b_gqa_decode_noalloc")
+    return out
+
+
 def embedding(token: torch.Tensor, table: torch.Tensor, scales: torch.Tensor,
               out: torch.Tensor | None = None) -> torch.Tensor:
     vocab, packed = table.shape

@@ -27,6 +27,7 @@ extern "C" {
 
 #define H4B_EINVAL (-1)       /* bad size, alignment or pointer */
 #define H4B_EUNSUPPORTED (-2) /* shape outside what the kernels implement */
+#define H4B_ETOOBIG (-3)      /* request exceeds the library's static scratch */
 
 /* Device-side status word (bit 1: a bounded wait gave up; bit 2: token id
  * out of range; bit 4: position beyond capacity). Reads and clears it; the
@@ -80,6 +81,23 @@ int h4b_add_inplace(float *x, const float *y, int n, void *stream);
 int h4b_gqa_decode(const float *query, const float *keys, const float *values, float *scores,
                    float *output, int context, int kv_heads, int groups, int head_dim,
                    int score_stride, void *stream);
+
+/* No counterpart in the reference. The same attention as h4b_gqa_decode for
+ * callers that cannot allocate device memory when they run it: for example
+ * a serving process that reserved nearly all HBM for its own pool up front
+ * (a fresh cudaMalloc would fail or fragment that reservation), or a plugin
+ * whose host application owns the device allocator and forbids side
+ * allocations. It takes no scratch argument and allocates nothing: the
+ * split partials live in a 1 MiB array inside the library (256K floats,
+ * held on every GPU that loads the library until the process exits). It
+ * needs kv_heads * groups * (head_dim + 4) <= 262144 floats and returns
+ * H4B_ETOOBIG beyond that. The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture. All calls share the one array: calls that
+ * overlap on the GPU (other streams, other host threads) race on it. No
+ * state carries over between calls -- every slot a call reads, it wrote. */
+int h4b_gqa_decode_noalloc(const float *query, const float *keys, const float *values, float *output,
+                           int context, int kv_heads, int groups, int head_dim, void *stream);
 
 /* Replaces LiteSparkQwen._embedding_into (cpu_lightspark.py:341-349):
  * out[k] = int4(embedding[token, k]) * scales[token]. The token id is read
