@@ -52,6 +52,10 @@ def parse_args():
     parser.add_argument("--shapes", default="q,k,v,o,gate,up,down",
                         help="gemv workload: comma-separated projection names")
     parser.add_argument("--iters", type=int, default=200, help="gemv workload: timed launches per shape")
+    parser.add_argument("--mode", choices=("persistent", "chain"), default="persistent",
+                        help="decode step: one persistent kernel per token, or the PDL kernel chain")
+    parser.add_argument("--layers", type=int, default=None,
+                        help="override the layer count (a smaller model for profiling captures; not the headline)")
     return parser.parse_args()
 
 
@@ -258,11 +262,11 @@ def run_ours(args, rank, world, local_rank, dist) -> int:
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
-    config = qwen3_4b_config()
+    config = qwen3_4b_config(**({"num_hidden_layers": args.layers} if args.layers else {}))
     checkpoint = synthetic_checkpoint(config, seed=args.seed)
     # every replica decodes its own random prompt
     prompt = synthetic_prompt(config, PROMPT, seed=args.seed + rank)
-    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype=args.kv_dtype, device=device)
+    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype=args.kv_dtype, device=device, mode=args.mode)
     capacity = PROMPT + args.warmup + args.steps + 1
 
     def barrier():
@@ -334,12 +338,13 @@ def run_ours(args, rank, world, local_rank, dist) -> int:
         "scaling": "weak", "vs_baseline": None, "dtype": "int4xint8", "data": "synthetic",
         "config": {"workload": "config0: Qwen3-4B int4 synthetic checkpoint (seed 0), 128-token random prompt, "
                                "batch-1 greedy decode", "prompt": PROMPT, "kv_dtype": args.kv_dtype,
+                   "layers": model.n_layers, "decode_step": args.mode,
                    "context": [PROMPT + args.warmup, PROMPT + args.warmup + args.steps],
                    "l2": "inputs larger than L2 (1.82 GB of weights streamed per token)",
                    "parallelism": f"replicas x{world}"},
         "e2e": {"value": round(world * args.steps / e2e_elapsed, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4},
-        "gpu_launches": args.steps * (5 * model.n_layers + 3),
+        "gpu_launches": args.steps * (1 if args.mode == "persistent" else 5 * model.n_layers + 3),
         "step_roofline": {"bytes_per_token": bytes_per_token,
                           "achieved_gbs": round(bytes_per_token * args.steps / elapsed / 1e9, 1),
                           "frac": round(bytes_per_token * args.steps / elapsed / 1e9 / peaks["hbm_gbs"], 4)},

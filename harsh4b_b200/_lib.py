@@ -37,7 +37,7 @@ class StateDesc(ctypes.Structure):
 
     _fields_ = [("capacity", _i32), ("kv_dtype", _i32), ("attn_splits", _i32)] + [
         (n, _vp) for n in ("k_cache", "v_cache", "position", "token", "next_token", "x", "qkv", "attended",
-                           "act", "logits", "absmax", "argmax_key", "attn_partials", "attn_counters")]
+                           "act", "logits", "absmax", "argmax_key", "attn_partials", "attn_counters", "sync")]
 
 
 _SIGNATURES = {
@@ -57,6 +57,9 @@ _SIGNATURES = {
     "h4b_decode_stage": [ctypes.POINTER(ModelDesc), ctypes.POINTER(StateDesc), _i32, _i32, _vp],
     "h4b_decode_step": [ctypes.POINTER(ModelDesc), ctypes.POINTER(StateDesc), _vp],
     "h4b_graph_create": [ctypes.POINTER(ModelDesc), ctypes.POINTER(StateDesc), _vp, ctypes.POINTER(_vp)],
+    "h4b_decode_persistent": [ctypes.POINTER(ModelDesc), ctypes.POINTER(StateDesc), _vp],
+    "h4b_graph_create_persistent": [ctypes.POINTER(ModelDesc), ctypes.POINTER(StateDesc), _vp,
+                                    ctypes.POINTER(_vp)],
     "h4b_graph_launch": [_vp, _vp],
     "h4b_graph_destroy": [_vp],
 }

@@ -232,8 +232,11 @@ int decode_step(const h4b_model* m, const h4b_state* s, cudaStream_t stream) {
     return launch_stage(m, s, STAGE_FINALIZE, 0, stream, true);
 }
 
+int prepare_persistent();  // persistent.cu
+
 int prepare_other_kernels() {
     int r = 0;
+    if ((r = prepare_persistent())) return r;
     if ((r = cudaFuncSetAttribute(gqa_split_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   2 * kSubTile * kHeadDim * 4)))
         return r;
@@ -325,16 +328,21 @@ extern "C" int h4b_decode_step(const h4b_model* model, const h4b_state* state, v
     return h4b::decode_step(model, state, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int h4b_graph_create(const h4b_model* model, const h4b_state* state, void* stream, void** graph_out) {
+namespace h4b {
+int decode_persistent(const h4b_model* m, const h4b_state* s, cudaStream_t stream);  // persistent.cu
+
+static int capture_step(const h4b_model* model, const h4b_state* state, void* stream, void** graph_out,
+                        int (*step)(const h4b_model*, const h4b_state*, cudaStream_t)) {
     if (!graph_out) return H4B_EINVAL;
-    int rc = h4b::validate(model, state);
+    int rc = validate(model, state);
     if (rc) return rc;
+    if (!g_prepared && (rc = prepare_kernels())) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    h4b::GraphHandle* h = new (std::nothrow) h4b::GraphHandle();
+    GraphHandle* h = new (std::nothrow) GraphHandle();
     if (!h) return H4B_EINVAL;
     cudaError_t e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
     if (e != cudaSuccess) { delete h; return static_cast<int>(e); }
-    rc = h4b::decode_step(model, state, s);
+    rc = step(model, state, s);
     e = cudaStreamEndCapture(s, &h->graph);
     if (rc || e != cudaSuccess) {
         if (h->graph) cudaGraphDestroy(h->graph);
@@ -349,6 +357,16 @@ extern "C" int h4b_graph_create(const h4b_model* model, const h4b_state* state, 
     }
     *graph_out = h;
     return 0;
+}
+}  // namespace h4b
+
+extern "C" int h4b_graph_create(const h4b_model* model, const h4b_state* state, void* stream, void** graph_out) {
+    return h4b::capture_step(model, state, stream, graph_out, h4b::decode_step);
+}
+
+extern "C" int h4b_graph_create_persistent(const h4b_model* model, const h4b_state* state, void* stream,
+                                           void** graph_out) {
+    return h4b::capture_step(model, state, stream, graph_out, h4b::decode_persistent);
 }
 
 extern "C" int h4b_graph_launch(void* graph, void* stream) {

@@ -3,3 +3,4 @@
 #include "gemv.cu"
 #include "attention.cu"
 #include "decode.cu"
+#include "persistent.cu"

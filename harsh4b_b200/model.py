@@ -21,6 +21,8 @@ from ._lib import ModelDesc, StateDesc, check, device_status, lib, STATUS_WAIT_T
 from .cache import Checkpoint, read_cache
 
 KV_DTYPES = {"float32": (0, torch.float32), "float16": (1, torch.float16)}
+MODES = ("persistent", "chain")
+PERSISTENT_ATTN_CHUNK = 32  # tokens per attention split in the persistent step (persistent.cu)
 SWIGLU_BLOCK = 4  # rows per gate/up interleave block (matches the kernel)
 
 PROFILE_CATEGORIES = (
@@ -80,6 +82,7 @@ class CudaDecodeState:
         self.k_cache = torch.zeros(shape, dtype=kv_torch, device=dev)
         self.v_cache = torch.zeros(shape, dtype=kv_torch, device=dev)
         self.splits = int(attn_splits or model.attn_splits)
+        partial_splits = max(self.splits, model.max_persistent_splits)
         i32 = dict(dtype=torch.int32, device=dev)
         f32 = dict(dtype=torch.float32, device=dev)
         self.position_dev = torch.zeros(1, **i32)
@@ -92,11 +95,13 @@ class CudaDecodeState:
         self.logits = torch.zeros(model.vocab, **f32)
         self.absmax = torch.zeros(2 * model.n_layers, **f32)
         self.argmax_key = torch.zeros(1, dtype=torch.int64, device=dev)
-        self.partials = torch.zeros(model.kv_heads * self.splits * model.groups * (model.head_dim + 4), **f32)
+        self.partials = torch.zeros(model.kv_heads * partial_splits * model.groups * (model.head_dim + 4), **f32)
         self.counters = torch.zeros(model.kv_heads, **i32)
+        self.sync = torch.zeros(5 * model.n_layers + 2 + model.n_layers * model.kv_heads, **i32)
         self.desc = StateDesc(self.capacity, code, self.splits, *[t.data_ptr() for t in (
             self.k_cache, self.v_cache, self.position_dev, self.token_dev, self.next_token_dev, self.x, self.qkv,
-            self.attended, self.act, self.logits, self.absmax, self.argmax_key, self.partials, self.counters)])
+            self.attended, self.act, self.logits, self.absmax, self.argmax_key, self.partials, self.counters,
+            self.sync)])
         check(lib().h4b_validate(ctypes.byref(model.desc), ctypes.byref(self.desc)), "h4b_validate")
         self.stream = torch.cuda.Stream(device=dev)
         self._token_host = torch.zeros(1, dtype=torch.int32).pin_memory()
@@ -108,9 +113,11 @@ class CudaDecodeState:
     def _ensure_graph(self) -> None:
         if self._graph is None:
             handle = ctypes.c_void_p()
+            create = (lib().h4b_graph_create_persistent if self.model.mode == "persistent"
+                      else lib().h4b_graph_create)
             with torch.cuda.device(self.model.device):
-                check(lib().h4b_graph_create(ctypes.byref(self.model.desc), ctypes.byref(self.desc),
-                                             self.stream.cuda_stream, ctypes.byref(handle)), "h4b_graph_create")
+                check(create(ctypes.byref(self.model.desc), ctypes.byref(self.desc), self.stream.cuda_stream,
+                             ctypes.byref(handle)), "h4b_graph_create")
             self._graph = handle
 
     def close(self) -> None:
@@ -160,10 +167,13 @@ class CudaQwen:
     """Qwen3 decode on one B200 from the packed int4 cache layout."""
 
     def __init__(self, config, layers, embedding, embedding_scales, final_norm, *, kv_dtype: str = "float16",
-                 device=None, attn_splits: int = 16):
+                 device=None, attn_splits: int = 16, mode: str = "persistent"):
         if kv_dtype not in KV_DTYPES:
             raise ValueError(f"kv_dtype must be one of {sorted(KV_DTYPES)}")
+        if mode not in MODES:
+            raise ValueError(f"mode must be one of {MODES}")
         lib()  # raises without a usable device or library
+        self.mode = mode
         self.config = dict(config)
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.kv_dtype = kv_dtype
@@ -181,6 +191,11 @@ class CudaQwen:
         self.groups = self.heads // self.kv_heads
         self.q_size = self.heads * self.head_dim
         self.kv_size = self.kv_heads * self.head_dim
+        sms = ctypes.c_int(0)
+        with torch.cuda.device(self.device):
+            check(lib().h4b_device_info(ctypes.byref(sms), None, None), "h4b_device_info")
+        self.sm_count = sms.value
+        self.max_persistent_splits = max(1, min(64, self.sm_count // self.kv_heads))
         layers = [_as_layer_tuple(layer) for layer in layers]
         if len(layers) != self.n_layers:
             raise ValueError("layer count does not match the config")
@@ -247,6 +262,17 @@ class CudaQwen:
 
     def new_state(self, capacity: int, attn_splits: int | None = None) -> CudaDecodeState:
         return CudaDecodeState(self, capacity, attn_splits)
+
+    def attention_split_rule(self, state: CudaDecodeState | None = None):
+        """How many context splits the attention of a token with context `ctx`
+        uses: fixed per state in the kernel chain, chosen per token in the
+        persistent step. Returns a function ctx -> splits (the CPU oracle takes
+        it to repeat the device's summation order)."""
+        if self.mode == "chain":
+            fixed = state.splits if state is not None else self.attn_splits
+            return lambda ctx: fixed
+        cap = self.max_persistent_splits
+        return lambda ctx: max(1, min(cap, -(-ctx // PERSISTENT_ATTN_CHUNK)))
 
     def _check(self, token_id: int, state: CudaDecodeState) -> None:
         if state.model is not self:

@@ -138,7 +138,8 @@ typedef struct h4b_model {
  * position, writes next_token (greedy) and advances position by one.
  * Scratch: x[H], qkv[q+2kv], attended[q], act[I], logits[V]; absmax[2L]
  * floats and argmax_key[1] are rewritten every step; attn_partials holds
- * kv_heads * attn_splits * groups * (head_dim + 4) floats; attn_counters
+ * kv_heads * max(attn_splits, persistent splits) * groups * (head_dim + 4)
+ * floats (the persistent step uses up to 148 / kv_heads splits); attn_counters
  * holds kv_heads ints and must be zero when the session is created. */
 typedef struct h4b_state {
     int capacity, kv_dtype, attn_splits;
@@ -149,6 +150,9 @@ typedef struct h4b_state {
     unsigned long long *argmax_key;
     float *attn_partials;
     int *attn_counters;
+    /* Persistent decode only: (5 * layers + 2) + layers * kv_heads uint32
+     * phase counters, zeroed by the step itself before each token. */
+    uint32_t *sync;
 } h4b_state;
 
 /* Checks the shapes/pointers of a model + state pair against what the
@@ -168,9 +172,21 @@ int h4b_decode_step(const h4b_model *model, const h4b_state *state, void *stream
  * argmax, 7 finalize (next_token, position += 1). */
 int h4b_decode_stage(const h4b_model *model, const h4b_state *state, int stage, int layer, void *stream);
 
+/* The same token as ONE cooperative kernel, one CTA per SM (preceded by a
+ * memset of state->sync, absmax and argmax_key). A producer warp per SM
+ * streams that SM's rows of every weight matrix for the whole token through
+ * a shared-memory ring with bulk copies, never waiting on activations;
+ * consumer warps wait on release/acquire phase counters between the 5 phases
+ * of each layer (bounded waits: a timeout sets status bit 1 and every CTA
+ * stops). Needs state->sync. Capturable in a CUDA graph. */
+int h4b_decode_persistent(const h4b_model *model, const h4b_state *state, void *stream);
+
 /* Captures h4b_decode_step into a CUDA graph bound to (model, state) and
  * instantiates it; *graph_out is an opaque handle. */
 int h4b_graph_create(const h4b_model *model, const h4b_state *state, void *stream, void **graph_out);
+/* Same, capturing h4b_decode_persistent. */
+int h4b_graph_create_persistent(const h4b_model *model, const h4b_state *state, void *stream,
+                                void **graph_out);
 int h4b_graph_launch(void *graph, void *stream);
 int h4b_graph_destroy(void *graph);
 

@@ -9,8 +9,9 @@ mirrors the device cache's precision; the default fp32 is the reference's
 own cache (cpu_lightspark.py:290).
 
 RMSNorm, qk-norm, attention and SiLU run in the device kernels' reduction
-order with the shared exp (see litespark_oracle.c); ``attn_splits`` must
-equal the device state's split count for bit-exact comparisons.
+order with the shared exp (see litespark_oracle.c); ``attn_splits`` (an int,
+or a function of the context length) must follow the device's split choice
+for bit-exact comparisons.
 """
 from __future__ import annotations
 
@@ -148,8 +149,10 @@ class OracleQwen:
 
     # cpu_lightspark.py:389-422: softmax(q.k / sqrt(d)) v over t <= position.
     def attention(self, state: OracleState, layer_index: int, q: np.ndarray) -> None:
+        context = state.position + 1
+        splits = self.attn_splits(context) if callable(self.attn_splits) else self.attn_splits
         gqa_splitk(np.ascontiguousarray(q), state.keys[layer_index], state.values[layer_index], state.attended,
-                   state.position + 1, self.kv_heads, self.groups, self.attn_splits)
+                   context, self.kv_heads, self.groups, int(splits))
 
     def _store(self, values: np.ndarray) -> np.ndarray:
         if self.kv_dtype == np.float32:

@@ -30,6 +30,15 @@ def oracle_decode(model, prompt, steps, teacher=None):
     return np.stack(logits), greedy
 
 
+def oracle_for(checkpoint, cuda_model, kv_dtype=None, attn_splits=None):
+    """The oracle that repeats `cuda_model`'s KV precision and attention split choice."""
+    kv = kv_dtype if kv_dtype is not None else (np.float16 if cuda_model.kv_dtype == "float16" else np.float32)
+    rule = cuda_model.attention_split_rule()
+    if cuda_model.mode == "chain" and attn_splits is not None:
+        rule = attn_splits
+    return oracle_model(checkpoint, kv_dtype=kv, attn_splits=rule)
+
+
 def cuda_decode(model, prompt, steps, teacher=None, attn_splits=None):
     state = model.new_state(len(prompt) + steps, attn_splits=attn_splits)
     logits = [model.forward_token(int(t), state).cpu().numpy().copy() for t in prompt]

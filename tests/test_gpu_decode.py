@@ -22,7 +22,7 @@ import pytest
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-from _models import cuda_decode, oracle_decode, oracle_model, top2_margin  # noqa: E402
+from _models import cuda_decode, oracle_decode, oracle_for, oracle_model, top2_margin  # noqa: E402
 from harsh4b_b200.model import CudaQwen  # noqa: E402
 from harsh4b_b200.synthetic import qwen3_4b_config, synthetic_checkpoint, synthetic_prompt, tiny_config  # noqa: E402
 
@@ -37,10 +37,11 @@ def tiny():
     return checkpoint, synthetic_prompt(checkpoint.config, 16, seed=11)
 
 
-def test_tiny_fp32_kv_bit_exact_with_oracle(tiny):
+@pytest.mark.parametrize("mode", ["persistent", "chain"])
+def test_tiny_fp32_kv_bit_exact_with_oracle(tiny, mode):
     checkpoint, prompt = tiny
-    want, greedy = oracle_decode(oracle_model(checkpoint), prompt, 24)
-    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float32")
+    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float32", mode=mode)
+    want, greedy = oracle_decode(oracle_for(checkpoint, model), prompt, 24)
     got, got_greedy = cuda_decode(model, prompt, 24)
     assert got_greedy == greedy
     np.testing.assert_array_equal(got, want)
@@ -48,11 +49,23 @@ def test_tiny_fp32_kv_bit_exact_with_oracle(tiny):
 
 
 @pytest.mark.parametrize("splits", [1, 3, 16])
-def test_tiny_fp16_kv_bit_exact_with_oracle(tiny, splits):
+def test_tiny_fp16_kv_chain_bit_exact_with_oracle(tiny, splits):
     checkpoint, prompt = tiny
-    want, greedy = oracle_decode(oracle_model(checkpoint, kv_dtype=np.float16, attn_splits=splits), prompt, 24)
-    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float16")
+    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float16", mode="chain")
+    want, greedy = oracle_decode(oracle_for(checkpoint, model, attn_splits=splits), prompt, 24)
     got, got_greedy = cuda_decode(model, prompt, 24, attn_splits=splits)
+    assert got_greedy == greedy
+    np.testing.assert_array_equal(got, want)
+
+
+def test_tiny_fp16_kv_persistent_long_context_bit_exact(tiny):
+    """Enough tokens for the persistent step to use several attention splits."""
+    checkpoint, prompt = tiny
+    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float16")
+    long_prompt = (prompt * 12)[:150]
+    want, greedy = oracle_decode(oracle_for(checkpoint, model), long_prompt, 16)
+    got, got_greedy = cuda_decode(model, long_prompt, 16)
+    assert model.attention_split_rule()(166) > 1
     assert got_greedy == greedy
     np.testing.assert_array_equal(got, want)
 
@@ -124,8 +137,8 @@ def test_config0_64_greedy_tokens_match_reference_path(full):
     """128 random prompt ids, 64 greedy tokens, batch 1,
     with the reference's fp32 KV cache: bit-exact logits, same greedy tokens."""
     checkpoint, prompt = full
-    want, greedy = oracle_decode(oracle_model(checkpoint), prompt, 64)
     model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float32")
+    want, greedy = oracle_decode(oracle_for(checkpoint, model), prompt, 64)
     got, got_greedy = cuda_decode(model, prompt, 64)
     assert got_greedy == greedy
     assert np.abs(got - want).max() <= LOGIT_TOL
@@ -133,19 +146,23 @@ def test_config0_64_greedy_tokens_match_reference_path(full):
     assert model.status() == 0
 
 
-def test_config0_fp16_kv_bit_exact_and_drift_report(full):
+@pytest.mark.parametrize("mode", ["persistent", "chain"])
+def test_config0_fp16_kv_bit_exact_and_drift_report(full, mode):
     """The production fp16 KV cache: bit-exact with the oracle at the same
     precision; its drift from the fp32-cache path is reported next to the
     same drift between two CPU oracles (it is a property of the precision,
     not of the kernels)."""
     checkpoint, prompt = full
-    want16, greedy16 = oracle_decode(oracle_model(checkpoint, kv_dtype=np.float16), prompt, 64)
-    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float16")
+    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float16", mode=mode)
+    want16, greedy16 = oracle_decode(oracle_for(checkpoint, model), prompt, 64)
     got, got_greedy = cuda_decode(model, prompt, 64)
     assert got_greedy == greedy16
     np.testing.assert_array_equal(got, want16)
-    want32, greedy32 = oracle_decode(oracle_model(checkpoint), prompt, 64, teacher=greedy16)
-    report = {"fp16_vs_fp32_kv_max_abs_logit_diff": float(np.abs(got - want32).max()),
-              "greedy_agreement_fp16_vs_fp32_kv": float(np.mean(np.array(greedy16) == np.array(greedy32))),
-              "min_top2_margin_fp32": float(top2_margin(want32[len(prompt) - 1:]).min())}
-    print(json.dumps(report))
+    assert model.status() == 0
+    if mode == "persistent":
+        want32, greedy32 = oracle_decode(oracle_for(checkpoint, model, kv_dtype=np.float32), prompt, 64,
+                                         teacher=greedy16)
+        report = {"fp16_vs_fp32_kv_max_abs_logit_diff": float(np.abs(got - want32).max()),
+                  "greedy_agreement_fp16_vs_fp32_kv": float(np.mean(np.array(greedy16) == np.array(greedy32))),
+                  "min_top2_margin_fp32": float(top2_margin(want32[len(prompt) - 1:]).min())}
+        print(json.dumps(report))
