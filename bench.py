@@ -395,7 +395,9 @@ def run_gemv(args) -> int:
         ops.int4_gemv_fused_quant(xt, ws[0], ss[0], out=out, acc=acc)
         q = np.empty(width, dtype=np.int8)
         _, want_acc = oracle.int4_gemv(q, packed, scales, oracle.quantize_activation(x, q))
-        exact = bool(np.array_equal(acc.cpu().numpy(), want_acc))
+        got_acc = acc.cpu().numpy()
+        exact = bool(np.array_equal(got_acc, want_acc))
+        mismatch = np.nonzero(got_acc != want_acc)[0]
         for i in range(min(3, args.iters)):
             ops.int4_gemv_fused_quant(xt, ws[i % copies], ss[i % copies], out=out)
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -408,8 +410,14 @@ def run_gemv(args) -> int:
         torch.cuda.synchronize()
         us = start.elapsed_time(end) * 1000.0 / args.iters
         gbs = bytes_per_launch / us / 1e3
+        from harsh4b_b200._lib import device_status
         results[name] = {"rows": rows, "width": width, "us": round(us, 3), "gbs": round(gbs, 1),
-                         "frac": round(gbs / peaks["hbm_gbs"], 4), "int32_bit_exact": exact}
+                         "frac": round(gbs / peaks["hbm_gbs"], 4), "int32_bit_exact": exact,
+                         "device_status": device_status()}
+        if not exact:
+            results[name]["mismatched_rows"] = int(mismatch.size)
+            results[name]["first_mismatches"] = mismatch[:6].tolist()
+            results[name]["diffs"] = (got_acc[mismatch[:6]].astype(np.int64) - want_acc[mismatch[:6]]).tolist()
         del ws, ss
     line = {"metric": "body GEMV HBM GB/s (fused int8 quantisation + int4 GEMV), batch 1",
             "unit": "GB/s", "peak": peaks["hbm_gbs"], "peak_source": peaks["source"], "iters": args.iters,

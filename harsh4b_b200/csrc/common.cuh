@@ -77,12 +77,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
+// try_wait that may park the thread for up to `hint_ns` inside the
+// instruction; it returns as soon as the phase completes.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(done) : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns) : "memory");
+    return done != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete. Returns
-// false (and reports) when the time limit passes.
+// false (and reports) when the time limit passes. The waiting thread parks
+// inside try_wait rather than spinning, so idle waiters take no issue slots
+// from the warps doing work; the clock is read only between parkings.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t start = globaltimer_ns();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_hint(bar, parity, 20000)) {
         if (globaltimer_ns() - start > limit_ns) {
             report(kStatusWaitTimeout);
             return false;

@@ -64,6 +64,11 @@ struct GemvArgs {
     unsigned long long* argmax_out;
 };
 
+// Bytes reserved for the quantised activation: rounded up to whole slots
+// (32 lanes x 32 B) plus 3 slots, the most an instantiated slot count
+// exceeds the needed one.
+__host__ __device__ inline int xq_region(int width) { return ((width + 1023) & ~1023) + 3072; }
+
 struct SmemLayout {
     int red, xq, gamma, acc, scale, ring, total;
 };
@@ -73,29 +78,81 @@ __host__ __device__ inline SmemLayout smem_layout(int width, int rows_cap, int s
     SmemLayout s;
     s.red = 2 * kMaxStages * 8;               // barriers first
     s.xq = s.red + 64 * 4;                    // 32 floats + flags
-    s.gamma = s.xq + ((width + 127) & ~127);  // RMSNorm weight (PRO_RMSNORM only)
+    s.gamma = s.xq + xq_region(width);
     s.acc = s.gamma + (with_gamma ? width * 4 : 0);
     s.scale = s.acc + rows_cap * 4;
     s.ring = (s.scale + rows_cap * 4 + 127) & ~127;
-    s.total = s.ring + stages * stage_bytes;
+    s.total = s.ring + stages * stage_bytes + 512;  // slot loads may run up to 496 B past a tile
     return s;
 }
 
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 // One 16-byte weight chunk (32 codes) against the lane's 32 activation
-// bytes. Word j of the chunk pairs with the activation words (even, odd) of
-// column group j and feeds accumulator j, so the four dp4a chains are
-// independent.
-__device__ __forceinline__ void dot_chunk(const uint4 w, const uint4 xa, const uint4 xb, int acc[4]) {
+// bytes. Word j pairs with the activation words (even, odd) of column group
+// j. A nibble n is read as u = n ^ 8 = s + 8: the low nibbles of a word
+// masked in place are 4 unsigned bytes u, the high nibbles masked in place
+// are 4 unsigned bytes 16u, so each word costs two LOP3 and two u8 x s8
+// dp4a, and the high sum is an exact multiple of 16 (see row_total).
+__device__ __forceinline__ void dot_chunk(const uint4 w, const uint4 xa, const uint4 xb, int lo[4], int hi[4]) {
     const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
     const uint32_t xe[4] = {xa.x, xa.z, xb.x, xb.z};
     const uint32_t xo[4] = {xa.y, xa.w, xb.y, xb.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const uint32_t lo = (ww[j] & 0x0F0F0F0Fu) ^ 0x08080808u;
-        const uint32_t hi = ((ww[j] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
-        acc[j] = __dp4a(static_cast<int>(lo), static_cast<int>(xe[j]), acc[j]);
-        acc[j] = __dp4a(static_cast<int>(hi), static_cast<int>(xo[j]), acc[j]);
+        const uint32_t u = ww[j] ^ 0x88888888u;
+        lo[j] = dp4a_us(u & 0x0F0F0F0Fu, xe[j], lo[j]);
+        hi[j] = dp4a_us(u & 0xF0F0F0F0u, xo[j], hi[j]);
     }
+}
+
+// A lane's share of one row: sum u*x over its codes minus 8 * sum(x) (bias).
+__device__ __forceinline__ int row_total(const int lo[4], const int hi[4], int bias) {
+    return bias + ((lo[0] + lo[1]) + (lo[2] + lo[3])) + (((hi[0] + hi[1]) + (hi[2] + hi[3])) >> 4);
+}
+
+// Row sums for rows b0 .. b0+RB-1 of a tile (a short batch repeats its last
+// row). Loads are unconditional: lanes past the row end read padding or the
+// next row and multiply it by zero activations.
+template <int SLOTS, int RB, bool XREG>
+__device__ __forceinline__ void tile_batch(const uint8_t* tile, int kb, int trows, int b0, const uint4* xa,
+                                           const uint4* xb, const int8_t* xq, int lane, int bias, int total[RB]) {
+    int lo[RB][4], hi[RB][4];
+#pragma unroll
+    for (int i = 0; i < RB; ++i)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) lo[i][q] = hi[i][q] = 0;
+#pragma unroll
+    for (int j = 0; j < SLOTS; ++j) {
+        const int c = lane + 32 * j;
+        uint4 va, vb;
+        if constexpr (XREG) {
+            va = xa[j];
+            vb = xb[j];
+        } else {
+            va = *reinterpret_cast<const uint4*>(xq + 32 * c);
+            vb = *reinterpret_cast<const uint4*>(xq + 32 * c + 16);
+        }
+#pragma unroll
+        for (int i = 0; i < RB; ++i) {
+            const int lr = min(b0 + i, trows - 1);
+            const uint4 w = *reinterpret_cast<const uint4*>(tile + static_cast<size_t>(lr) * kb + 16 * c);
+            dot_chunk(w, va, vb, lo[i], hi[i]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < RB; ++i) total[i] = __reduce_add_sync(0xffffffffu, row_total(lo[i], hi[i], bias));
+}
+
+// Zero xq past the activation to the end of its region, so the unconditional
+// slot loads of the shared-memory activation path read zeros.
+__device__ __forceinline__ void zero_xq_tail(int8_t* xq, int n, int tid, int nthreads) {
+    const int end = xq_region(n);
+    for (int i = n + 4 * tid; i < end; i += 4 * nthreads) *reinterpret_cast<uint32_t*>(xq + i) = 0u;
 }
 
 // Writes the 8 quantised values of group g (columns 8g..8g+7) as
@@ -130,6 +187,7 @@ __device__ float gemv_prologue(const GemvArgs& a, int8_t* xq, float* red, const 
             }
             store_group(xq, g, q);
         }
+        zero_xq_tail(xq, a.width, tid, kConsumers);
         return a.act_scale;
     } else {
         float inv = 1.0f;
@@ -176,6 +234,7 @@ __device__ float gemv_prologue(const GemvArgs& a, int8_t* xq, float* red, const 
             }
             store_group(xq, g, q);
         }
+        zero_xq_tail(xq, a.width, tid, kConsumers);
         return dequant_scale(m);
     }
 }
@@ -266,7 +325,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
         const int chunks = a.width >> 5;
         constexpr bool kXReg = SLOTS <= kMaxRegSlots;
         constexpr int kXSlots = kXReg ? SLOTS : 1;
-        constexpr int RB = SLOTS <= 3 ? 4 : (SLOTS <= 4 ? 3 : 2);  // rows per batch
+        constexpr int RB = 2;  // rows per batch
         uint4 xa[kXSlots], xb[kXSlots];
         int bias = 0;
 #pragma unroll
@@ -298,38 +357,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
             const uint8_t* tile = ring + static_cast<size_t>(s) * stage_bytes;
             const int trows = min(a.tile_rows, nrows - t * a.tile_rows);
             for (int b0 = 0; b0 < trows; b0 += RB) {
-                int acc[RB][4];
-#pragma unroll
-                for (int i = 0; i < RB; ++i) {
-                    acc[i][0] = bias;
-                    acc[i][1] = acc[i][2] = acc[i][3] = 0;
-                }
-#pragma unroll
-                for (int j = 0; j < SLOTS; ++j) {
-                    const int c = lane + 32 * j;
-                    if (c < chunks) {
-                        uint4 w[RB];
-#pragma unroll
-                        for (int i = 0; i < RB; ++i) {
-                            const int lr = min(b0 + i, trows - 1);  // a short batch repeats its last row
-                            w[i] = *reinterpret_cast<const uint4*>(tile + static_cast<size_t>(lr) * kb + 16 * c);
-                        }
-                        uint4 va, vb;
-                        if constexpr (kXReg) {
-                            va = xa[j];
-                            vb = xb[j];
-                        } else {
-                            va = *reinterpret_cast<const uint4*>(xq + 32 * c);
-                            vb = *reinterpret_cast<const uint4*>(xq + 32 * c + 16);
-                        }
-#pragma unroll
-                        for (int i = 0; i < RB; ++i) dot_chunk(w[i], va, vb, acc[i]);
-                    }
-                }
                 int total[RB];
-#pragma unroll
-                for (int i = 0; i < RB; ++i)
-                    total[i] = __reduce_add_sync(0xffffffffu, (acc[i][0] + acc[i][1]) + (acc[i][2] + acc[i][3]));
+                tile_batch<SLOTS, RB, kXReg>(tile, kb, trows, b0, xa, xb, xq, lane, bias, total);
                 if (lane == 0) {
 #pragma unroll
                     for (int i = 0; i < RB; ++i)
@@ -441,9 +470,16 @@ int plan_gemv(int rows, int width, int row_align, GemvPlan* p) {
     // Enough tiles per CTA for every consumer warp, at most 8 rows / 16 KB each.
     int tile_rows = max(1, min(8, (per_cta + kConsumerWarps - 1) / kConsumerWarps));
     tile_rows = max(1, min(tile_rows, kStageTarget / kb));
+    // The ring depth is a multiple of the consumer warps: tile t sits in slot
+    // t % stages and belongs to warp t % 8, so every slot has one owner that
+    // waits on the slot's phases in order. (With a shared slot a warp could
+    // start waiting for a tile while the slot's previous tile, owned by
+    // another warp, is still in flight -- and the mbarrier parity of that
+    // older phase would read as complete.)
+    tile_rows = max(1, min(tile_rows, kRingBytes / (kConsumerWarps * kb)));
     const int stage_bytes = tile_rows * kb;
-    if (stage_bytes > 64 * 1024) return H4B_EUNSUPPORTED;
-    const int stages = max(2, min(kMaxStages, kRingBytes / stage_bytes));
+    if (stage_bytes > 64 * 1024 || kConsumerWarps * stage_bytes > kRingBytes) return H4B_EUNSUPPORTED;
+    const int stages = min(kMaxStages, kRingBytes / stage_bytes) / kConsumerWarps * kConsumerWarps;
     const int rows_cap = (per_cta + 31) & ~31;
     const SmemLayout L = smem_layout(width, rows_cap, stages, stage_bytes, true);
     if (L.total > 227 * 1024) return H4B_EUNSUPPORTED;

@@ -26,8 +26,9 @@ namespace h4b {
 constexpr int kMkWarps = 8;  // consumer warps
 constexpr int kMkConsumers = kMkWarps * 32;
 constexpr int kMkThreads = kMkConsumers + 32;
-constexpr int kMkSlotBytes = 8192;
-constexpr int kMkMaxStages = 32;
+constexpr int kMkMaxSlotBytes = 16384;
+constexpr int kMkStages = 16;  // a multiple of kMkWarps: each ring slot has one owning warp
+constexpr int kMkMaxStages = kMkStages;
 constexpr int kMkMaxHidden = 8192;  // RMSNorm inputs kept in registers (4 groups of 8 per thread)
 constexpr int kMkMaxWidth = 16384;
 
@@ -39,6 +40,7 @@ struct MkArgs {
     uint32_t* ready;       // [5 * layers + 2] phase counters
     uint32_t* attn_count;  // [layers][kv_heads] split-merge counters
     int stages;
+    int slot_bytes;        // ring slot size (a tile is at most one slot)
     int attn_chunk;        // target tokens per attention split
     int max_splits;        // splits per kv head at most
     int xq_bytes, rows_cap;
@@ -97,7 +99,7 @@ __device__ __forceinline__ Seg mk_segment(const MkArgs& a, int g, int cta, int n
     const int u1 = static_cast<int>(static_cast<long long>(cta + 1) * units / nctas);
     s.r0 = u0 * align;
     s.nrows = (u1 - u0) * align;
-    s.tile_rows = max(1, min((s.nrows + kMkWarps - 1) / kMkWarps, kMkSlotBytes / s.kb));
+    s.tile_rows = max(1, min((s.nrows + kMkWarps - 1) / kMkWarps, a.slot_bytes / s.kb));
     s.ntiles = (s.nrows + s.tile_rows - 1) / s.tile_rows;
     return s;
 }
@@ -128,7 +130,9 @@ __device__ bool mk_wait(const uint32_t* counter, uint32_t target, int* flags) {
     bool failed = false;
     if (threadIdx.x == 0 && ld_acquire_u32(counter) < target) {
         const uint64_t start = globaltimer_ns();
-        while (ld_acquire_u32(counter) < target) {
+        for (uint32_t spin = 1; ld_acquire_u32(counter) < target; ++spin) {
+            __nanosleep(32);  // keep the poll off the issue slots of the working warps
+            if ((spin & 63) != 0) continue;
             if (wait_failed_before() || *reinterpret_cast<volatile int*>(&flags[0])) {
                 failed = true;
                 break;
@@ -205,6 +209,7 @@ __device__ float mk_prologue_rms(const float* x, bool from_smem, const float* ga
             store_group(xq, g, q);
         }
     }
+    zero_xq_tail(xq, n, tid, kMkConsumers);
     named_sync(1, kMkConsumers);
     return dequant_scale(m);
 }
@@ -221,13 +226,14 @@ __device__ float mk_prologue_quant(const float* v, const float* absmax_slot, int
         for (int e = 0; e < 8; ++e) q[e] = quantize_one(x[e], qs);
         store_group(xq, g, q);
     }
+    zero_xq_tail(xq, n, threadIdx.x, kMkConsumers);
     named_sync(1, kMkConsumers);
     return dequant_scale(m);
 }
 
 // This CTA's tiles of one GEMV segment: int32 row sums into acc_s.
 template <int SLOTS, int RB>
-__device__ void mk_tiles(const Seg& sg, uint32_t seq0, int stages, const uint8_t* ring, uint64_t* full,
+__device__ void mk_tiles(const Seg& sg, uint32_t seq0, int stages, int slot_bytes, const uint8_t* ring, uint64_t* full,
                          uint64_t* empty, const int8_t* xq, int32_t* acc_s, int* flags) {
     constexpr bool kXReg = SLOTS <= kMaxRegSlots;
     constexpr int kXSlots = kXReg ? SLOTS : 1;
@@ -262,41 +268,11 @@ __device__ void mk_tiles(const Seg& sg, uint32_t seq0, int stages, const uint8_t
             atomicOr(&flags[0], 1);
             break;
         }
-        const uint8_t* tile = ring + static_cast<size_t>(slot) * kMkSlotBytes;
+        const uint8_t* tile = ring + static_cast<size_t>(slot) * slot_bytes;
         const int trows = min(sg.tile_rows, sg.nrows - t * sg.tile_rows);
         for (int b0 = 0; b0 < trows; b0 += RB) {
-            int acc[RB][4];
-#pragma unroll
-            for (int i = 0; i < RB; ++i) {
-                acc[i][0] = bias;
-                acc[i][1] = acc[i][2] = acc[i][3] = 0;
-            }
-#pragma unroll
-            for (int j = 0; j < SLOTS; ++j) {
-                const int c = lane + 32 * j;
-                if (c < chunks) {
-                    uint4 w[RB];
-#pragma unroll
-                    for (int i = 0; i < RB; ++i) {
-                        const int lr = min(b0 + i, trows - 1);
-                        w[i] = *reinterpret_cast<const uint4*>(tile + static_cast<size_t>(lr) * sg.kb + 16 * c);
-                    }
-                    uint4 va, vb;
-                    if constexpr (kXReg) {
-                        va = xa[j];
-                        vb = xb[j];
-                    } else {
-                        va = *reinterpret_cast<const uint4*>(xq + 32 * c);
-                        vb = *reinterpret_cast<const uint4*>(xq + 32 * c + 16);
-                    }
-#pragma unroll
-                    for (int i = 0; i < RB; ++i) dot_chunk(w[i], va, vb, acc[i]);
-                }
-            }
             int total[RB];
-#pragma unroll
-            for (int i = 0; i < RB; ++i)
-                total[i] = __reduce_add_sync(0xffffffffu, (acc[i][0] + acc[i][1]) + (acc[i][2] + acc[i][3]));
+            tile_batch<SLOTS, RB, kXReg>(tile, sg.kb, trows, b0, xa, xb, xq, lane, bias, total);
             if (lane == 0) {
 #pragma unroll
                 for (int i = 0; i < RB; ++i)
@@ -309,18 +285,18 @@ __device__ void mk_tiles(const Seg& sg, uint32_t seq0, int stages, const uint8_t
     named_sync(1, kMkConsumers);  // acc_s complete
 }
 
-__device__ void mk_run_tiles(const Seg& sg, uint32_t seq0, int stages, const uint8_t* ring, uint64_t* full,
+__device__ void mk_run_tiles(const Seg& sg, uint32_t seq0, int stages, int slot_bytes, const uint8_t* ring, uint64_t* full,
                              uint64_t* empty, const int8_t* xq, int32_t* acc_s, int* flags) {
     const int need = ((sg.width >> 5) + 31) / 32;
-    if (need <= 1) mk_tiles<1, 4>(sg, seq0, stages, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 2) mk_tiles<2, 4>(sg, seq0, stages, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 3) mk_tiles<3, 4>(sg, seq0, stages, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 4) mk_tiles<4, 3>(sg, seq0, stages, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 6) mk_tiles<6, 2>(sg, seq0, stages, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 8) mk_tiles<8, 2>(sg, seq0, stages, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 10) mk_tiles<10, 2>(sg, seq0, stages, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 12) mk_tiles<12, 2>(sg, seq0, stages, ring, full, empty, xq, acc_s, flags);
-    else mk_tiles<16, 2>(sg, seq0, stages, ring, full, empty, xq, acc_s, flags);
+    if (need <= 1) mk_tiles<1, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
+    else if (need <= 2) mk_tiles<2, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
+    else if (need <= 3) mk_tiles<3, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
+    else if (need <= 4) mk_tiles<4, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
+    else if (need <= 6) mk_tiles<6, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
+    else if (need <= 8) mk_tiles<8, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
+    else if (need <= 10) mk_tiles<10, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
+    else if (need <= 12) mk_tiles<12, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
+    else mk_tiles<16, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
 }
 
 // Starts the 4-byte async copies of a segment's row scales into sc_s.
@@ -495,18 +471,19 @@ struct MkSmem {
     int bars, red, xq, gamma, acc, scale, att, ring, total;
 };
 
-__host__ __device__ inline MkSmem mk_smem_layout(int xq_bytes, int hidden, int rows_cap, int kv_bytes, int stages) {
+__host__ __device__ inline MkSmem mk_smem_layout(int xq_bytes, int hidden, int rows_cap, int kv_bytes, int stages,
+                                                 int slot_bytes) {
     MkSmem s;
     s.bars = 0;
     s.red = 2 * kMkMaxStages * 8;
     s.xq = s.red + 64 * 4;
-    s.gamma = s.xq + ((xq_bytes + 127) & ~127);
+    s.gamma = s.xq + xq_region(xq_bytes);
     s.acc = s.gamma + ((hidden * 4 + 127) & ~127);
     s.scale = s.acc + rows_cap * 4;
     s.att = (s.scale + rows_cap * 4 + 127) & ~127;
     const int att_bytes = 2 * kSubTile * kHeadDim * kv_bytes;
     s.ring = (s.att + (att_bytes > hidden * 4 ? att_bytes : hidden * 4) + 127) & ~127;
-    s.total = s.ring + stages * kMkSlotBytes;
+    s.total = s.ring + stages * slot_bytes + 512;  // slot loads may run up to 496 B past a tile
     return s;
 }
 
@@ -515,7 +492,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
     extern __shared__ __align__(128) uint8_t smem[];
     const h4b_model& m = a.m;
     const h4b_state& st = a.s;
-    const MkSmem L = mk_smem_layout(a.xq_bytes, m.hidden, a.rows_cap, sizeof(KV), a.stages);
+    const MkSmem L = mk_smem_layout(a.xq_bytes, m.hidden, a.rows_cap, sizeof(KV), a.stages, a.slot_bytes);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
     uint64_t* empty = full + kMkMaxStages;
     float* red = reinterpret_cast<float*>(smem + L.red);
@@ -572,7 +549,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
                     const int rows_t = min(sg.tile_rows, sg.nrows - t * sg.tile_rows);
                     const uint32_t bytes = static_cast<uint32_t>(rows_t) * sg.kb;
                     mbar_arrive_expect_tx(&full[slot], bytes);
-                    bulk_g2s(ring + static_cast<size_t>(slot) * kMkSlotBytes,
+                    bulk_g2s(ring + static_cast<size_t>(slot) * a.slot_bytes,
                              sg.w + static_cast<size_t>(sg.r0 + t * sg.tile_rows) * sg.kb, bytes, &full[slot]);
                 }
             }
@@ -621,7 +598,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         async_copy_wait_all();
         named_sync(1, kMkConsumers);
         float act = mk_prologue_rms(l == 0 ? xs : st.x, l == 0, gamma_s, H, eps, xq, red);
-        mk_run_tiles(sg, seq, a.stages, ring, full, empty, xq, acc_s, flags);
+        mk_run_tiles(sg, seq, a.stages, a.slot_bytes, ring, full, empty, xq, acc_s, flags);
         seq += sg.ntiles;
         if (mk_stop(flags)) return;
         for (int i = tid; i < sg.nrows; i += kMkConsumers) __stcg(st.qkv + sg.r0 + i, mk_value(acc_s, sc_s, i, act));
@@ -637,7 +614,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         if (!mk_wait(&a.ready[ph_attn(l)], kv_heads, flags)) return;
         async_copy_wait_all();
         act = mk_prologue_quant(st.attended, st.absmax + 2 * l, m.heads * m.head_dim, xq);
-        mk_run_tiles(sg, seq, a.stages, ring, full, empty, xq, acc_s, flags);
+        mk_run_tiles(sg, seq, a.stages, a.slot_bytes, ring, full, empty, xq, acc_s, flags);
         seq += sg.ntiles;
         if (mk_stop(flags)) return;
         for (int i = tid; i < sg.nrows; i += kMkConsumers)
@@ -652,7 +629,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         async_copy_wait_all();
         named_sync(1, kMkConsumers);
         act = mk_prologue_rms(st.x, false, gamma_s, H, eps, xq, red);
-        mk_run_tiles(sg, seq, a.stages, ring, full, empty, xq, acc_s, flags);
+        mk_run_tiles(sg, seq, a.stages, a.slot_bytes, ring, full, empty, xq, acc_s, flags);
         seq += sg.ntiles;
         if (mk_stop(flags)) return;
         {
@@ -676,7 +653,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         if (!mk_wait(&a.ready[ph_gate_up(l)], nctas, flags)) return;
         async_copy_wait_all();
         act = mk_prologue_quant(st.act, st.absmax + 2 * l + 1, m.intermediate, xq);
-        mk_run_tiles(sg, seq, a.stages, ring, full, empty, xq, acc_s, flags);
+        mk_run_tiles(sg, seq, a.stages, a.slot_bytes, ring, full, empty, xq, acc_s, flags);
         seq += sg.ntiles;
         if (mk_stop(flags)) return;
         for (int i = tid; i < sg.nrows; i += kMkConsumers)
@@ -692,7 +669,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
     async_copy_wait_all();
     named_sync(1, kMkConsumers);
     const float act = mk_prologue_rms(st.x, false, gamma_s, H, eps, xq, red);
-    mk_run_tiles(sg, seq, a.stages, ring, full, empty, xq, acc_s, flags);
+    mk_run_tiles(sg, seq, a.stages, a.slot_bytes, ring, full, empty, xq, acc_s, flags);
     if (mk_stop(flags)) return;
     unsigned long long best = 0ull;
     for (int i = tid; i < sg.nrows; i += kMkConsumers) {
@@ -744,7 +721,7 @@ static int plan_persistent(const h4b_model* m, const h4b_state* s, MkPlan* p) {
     if (m->hidden > kMkMaxHidden) return H4B_EUNSUPPORTED;
     const int q_size = m->heads * m->head_dim;
     const int max_width = std::max(m->hidden, std::max(q_size, m->intermediate));
-    if (max_width > kMkMaxWidth || max_width / 2 > kMkSlotBytes) return H4B_EUNSUPPORTED;
+    if (max_width > kMkMaxWidth) return H4B_EUNSUPPORTED;
     MkArgs& a = p->args;
     a = MkArgs{};
     a.m = *m;
@@ -759,11 +736,12 @@ static int plan_persistent(const h4b_model* m, const h4b_state* s, MkPlan* p) {
     const int biggest = std::max({m->vocab, 2 * m->intermediate, q_size + 2 * m->kv_heads * m->head_dim, m->hidden});
     a.rows_cap = ((biggest + nctas - 1) / nctas + 2 * kSwigluBlock + 31) & ~31;
     const int kv_bytes = s->kv_dtype == 0 ? 4 : 2;
-    const MkSmem base = mk_smem_layout(a.xq_bytes, m->hidden, a.rows_cap, kv_bytes, 0);
+    const MkSmem base = mk_smem_layout(a.xq_bytes, m->hidden, a.rows_cap, kv_bytes, 0, 0);
     const int budget = 227 * 1024 - base.total;
-    a.stages = std::min(kMkMaxStages, budget / kMkSlotBytes);
-    if (a.stages < 4) return H4B_EUNSUPPORTED;
-    p->smem = mk_smem_layout(a.xq_bytes, m->hidden, a.rows_cap, kv_bytes, a.stages).total;
+    a.stages = kMkStages;
+    a.slot_bytes = std::min(kMkMaxSlotBytes, budget / kMkStages / 1024 * 1024);
+    if (a.slot_bytes < max_width / 2) return H4B_EUNSUPPORTED;  // one row must fit a slot
+    p->smem = mk_smem_layout(a.xq_bytes, m->hidden, a.rows_cap, kv_bytes, a.stages, a.slot_bytes).total;
     return 0;
 }
 

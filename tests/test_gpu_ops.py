@@ -148,3 +148,20 @@ def test_embedding_and_argmax_exact():
     logits[[5, 70000]] = logits.max() + 1  # a tie: the first index wins
     assert ops.argmax(cuda(logits)).item() == 5
     assert ops.argmax(cuda(np.array([-1.0, 3.0, 2.0], dtype=np.float32))).item() == 1
+
+
+def test_long_gemv_repeated_launches_exact():
+    """A long GEMV wraps the shared-memory ring ~16 times per CTA; repeated
+    launches catch ordering races between the ring's producer and its
+    consumer warps (each launch must stay bit-exact)."""
+    rows, width = 151936, 2560
+    rng = np.random.default_rng([6, rows, width])
+    packed, scales = int4_matrix(rng, rows, width), row_scales(rng, rows)
+    w, s = cuda(packed), cuda(scales)
+    for trial in range(12):
+        x = outlier_activation(width, seed=100 + trial)
+        q = np.empty(width, dtype=np.int8)
+        _, want = oracle.int4_gemv(q, packed, scales, oracle.quantize_activation(x, q))
+        acc = torch.empty(rows, dtype=torch.int32, device="cuda")
+        ops.int4_gemv_fused_quant(cuda(x), w, s, acc=acc)
+        np.testing.assert_array_equal(acc.cpu().numpy(), want)
