@@ -37,7 +37,7 @@ class StateDesc(ctypes.Structure):
 
     _fields_ = [("capacity", _i32), ("kv_dtype", _i32), ("attn_splits", _i32)] + [
         (n, _vp) for n in ("k_cache", "v_cache", "position", "token", "next_token", "x", "qkv", "attended",
-                           "act", "logits", "absmax", "argmax_key", "attn_partials", "attn_counters", "sync")]
+                           "act", "logits", "absmax", "argmax_key", "attn_partials", "attn_counters", "exchange")]
 
 
 _SIGNATURES = {
@@ -62,7 +62,9 @@ _SIGNATURES = {
                                     ctypes.POINTER(_vp)],
     "h4b_graph_launch": [_vp, _vp],
     "h4b_graph_destroy": [_vp],
+    "h4b_persistent_exchange_words": [ctypes.POINTER(ModelDesc)],
 }
+_RESTYPES = {"h4b_persistent_exchange_words": ctypes.c_longlong}
 
 
 def exported_symbols() -> list[str]:
@@ -80,7 +82,7 @@ def load_library(path: str | None = None) -> ctypes.CDLL:
     for name, argtypes in _SIGNATURES.items():
         function = getattr(lib, name)
         function.argtypes = argtypes
-        function.restype = _i32
+        function.restype = _RESTYPES.get(name, _i32)
     return lib
 
 

@@ -32,18 +32,22 @@ def stale() -> bool:
     return any(p.stat().st_mtime > built for p in inputs())
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and not stale():
+def build(force: bool = False, verbose: bool = False, output: Path | None = None,
+          defines: tuple[str, ...] = ()) -> Path:
+    """Compiles the library. `output`/`defines` make an instrumented copy
+    elsewhere (e.g. defines=("H4B_PHASE_TRACE",) for the phase timeline)."""
+    target = Path(output) if output is not None else LIBRARY
+    if output is None and not force and not stale():
         return LIBRARY
-    temporary = LIBRARY.with_suffix(f".{os.getpid()}.tmp.so")
+    temporary = target.with_suffix(f".{os.getpid()}.tmp.so")
     command = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "--shared", "-Xcompiler", "-fPIC",
-               "-cudart", "static", f"-I{PACKAGE.parent / 'include'}",
+               "-cudart", "static", f"-I{PACKAGE.parent / 'include'}", *(f"-D{d}" for d in defines),
                str(SOURCES / "harsh4b_b200.cu"), "-o", str(temporary)]
     if verbose:
         command.insert(1, "-Xptxas=-v")
     subprocess.run(command, check=True)
-    os.replace(temporary, LIBRARY)
-    return LIBRARY
+    os.replace(temporary, target)
+    return target
 
 
 if __name__ == "__main__":

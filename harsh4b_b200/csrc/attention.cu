@@ -91,28 +91,42 @@ __device__ __forceinline__ float dot4(float4 a, float4 b) {
     return __fmaf_rn(a.w, b.w, __fmaf_rn(a.z, b.z, __fmaf_rn(a.y, b.y, __fmul_rn(a.x, b.x))));
 }
 
+// Constants the per-head norm and RoPE of one lane read: gamma[4 lane ..],
+// cos/sin[(4 lane) mod 64 ..]. They are weights and tables, so callers may
+// load them before the head itself is ready.
+struct HeadConsts {
+    float4 g, c, s;
+};
+
+__device__ __forceinline__ HeadConsts head_consts(const float* gamma, const float* cs, const float* sn, int lane) {
+    HeadConsts k;
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int i = (4 * lane) & (kHeadDim / 2 - 1);
+    k.g = gamma ? *reinterpret_cast<const float4*>(gamma + 4 * lane) : z;
+    k.c = cs ? *reinterpret_cast<const float4*>(cs + i) : z;
+    k.s = sn ? *reinterpret_cast<const float4*>(sn + i) : z;
+    return k;
+}
+
 // Per-head RMSNorm (cpu_lightspark.py:373-379) and half-split RoPE
 // (cpu_lightspark.py:381-387) on one 128-wide head held 4 values per lane.
-__device__ __forceinline__ float4 norm_rope(float4 v, const float* gamma, const float* cs, const float* sn,
-                                            float eps, int lane) {
-    if (gamma) {
+__device__ __forceinline__ float4 norm_rope_with(float4 v, const HeadConsts& k, bool has_gamma, bool has_rope,
+                                                 float eps, int lane) {
+    if (has_gamma) {
         const float ss = warp_sum(dot4(v, v));
         const float root = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(kHeadDim)), eps));
-        const float4 g = *reinterpret_cast<const float4*>(gamma + 4 * lane);
-        v.x = __fmul_rn(__fdiv_rn(v.x, root), g.x);
-        v.y = __fmul_rn(__fdiv_rn(v.y, root), g.y);
-        v.z = __fmul_rn(__fdiv_rn(v.z, root), g.z);
-        v.w = __fmul_rn(__fdiv_rn(v.w, root), g.w);
+        v.x = __fmul_rn(__fdiv_rn(v.x, root), k.g.x);
+        v.y = __fmul_rn(__fdiv_rn(v.y, root), k.g.y);
+        v.z = __fmul_rn(__fdiv_rn(v.z, root), k.g.z);
+        v.w = __fmul_rn(__fdiv_rn(v.w, root), k.g.w);
     }
-    if (cs) {
+    if (has_rope) {
         float4 other;
         other.x = __shfl_xor_sync(0xffffffffu, v.x, 16);
         other.y = __shfl_xor_sync(0xffffffffu, v.y, 16);
         other.z = __shfl_xor_sync(0xffffffffu, v.z, 16);
         other.w = __shfl_xor_sync(0xffffffffu, v.w, 16);
-        const int i = (4 * lane) & (kHeadDim / 2 - 1);
-        const float4 c = *reinterpret_cast<const float4*>(cs + i);
-        const float4 s = *reinterpret_cast<const float4*>(sn + i);
+        const float4 c = k.c, s = k.s;
         if (lane < 16) {  // first half: x1*cos - x2*sin
             v = make_float4(__fsub_rn(__fmul_rn(v.x, c.x), __fmul_rn(other.x, s.x)),
                             __fsub_rn(__fmul_rn(v.y, c.y), __fmul_rn(other.y, s.y)),
@@ -128,23 +142,42 @@ __device__ __forceinline__ float4 norm_rope(float4 v, const float* gamma, const 
     return v;
 }
 
-// Combine split results (m_i, l_i, o_i) of one q head into the output.
+__device__ __forceinline__ float4 norm_rope(float4 v, const float* gamma, const float* cs, const float* sn,
+                                            float eps, int lane) {
+    return norm_rope_with(v, head_consts(gamma, cs, sn, lane), gamma != nullptr, cs != nullptr, eps, lane);
+}
+
+// Combine split results (m_i, l_i, o_i) of one q head into the output, in
+// split order. The loads are batched (m and l one split per lane, o eight
+// splits at a time) so the merge costs a few L2 round trips, not one per
+// split; the arithmetic is the same sequence as a plain loop over splits.
 __device__ __forceinline__ float4 merge_splits(const float* base, int splits, int stride, int lane) {
     float mmax = -INFINITY;
-    for (int s = 0; s < splits; ++s) mmax = fmaxf(mmax, __ldcg(base + s * stride + kHeadDim));
+    for (int s = lane; s < splits; s += 32) mmax = fmaxf(mmax, __ldcg(base + s * stride + kHeadDim));
+    mmax = warp_max(mmax);
     float l = 0.f;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < splits; ++s) {
-        const float* p = base + s * stride;
-        const float ls = __ldcg(p + kHeadDim + 1);
-        if (ls == 0.f) continue;
-        const float w = exp_cw(__ldcg(p + kHeadDim) - mmax);
-        l = __fmaf_rn(ls, w, l);
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(p + 4 * lane));
-        o.x = __fmaf_rn(v.x, w, o.x);
-        o.y = __fmaf_rn(v.y, w, o.y);
-        o.z = __fmaf_rn(v.z, w, o.z);
-        o.w = __fmaf_rn(v.w, w, o.w);
+    constexpr int kBatch = 8;
+    for (int s0 = 0; s0 < splits; s0 += kBatch) {
+        float ms[kBatch], ls[kBatch];
+        float4 vs[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const float* p = base + min(s0 + j, splits - 1) * stride;
+            ms[j] = __ldcg(p + kHeadDim);
+            ls[j] = __ldcg(p + kHeadDim + 1);
+            vs[j] = __ldcg(reinterpret_cast<const float4*>(p + 4 * lane));
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            if (s0 + j >= splits || ls[j] == 0.f) continue;
+            const float w = exp_cw(ms[j] - mmax);
+            l = __fmaf_rn(ls[j], w, l);
+            o.x = __fmaf_rn(vs[j].x, w, o.x);
+            o.y = __fmaf_rn(vs[j].y, w, o.y);
+            o.z = __fmaf_rn(vs[j].z, w, o.z);
+            o.w = __fmaf_rn(vs[j].w, w, o.w);
+        }
     }
     const float inv = __fdiv_rn(1.0f, l);
     return make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
@@ -166,6 +199,78 @@ __device__ __forceinline__ float transpose_reduce32(float v[32], int lane) {
         }
     }
     return v[0];
+}
+
+// Starts the asynchronous copy of sub-tile rows [base, base + n) of one kv
+// head's K and V into ks/vs (16-byte pieces spread over `threads` threads),
+// leaving out row `skip` (the new token, which arrives from registers).
+template <typename KV>
+__device__ __forceinline__ void stage_subtile(const KV* kc, const KV* vc, long long time_stride, int base, int n,
+                                              int skip, KV* ks, KV* vs, int tid, int threads) {
+    constexpr int kRowVecs = kHeadDim * sizeof(KV) / 16;
+    for (int i = tid; i < 2 * n * kRowVecs; i += threads) {
+        const int which = i / (n * kRowVecs), rest = i % (n * kRowVecs);
+        const int r = rest / kRowVecs, piece = rest % kRowVecs;
+        if (base + r == skip) continue;
+        const KV* src = (which ? vc : kc) + static_cast<long long>(base + r) * time_stride;
+        async_copy16(reinterpret_cast<uint4*>((which ? vs : ks) + r * kHeadDim) + piece,
+                     reinterpret_cast<const uint4*>(src) + piece);
+    }
+}
+
+// Folds one staged sub-tile (n <= kSubTile tokens in ks/vs) into a q head's
+// running (m, l, o): scores 32 tokens per round (lane l ends with token
+// 32 r + l), a two-pass softmax over the sub-tile, p * v accumulated in token
+// order, then the running merge. The p * v loop is unrolled over whole
+// rounds; tokens past n add p = 0 times a staged row, which leaves every
+// partial sum unchanged.
+template <typename KV>
+__device__ __forceinline__ void attend_subtile(float4 q, const KV* ks, const KV* vs, int n, float scale, int lane,
+                                               float& m, float& l, float4& o) {
+    float p_round[2];
+    float mt = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        if (32 * r >= n) {  // uniform: the sub-tile has no second round
+            p_round[r] = -INFINITY;
+            continue;
+        }
+        float part[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+            const int tt = min(32 * r + t, n - 1);
+            part[t] = dot4(q, load4<KV>(ks + tt * kHeadDim + 4 * lane));
+        }
+        const float sc = __fmul_rn(transpose_reduce32(part, lane), scale);
+        p_round[r] = (32 * r + lane < n) ? sc : -INFINITY;
+        mt = fmaxf(mt, p_round[r]);
+    }
+    mt = warp_max(mt);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) p_round[r] = (32 * r + lane < n) ? exp_cw(p_round[r] - mt) : 0.f;
+    const float lt = warp_sum(p_round[0] + p_round[1]);
+    float4 ot = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        if (32 * r >= n) break;
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+            const float p = __shfl_sync(0xffffffffu, p_round[r], t);
+            const float4 v = load4<KV>(vs + min(32 * r + t, n - 1) * kHeadDim + 4 * lane);
+            ot.x = __fmaf_rn(p, v.x, ot.x);
+            ot.y = __fmaf_rn(p, v.y, ot.y);
+            ot.z = __fmaf_rn(p, v.z, ot.z);
+            ot.w = __fmaf_rn(p, v.w, ot.w);
+        }
+    }
+    const float mn = fmaxf(m, mt);
+    const float c_old = exp_cw(m - mn), c_new = exp_cw(mt - mn);
+    l = __fmaf_rn(l, c_old, __fmul_rn(lt, c_new));
+    o.x = __fmaf_rn(o.x, c_old, __fmul_rn(ot.x, c_new));
+    o.y = __fmaf_rn(o.y, c_old, __fmul_rn(ot.y, c_new));
+    o.z = __fmaf_rn(o.z, c_old, __fmul_rn(ot.z, c_new));
+    o.w = __fmaf_rn(o.w, c_old, __fmul_rn(ot.w, c_new));
+    m = mn;
 }
 
 template <typename KV>
@@ -216,67 +321,19 @@ __global__ void __launch_bounds__(256) gqa_split_kernel(const AttnArgs a) {
     }
 
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(kHeadDim)));
-    constexpr int kRowVecs = kHeadDim * sizeof(KV) / 16;  // 16-byte pieces per row
     float m = -INFINITY, l = 0.f;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int base = t0; base < t1; base += kSubTile) {
         const int n = min(kSubTile, t1 - base);
         __syncthreads();  // the previous sub-tile is consumed
-        for (int i = threadIdx.x; i < 2 * n * kRowVecs; i += blockDim.x) {
-            const int which = i / (n * kRowVecs), rest = i % (n * kRowVecs);
-            const int r = rest / kRowVecs, piece = rest % kRowVecs;
-            if (base + r == pos && owns_new) continue;  // filled from registers below
-            const KV* src = (which ? vc : kc) + static_cast<long long>(base + r) * a.time_stride;
-            reinterpret_cast<uint4*>((which ? vs : ks) + r * kHeadDim)[piece] =
-                __ldcg(reinterpret_cast<const uint4*>(src) + piece);
-        }
+        stage_subtile<KV>(kc, vc, a.time_stride, base, n, owns_new ? pos : -1, ks, vs, threadIdx.x, blockDim.x);
         if (owns_new && pos >= base && pos < base + n) {
             if (warp == 0) store4<KV>(ks + (pos - base) * kHeadDim + 4 * lane, k_new);
             if (warp == a.groups - 1) store4<KV>(vs + (pos - base) * kHeadDim + 4 * lane, v_new);
         }
+        async_copy_wait_all();
         __syncthreads();
-
-        // scores, 32 tokens per round; lane l ends with token (round * 32 + l)
-        float p_round[2];
-        float mt = -INFINITY;
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            if (32 * r >= n) {  // uniform: the sub-tile has no second round
-                p_round[r] = -INFINITY;
-                continue;
-            }
-            float part[32];
-#pragma unroll
-            for (int t = 0; t < 32; ++t) {
-                const int tt = min(32 * r + t, n - 1);
-                part[t] = dot4(q, load4<KV>(ks + tt * kHeadDim + 4 * lane));
-            }
-            const float sc = __fmul_rn(transpose_reduce32(part, lane), scale);
-            const bool valid = 32 * r + lane < n;
-            p_round[r] = valid ? sc : -INFINITY;
-            mt = fmaxf(mt, p_round[r]);
-        }
-        mt = warp_max(mt);
-#pragma unroll
-        for (int r = 0; r < 2; ++r) p_round[r] = (32 * r + lane < n) ? exp_cw(p_round[r] - mt) : 0.f;
-        const float lt = warp_sum(p_round[0] + p_round[1]);
-        float4 ot = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int t = 0; t < n; ++t) {
-            const float p = __shfl_sync(0xffffffffu, p_round[t >> 5], t & 31);
-            const float4 v = load4<KV>(vs + t * kHeadDim + 4 * lane);
-            ot.x = __fmaf_rn(p, v.x, ot.x);
-            ot.y = __fmaf_rn(p, v.y, ot.y);
-            ot.z = __fmaf_rn(p, v.z, ot.z);
-            ot.w = __fmaf_rn(p, v.w, ot.w);
-        }
-        const float mn = fmaxf(m, mt);
-        const float c_old = exp_cw(m - mn), c_new = exp_cw(mt - mn);
-        l = __fmaf_rn(l, c_old, __fmul_rn(lt, c_new));
-        o.x = __fmaf_rn(o.x, c_old, __fmul_rn(ot.x, c_new));
-        o.y = __fmaf_rn(o.y, c_old, __fmul_rn(ot.y, c_new));
-        o.z = __fmaf_rn(o.z, c_old, __fmul_rn(ot.z, c_new));
-        o.w = __fmaf_rn(o.w, c_old, __fmul_rn(ot.w, c_new));
-        m = mn;
+        attend_subtile<KV>(q, ks, vs, n, scale, lane, m, l, o);
     }
 
     float* out_h = a.out + b * a.out_batch_stride + static_cast<long long>(h) * kHeadDim;

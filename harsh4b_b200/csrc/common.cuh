@@ -38,6 +38,36 @@ __device__ __forceinline__ bool wait_failed_before() {
     return (*reinterpret_cast<volatile int*>(&g_status) & kStatusWaitTimeout) != 0;
 }
 
+// ---- optional phase timeline ----------------------------------------------
+// Built with -DH4B_PHASE_TRACE, H4B_TRACE(ev) records %globaltimer for event
+// `ev` (< 2048) on three CTAs (first, middle, last) into g_phase_trace, which
+// h4b_phase_trace copies out. In the normal build it compiles to nothing.
+#ifdef H4B_PHASE_TRACE
+__device__ unsigned long long g_phase_trace[3][2048];
+__device__ __forceinline__ int trace_slot() {
+    const unsigned c = blockIdx.x;
+    return c == 0 ? 0 : (c == gridDim.x / 2 ? 1 : (c == gridDim.x - 1 ? 2 : -1));
+}
+#define H4B_TRACE_ANY(ev)                                                             \
+    do {                                                                              \
+        const int _s = ::h4b::trace_slot();                                           \
+        if (_s >= 0) ::h4b::g_phase_trace[_s][(ev)] = ::h4b::globaltimer_ns();        \
+    } while (0)
+#define H4B_TRACE(ev)                                \
+    do {                                             \
+        if (threadIdx.x == 0) H4B_TRACE_ANY(ev);     \
+    } while (0)
+#define H4B_TRACE_VAL(ev, val)                                                           \
+    do {                                                                                 \
+        const int _s = ::h4b::trace_slot();                                              \
+        if (_s >= 0) ::h4b::g_phase_trace[_s][(ev)] = static_cast<unsigned long long>(val); \
+    } while (0)
+#else
+#define H4B_TRACE_VAL(ev, val) do { } while (0)
+#define H4B_TRACE_ANY(ev) do { } while (0)
+#define H4B_TRACE(ev) do { } while (0)
+#endif
+
 // ---- programmatic dependent launch ---------------------------------------
 // Everything before pdl_wait() may only touch data no earlier kernel in the
 // stream writes (weights, scales, tables). pdl_trigger() lets the next
@@ -115,8 +145,83 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ void async_copy4(void* dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(smem_addr(dst)), "l"(src) : "memory");
 }
+// 16-byte asynchronous copy through L2 only (data another SM may have
+// written in an earlier launch); both addresses 16-byte aligned.
+__device__ __forceinline__ void async_copy16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_addr(dst)), "l"(src) : "memory");
+}
 __device__ __forceinline__ void async_copy_wait_all() {
     asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// ---- tagged exchange words ------------------------------------------------------
+// A 64-bit word carries a 32-bit payload (low half) and a 32-bit tag (high
+// half) and is written and read with single 8-byte accesses, which are
+// single-copy atomic: a reader that sees the tag it expects also sees the
+// payload stored with it. Producers store with no fence and consumers poll
+// the words themselves, so a cross-SM handoff costs one store plus one load
+// instead of store, fence, flag, poll and load.
+__device__ __forceinline__ unsigned long long ll_pack(float v, uint32_t tag) {
+    return (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ uint32_t ll_tag(unsigned long long w) { return static_cast<uint32_t>(w >> 32); }
+__device__ __forceinline__ float ll_value(unsigned long long w) {
+    return __uint_as_float(static_cast<uint32_t>(w & 0xFFFFFFFFull));
+}
+__device__ __forceinline__ void ll_store(unsigned long long* p, float v, uint32_t tag) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" :: "l"(p), "l"(ll_pack(v, tag)) : "memory");
+}
+__device__ __forceinline__ void ll_store_raw2(unsigned long long* p, unsigned long long a, unsigned long long b) {
+    asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" :: "l"(p), "l"(a), "l"(b) : "memory");
+}
+// Two adjacent words (p 16-byte aligned).
+__device__ __forceinline__ void ll_store2(unsigned long long* p, float a, float b, uint32_t tag) {
+    ll_store_raw2(p, ll_pack(a, tag), ll_pack(b, tag));
+}
+__device__ __forceinline__ ulonglong2 ll_load2(const unsigned long long* p) {
+    ulonglong2 w;
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+    return w;
+}
+__device__ __forceinline__ unsigned long long ll_load(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+// Bounded polling: a poll loop calls poll_expired() between rounds; it
+// backs off briefly and returns true (after reporting) once the wait limit
+// has passed or another wait has already failed.
+struct PollClock {
+    uint64_t start = 0;
+    uint32_t rounds = 0;
+};
+__device__ __forceinline__ bool poll_expired(PollClock& c) {
+    if (c.rounds++ == 0) {
+        c.start = globaltimer_ns();
+        return false;
+    }
+    __nanosleep(96);
+    if ((c.rounds & 255) != 0) return false;
+    if (wait_failed_before()) return true;
+    if (globaltimer_ns() - c.start > kWaitLimitNs) {
+        report(kStatusWaitTimeout);
+        return true;
+    }
+    return false;
+}
+
+// ---- grid-scope release / acquire counters ------------------------------------
+// Release-add: every write this thread has observed (the CTA's writes, after
+// a CTA barrier) is visible at GPU scope before the count moves.
+__device__ __forceinline__ void red_release_add(uint32_t* counter, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(counter), "r"(v) : "memory");
+}
+// Acquire-release add that returns the previous count (last-arriver tests).
+__device__ __forceinline__ uint32_t atom_acq_rel_add(uint32_t* counter, uint32_t v) {
+    uint32_t prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(prev) : "l"(counter), "r"(v) : "memory");
+    return prev;
 }
 
 // ---- named barrier among a subset of warps ------------------------------------

@@ -23,35 +23,70 @@
 
 namespace h4b {
 
-constexpr int kMkWarps = 8;  // consumer warps
+// 7 consumer warps + 1 producer warp: two warps per SM sub-partition, so a
+// thread may hold up to 255 registers (9 warps would cap it at 168).
+constexpr int kMkWarps = 7;  // consumer warps
 constexpr int kMkConsumers = kMkWarps * 32;
+constexpr int kRmsLanes = 256;  // lanes of the RMSNorm reduction order (see mk_prologue_rms_g)
+static_assert(kMkConsumers >= kRmsLanes - 32 && kMkConsumers <= kRmsLanes, "RMS lane map");
 constexpr int kMkThreads = kMkConsumers + 32;
 constexpr int kMkMaxSlotBytes = 16384;
-constexpr int kMkStages = 16;  // a multiple of kMkWarps: each ring slot has one owning warp
+constexpr int kMkStages = 14;  // a multiple of kMkWarps: each ring slot has one owning warp
 constexpr int kMkMaxStages = kMkStages;
-constexpr int kMkMaxHidden = 8192;  // RMSNorm inputs kept in registers (4 groups of 8 per thread)
+constexpr int kMkMaxHidden = 4096;  // RMSNorm inputs kept in registers (2 groups of 8 per lane)
 constexpr int kMkMaxWidth = 16384;
 
 enum { SEG_QKV = 0, SEG_O = 1, SEG_GATE_UP = 2, SEG_DOWN = 3 };
 
+constexpr int kMkMaxCtas = 1024;   // exchange words sized for up to this many CTAs
+constexpr int kMkSplitCap = 64;    // attention splits per kv head at most
+
+// Tagged exchange words (state->exchange): every value one CTA hands to
+// others is a 64-bit word {tag, fp32 payload}. Offsets in words; every
+// region starts on a 16-byte boundary.
+struct XLayout {
+    long long x_o, x_down, qkv, part, att, att_max, act, act_max, keys, gen, total;
+};
+
+__host__ __device__ inline long long round4(long long n) { return (n + 3) & ~3ll; }
+
+__host__ __device__ inline XLayout x_layout(const h4b_model& m) {
+    const long long H = m.hidden, Q = static_cast<long long>(m.heads) * m.head_dim;
+    const long long KV = static_cast<long long>(m.kv_heads) * m.head_dim;
+    const long long groups = m.kv_heads > 0 ? m.heads / m.kv_heads : 0;
+    XLayout x;
+    x.x_o = 0;                                  // x after the o residual, [H]
+    x.x_down = x.x_o + round4(H);               // x after the down residual, [H]
+    x.qkv = x.x_down + round4(H);               // q, k, v projections, [Q + 2 KV]
+    x.part = x.qkv + round4(Q + 2 * KV);        // split partials [kv][splits][groups][kPartialStride]
+    x.att = x.part + static_cast<long long>(m.kv_heads) * kMkSplitCap * groups * kPartialStride;
+    x.att_max = x.att + round4(Q);              // attended [Q], then its absmax per kv head
+    x.act = x.att_max + round4(m.kv_heads);     // SwiGLU output [I], then its absmax per CTA
+    x.act_max = x.act + round4(m.intermediate);
+    x.keys = x.act_max + kMkMaxCtas;            // per-CTA argmax key (two words)
+    x.gen = x.keys + 2 * kMkMaxCtas;            // per-CTA launch counters (never cleared)
+    x.total = x.gen + kMkMaxCtas;
+    return x;
+}
+
+// Tags: launch generation g (per-CTA counters that every launch advances, so
+// all CTAs agree without any clearing) and 6 handoffs per layer plus the
+// final one. A stale word always carries an older tag.
+enum { TAG_QKV = 0, TAG_PART = 1, TAG_ATT = 2, TAG_XO = 3, TAG_ACT = 4, TAG_XDOWN = 5, kTagsPerLayer = 6 };
+__host__ __device__ inline uint32_t mk_tag_base(uint32_t gen, int layers) {
+    return 1u + gen * static_cast<uint32_t>(kTagsPerLayer * layers + 2);
+}
+
 struct MkArgs {
     h4b_model m;
     h4b_state s;
-    uint32_t* ready;       // [5 * layers + 2] phase counters
-    uint32_t* attn_count;  // [layers][kv_heads] split-merge counters
+    XLayout x;
     int stages;
     int slot_bytes;        // ring slot size (a tile is at most one slot)
     int attn_chunk;        // target tokens per attention split
     int max_splits;        // splits per kv head at most
     int xq_bytes, rows_cap;
 };
-
-// Phase counter indices.
-__host__ __device__ inline int ph_qkv(int l) { return 5 * l; }
-__host__ __device__ inline int ph_attn(int l) { return 5 * l + 1; }
-__host__ __device__ inline int ph_o(int l) { return 5 * l + 2; }
-__host__ __device__ inline int ph_gate_up(int l) { return 5 * l + 3; }
-__host__ __device__ inline int ph_down(int l) { return 5 * l + 4; }
 
 struct Seg {
     const uint8_t* w;
@@ -104,109 +139,192 @@ __device__ __forceinline__ Seg mk_segment(const MkArgs& a, int g, int cta, int n
     return s;
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// The consumers' stop decision. flags[0] is a stop request any warp may set
-// at any time (the producer included); flags[1] is a snapshot only consumer
-// thread 0 writes, before named barrier 1, and every consumer reads after
-// it -- so all consumer threads take the same branch and none is left
+// The consumers' stop decision: any consumer thread may report a failure
+// (`failed`); flags[0] also carries stop requests from any warp, the
+// producer included. Thread 0 snapshots flags[0] into flags[1] between two
+// barriers, so every consumer thread takes the same branch and none is left
 // waiting at a later named barrier.
-__device__ bool mk_stop(int* flags, bool own_failure = false) {
-    if (threadIdx.x == 0) {
-        if (own_failure) atomicOr(&flags[0], 1);
-        flags[1] = *reinterpret_cast<volatile int*>(&flags[0]);
-    }
+__device__ bool mk_stop(int* flags, bool failed = false) {
+    if (failed) atomicOr(&flags[0], 1);
+    named_sync(1, kMkConsumers);
+    if (threadIdx.x == 0) flags[1] = *reinterpret_cast<volatile int*>(&flags[0]);
     named_sync(1, kMkConsumers);
     return flags[1] != 0;
 }
 
-// Consumer-side dependency wait: thread 0 polls; returns false (for every
-// consumer thread alike) if the CTA must stop.
-__device__ bool mk_wait(const uint32_t* counter, uint32_t target, int* flags) {
-    bool failed = false;
-    if (threadIdx.x == 0 && ld_acquire_u32(counter) < target) {
-        const uint64_t start = globaltimer_ns();
-        for (uint32_t spin = 1; ld_acquire_u32(counter) < target; ++spin) {
-            __nanosleep(32);  // keep the poll off the issue slots of the working warps
-            if ((spin & 63) != 0) continue;
-            if (wait_failed_before() || *reinterpret_cast<volatile int*>(&flags[0])) {
-                failed = true;
-                break;
-            }
-            if (globaltimer_ns() - start > kWaitLimitNs) {
-                report(kStatusWaitTimeout);
-                failed = true;
-                break;
+// Polls the 8-word groups lane_id + k * 256 (k < G, < groups) of exchange
+// words until each carries `tag`; leaves the payloads in v. All loads of a
+// round are issued before any is checked, so a round costs one L2 round
+// trip. On timeout sets the CTA stop flag (values are then zero).
+template <int G>
+__device__ void mk_poll_lane(const unsigned long long* w, int lane_id, int groups, uint32_t tag, float v[G][8],
+                             int* flags) {
+    unsigned pending = 0;
+#pragma unroll
+    for (int k = 0; k < G; ++k)
+        if (lane_id + k * kRmsLanes < groups) pending |= 1u << k;
+    PollClock clk;
+    while (pending) {
+        if (clk.rounds != 0) {
+            // Data not complete yet: watch one word per pending group
+            // (little L2 traffic) before loading the groups again.
+            bool seen = true;
+#pragma unroll
+            for (int k = 0; k < G; ++k)
+                if (pending & (1u << k)) seen = seen && ll_tag(ll_load(w + 8 * (lane_id + k * kRmsLanes) + 7)) == tag;
+            if (!seen) {
+                if (poll_expired(clk)) {
+                    atomicOr(&flags[0], 1);
+#pragma unroll
+                    for (int k = 0; k < G; ++k)
+                        if (pending & (1u << k))
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) v[k][e] = 0.f;
+                    return;
+                }
+                continue;
             }
         }
+        ulonglong2 raw[G][4];
+#pragma unroll
+        for (int k = 0; k < G; ++k) {
+            if (pending & (1u << k)) {
+                const unsigned long long* p = w + 8 * (lane_id + k * kRmsLanes);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) raw[k][j] = ll_load2(p + 2 * j);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < G; ++k) {
+            if (!(pending & (1u << k))) continue;
+            bool ok = true;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ok = ok && ll_tag(raw[k][j].x) == tag && ll_tag(raw[k][j].y) == tag;
+            if (ok) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    v[k][2 * j] = ll_value(raw[k][j].x);
+                    v[k][2 * j + 1] = ll_value(raw[k][j].y);
+                }
+                pending &= ~(1u << k);
+            }
+        }
+        if (pending && poll_expired(clk)) {
+            atomicOr(&flags[0], 1);
+#pragma unroll
+            for (int k = 0; k < G; ++k)
+                if (pending & (1u << k))
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[k][e] = 0.f;
+            break;
+        }
     }
-    return !mk_stop(flags, failed);
 }
 
-// All consumer writes of this phase are done: publish them.
-__device__ __forceinline__ void mk_signal(uint32_t* counter) {
-    named_sync(1, kMkConsumers);
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(counter, 1u);
+// Polls one exchange word per thread (index tid + k * kMkConsumers < n) and
+// returns the max of the payloads it saw (0 when it holds none).
+__device__ float mk_poll_max(const unsigned long long* w, int n, uint32_t tag, int* flags) {
+    float mx = 0.f;
+    for (int i = threadIdx.x; i < n; i += kMkConsumers) {
+        PollClock clk;
+        unsigned long long word = ll_load(w + i);
+        while (ll_tag(word) != tag) {
+            if (poll_expired(clk)) {
+                atomicOr(&flags[0], 1);
+                break;
+            }
+            word = ll_load(w + i);
+        }
+        mx = fmaxf(mx, ll_tag(word) == tag ? ll_value(word) : 0.f);
     }
+    return mx;
 }
 
-__device__ __forceinline__ void load8_cg(const float* p, float v[8]) {
-    const float4 a = __ldcg(reinterpret_cast<const float4*>(p));
-    const float4 b = __ldcg(reinterpret_cast<const float4*>(p + 4));
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
+// The RMSNorm sum of squares is defined over 256 lanes (the GEMV kernel's
+// consumer threads, which the CPU oracle follows): lane p sums groups
+// p, p + 256, ... of 8 values with fmaf, each warp of lanes is summed with a
+// butterfly, and the 8 warp totals are added in order. Consumer thread t
+// computes lane t; warp 0 also computes lanes 224..255 (lane-warp 7).
 
-// RMSNorm + absmax quantisation of x (n <= kMkMaxHidden) into xq, in the
-// same order as the GEMV kernel's prologue; returns the dequant scale.
-__device__ float mk_prologue_rms(const float* x, bool from_smem, const float* gamma_s, int n, float eps,
-                                 int8_t* xq, float* red) {
-    const int tid = threadIdx.x;
+// RMSNorm + absmax quantisation of x (n <= G * 8 * 256) into xq, in the same
+// order as the GEMV kernel's prologue; returns the dequant scale. x is the
+// embedding row in shared memory (xs) or exchange words carrying `tag`.
+template <int G>
+__device__ float mk_prologue_rms_g(const float* xs, const unsigned long long* xw, uint32_t tag, const float* gamma_s,
+                                   int n, float eps, int8_t* xq, float* red, int* flags) {
+    const int tid = threadIdx.x, warp = tid >> 5;
     const int groups = n >> 3;
-    float v[4][8];
-    float ss = 0.f;
+    const bool extra = tid + kMkConsumers < kRmsLanes;  // warp 0: also lane tid + kMkConsumers
+    float v[2][G][8];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int g = tid + k * kMkConsumers;
-        if (g < groups) {
-            if (from_smem) load8(x + 8 * g, v[k]);
-            else load8_cg(x + 8 * g, v[k]);
+    for (int r = 0; r < 2; ++r) {
+        const int lane_id = tid + r * kMkConsumers;
+        if (r == 1 && !extra) break;
+        if (xw) {
+            mk_poll_lane<G>(xw, lane_id, groups, tag, v[r], flags);
+        } else {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) ss = __fmaf_rn(v[k][e], v[k][e], ss);
+            for (int k = 0; k < G; ++k) {
+                const int g = lane_id + k * kRmsLanes;
+                if (g < groups) load8(xs + 8 * g, v[r][k]);
+            }
         }
     }
-    ss = group_sum(ss, red, kMkWarps, 1);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(n)), eps)));
+    float ss[2] = {0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int lane_id = tid + r * kMkConsumers;
+#pragma unroll
+        for (int k = 0; k < G; ++k) {
+            if ((r == 0 || extra) && lane_id + k * kRmsLanes < groups) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ss[r] = __fmaf_rn(v[r][k][e], v[r][k][e], ss[r]);
+            }
+        }
+    }
+    const float w0 = warp_sum(ss[0]);
+    const float w1 = warp_sum(ss[1]);  // meaningful in warp 0 only
+    if ((tid & 31) == 0) {
+        red[warp] = w0;
+        if (warp == 0) red[kRmsLanes / 32 - 1] = w1;
+    }
+    named_sync(1, kMkConsumers);
+    float total = 0.f;
+    for (int w = 0; w < kRmsLanes / 32; ++w) total += red[w];
+    named_sync(1, kMkConsumers);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(n)), eps)));
     float local = 0.f;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int g = tid + k * kMkConsumers;
-        if (g < groups) {
-            float gm[8];
-            load8(gamma_s + 8 * g, gm);
+    for (int r = 0; r < 2; ++r) {
+        const int lane_id = tid + r * kMkConsumers;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                v[k][e] = __fmul_rn(__fmul_rn(v[k][e], inv), gm[e]);
-                local = fmaxf(local, fabsf(v[k][e]));
+        for (int k = 0; k < G; ++k) {
+            const int g = lane_id + k * kRmsLanes;
+            if ((r == 0 || extra) && g < groups) {
+                float gm[8];
+                load8(gamma_s + 8 * g, gm);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    v[r][k][e] = __fmul_rn(__fmul_rn(v[r][k][e], inv), gm[e]);
+                    local = fmaxf(local, fabsf(v[r][k][e]));
+                }
             }
         }
     }
     const float m = group_max(local, red, kMkWarps, 1);
     const float qs = quant_multiplier(m);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int g = tid + k * kMkConsumers;
-        if (g < groups) {
-            int q[8];
+    for (int r = 0; r < 2; ++r) {
+        const int lane_id = tid + r * kMkConsumers;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) q[e] = quantize_one(v[k][e], qs);
-            store_group(xq, g, q);
+        for (int k = 0; k < G; ++k) {
+            const int g = lane_id + k * kRmsLanes;
+            if ((r == 0 || extra) && g < groups) {
+                int q[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) q[e] = quantize_one(v[r][k][e], qs);
+                store_group(xq, g, q);
+            }
         }
     }
     zero_xq_tail(xq, n, tid, kMkConsumers);
@@ -214,19 +332,76 @@ __device__ float mk_prologue_rms(const float* x, bool from_smem, const float* ga
     return dequant_scale(m);
 }
 
-// Quantisation of v with the absmax its producers published.
-__device__ float mk_prologue_quant(const float* v, const float* absmax_slot, int n, int8_t* xq) {
-    const float m = __ldcg(absmax_slot);
+__device__ float mk_prologue_rms(const float* xs, const unsigned long long* xw, uint32_t tag, const float* gamma_s,
+                                 int n, float eps, int8_t* xq, float* red, int* flags) {
+    return mk_prologue_rms_g<kMkMaxHidden / (8 * kRmsLanes)>(xs, xw, tag, gamma_s, n, eps, xq, red, flags);
+}
+
+// Quantisation of n exchange words carrying `tag` with the absmax over the
+// nmax partial maxima its producers published (also tagged `tag`). Groups
+// g = tid + k * kMkConsumers of 8 words are loaded kMkQuantGroups at a time
+// and quantised as soon as their tags check.
+constexpr int kMkQuantGroups = 4;
+__device__ float mk_prologue_quant(const unsigned long long* vw, const unsigned long long* maxw, int nmax, uint32_t tag,
+                                   int n, int8_t* xq, float* red, int* flags) {
+    const int tid = threadIdx.x;
+    const int groups = n >> 3;
+    const float m = group_max(mk_poll_max(maxw, nmax, tag, flags), red, kMkWarps, 1);
     const float qs = quant_multiplier(m);
-    for (int g = threadIdx.x; g < (n >> 3); g += kMkConsumers) {
-        float x[8];
-        int q[8];
-        load8_cg(v + 8 * g, x);
+    for (int g0 = tid; g0 < groups; g0 += kMkQuantGroups * kMkConsumers) {
+        unsigned pending = 0;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) q[e] = quantize_one(x[e], qs);
-        store_group(xq, g, q);
+        for (int k = 0; k < kMkQuantGroups; ++k)
+            if (g0 + k * kMkConsumers < groups) pending |= 1u << k;
+        PollClock clk;
+        while (pending) {
+            if (clk.rounds != 0) {
+                bool seen = true;
+#pragma unroll
+                for (int k = 0; k < kMkQuantGroups; ++k)
+                    if (pending & (1u << k))
+                        seen = seen && ll_tag(ll_load(vw + 8 * (g0 + k * kMkConsumers) + 7)) == tag;
+                if (!seen) {
+                    if (poll_expired(clk)) {
+                        atomicOr(&flags[0], 1);
+                        break;
+                    }
+                    continue;
+                }
+            }
+            ulonglong2 raw[kMkQuantGroups][4];
+#pragma unroll
+            for (int k = 0; k < kMkQuantGroups; ++k) {
+                if (pending & (1u << k)) {
+                    const unsigned long long* p = vw + 8 * (g0 + k * kMkConsumers);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) raw[k][j] = ll_load2(p + 2 * j);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kMkQuantGroups; ++k) {
+                if (!(pending & (1u << k))) continue;
+                bool ok = true;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) ok = ok && ll_tag(raw[k][j].x) == tag && ll_tag(raw[k][j].y) == tag;
+                if (ok) {
+                    int q[8];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        q[2 * j] = quantize_one(ll_value(raw[k][j].x), qs);
+                        q[2 * j + 1] = quantize_one(ll_value(raw[k][j].y), qs);
+                    }
+                    store_group(xq, g0 + k * kMkConsumers, q);
+                    pending &= ~(1u << k);
+                }
+            }
+            if (pending && poll_expired(clk)) {
+                atomicOr(&flags[0], 1);
+                break;
+            }
+        }
     }
-    zero_xq_tail(xq, n, threadIdx.x, kMkConsumers);
+    zero_xq_tail(xq, n, tid, kMkConsumers);
     named_sync(1, kMkConsumers);
     return dequant_scale(m);
 }
@@ -268,6 +443,7 @@ __device__ void mk_tiles(const Seg& sg, uint32_t seq0, int stages, int slot_byte
             atomicOr(&flags[0], 1);
             break;
         }
+        if (lane == 0 && gseq >= 40 && gseq < 140) H4B_TRACE_ANY(1200 + gseq - 40);
         const uint8_t* tile = ring + static_cast<size_t>(slot) * slot_bytes;
         const int trows = min(sg.tile_rows, sg.nrows - t * sg.tile_rows);
         for (int b0 = 0; b0 < trows; b0 += RB) {
@@ -281,6 +457,7 @@ __device__ void mk_tiles(const Seg& sg, uint32_t seq0, int stages, int slot_byte
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
+        if (lane == 0 && gseq >= 40 && gseq < 140) H4B_TRACE_ANY(1300 + gseq - 40);
     }
     named_sync(1, kMkConsumers);  // acc_s complete
 }
@@ -309,15 +486,51 @@ __device__ __forceinline__ void mk_fetch_gamma(const float* gamma, float* gamma_
     for (int i = threadIdx.x; i < n; i += kMkConsumers) async_copy4(gamma_s + i, gamma + i);
 }
 
+// Starts fetching what GEMV segment g + 1 needs while segment g's tiles run:
+// its row scales (into scale buffer (g + 1) & 1) and, after an RMSNorm
+// prologue (qkv, gate/up), the norm weight of the next RMSNorm phase.
+__device__ __forceinline__ void mk_prefetch_next(const MkArgs& a, int g, int cta, int nctas, float* sc_base,
+                                                 float* gamma_s) {
+    const h4b_model& m = a.m;
+    const int H = m.hidden, l = g >> 2;
+    if (g < 4 * m.layers) mk_fetch_scales(mk_segment(a, g + 1, cta, nctas), sc_base + ((g + 1) & 1) * a.rows_cap);
+    if (g >= 4 * m.layers) return;
+    if ((g & 3) == SEG_QKV) mk_fetch_gamma(m.norm_post + static_cast<size_t>(l) * H, gamma_s, H);
+    if ((g & 3) == SEG_GATE_UP)
+        mk_fetch_gamma(l + 1 < m.layers ? m.norm_in + static_cast<size_t>(l + 1) * H : m.norm_final, gamma_s, H);
+}
+
 __device__ __forceinline__ float mk_value(const int32_t* acc_s, const float* sc_s, int i, float act_scale) {
     return __fmul_rn(__fmul_rn(static_cast<float>(acc_s[i]), act_scale), sc_s[i]);
 }
 
+// Polls the 4 exchange words of a 128-wide head that lane `lane` holds.
+__device__ __forceinline__ bool mk_poll_head(const unsigned long long* w, int lane, uint32_t tag, float4& out) {
+    const unsigned long long* p = w + 4 * lane;
+    PollClock clk;
+    while (true) {
+        const ulonglong2 a = ll_load2(p), b = ll_load2(p + 2);
+        if (ll_tag(a.x) == tag && ll_tag(a.y) == tag && ll_tag(b.x) == tag && ll_tag(b.y) == tag) {
+            out = make_float4(ll_value(a.x), ll_value(a.y), ll_value(b.x), ll_value(b.y));
+            return true;
+        }
+        if (poll_expired(clk)) {
+            out = make_float4(0.f, 0.f, 0.f, 0.f);
+            return false;
+        }
+    }
+}
+
 // One attention split (kv head h, split `split` of `splits`) for layer l,
-// in the order of gqa_split_kernel; the last split of head h merges.
+// in the order of gqa_split_kernel. The first sub-tile of past K/V rows and
+// the norm/RoPE constants are fetched before the new token's q/k/v are
+// polled. Splits other than 0 publish (o, m, l) per q head as exchange
+// words; split 0 merges them in split order (merge_splits' arithmetic) and
+// publishes the attended heads and their absmax. Returns false if the CTA
+// must stop.
 template <typename KV>
-__device__ void mk_attention(const MkArgs& a, int l, int h, int split, int splits, int pos, KV* ks, KV* vs,
-                             float* red, int* flags) {
+__device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t tbase, int l, int h, int split,
+                             int splits, int pos, KV* ks, KV* vs, float* consts_s, float* red, int* flags) {
     const h4b_model& m = a.m;
     const h4b_state& st = a.s;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -331,130 +544,180 @@ __device__ void mk_attention(const MkArgs& a, int l, int h, int split, int split
     const int t0 = min(ctx, split * chunk), t1 = min(ctx, t0 + chunk);
     const float* cs = m.rope_cos + static_cast<long long>(pos) * (d / 2);
     const float* sn = m.rope_sin + static_cast<long long>(pos) * (d / 2);
-    const float* qn = m.norm_q + static_cast<size_t>(l) * d;
-    const float* kn = m.norm_k + static_cast<size_t>(l) * d;
     const size_t kv_layer = static_cast<size_t>(m.kv_heads) * st.capacity * d;
     KV* kc = static_cast<KV*>(st.k_cache) + l * kv_layer + static_cast<size_t>(h) * st.capacity * d;
     KV* vc = static_cast<KV*>(st.v_cache) + l * kv_layer + static_cast<size_t>(h) * st.capacity * d;
-
-    float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (head_warp) {
-        q = __ldcg(reinterpret_cast<const float4*>(st.qkv + static_cast<long long>(qh) * d + 4 * lane));
-        q = norm_rope(q, qn, cs, sn, m.eps, lane);
-    }
     const bool owns_new = t0 <= pos && pos < t1;
-    float4 k_new = make_float4(0.f, 0.f, 0.f, 0.f), v_new = k_new;
+    const uint32_t tag_qkv = tbase + kTagsPerLayer * l + TAG_QKV;
+    const uint32_t tag_part = tbase + kTagsPerLayer * l + TAG_PART;
+    const uint32_t tag_att = tbase + kTagsPerLayer * l + TAG_ATT;
+
+    if (t0 < t1) stage_subtile<KV>(kc, vc, d, t0, min(kSubTile, t1 - t0), owns_new ? pos : -1, ks, vs, threadIdx.x,
+                                   kMkConsumers);
+    // q/k norm weights and this position's RoPE row into consts_s
+    // ([0, d) q gamma, [d, 2d) k gamma, [2d, 2.5d) cos, [2.5d, 3d) sin).
+    for (int i = threadIdx.x; i < 3 * d / 4; i += kMkConsumers) {
+        const float* src = i < d / 4 ? m.norm_q + static_cast<size_t>(l) * d + 4 * i
+                         : i < d / 2 ? m.norm_k + static_cast<size_t>(l) * d + 4 * (i - d / 4)
+                         : i < 5 * d / 8 ? cs + 4 * (i - d / 2)
+                                         : sn + 4 * (i - 5 * d / 8);
+        async_copy16(consts_s + 4 * i, src);
+    }
+    if (l == 1) H4B_TRACE(1500);
+
+    const unsigned long long* qkv = xw + a.x.qkv;
+    bool ok = true;
+    float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 k_new = q, v_new = q;
+    if (head_warp) ok = mk_poll_head(qkv + static_cast<long long>(qh) * d, lane, tag_qkv, q);
+    if (owns_new && warp == 0) ok = mk_poll_head(qkv + q_size + static_cast<long long>(h) * d, lane, tag_qkv, k_new) && ok;
+    if (owns_new && warp == groups - 1)
+        ok = mk_poll_head(qkv + q_size + kv_size + static_cast<long long>(h) * d, lane, tag_qkv, v_new) && ok;
+    if (mk_stop(flags, !ok)) {
+        async_copy_wait_all();
+        return false;
+    }
+    if (l == 1) H4B_TRACE(1501);
+    async_copy_wait_all();
+    named_sync(1, kMkConsumers);  // consts_s (and the first sub-tile) landed
+    if (head_warp) q = norm_rope_with(q, head_consts(consts_s, consts_s + 2 * d, consts_s + 5 * d / 2, lane), true,
+                                      true, m.eps, lane);
     if (owns_new) {
         if (warp == 0) {
-            k_new = __ldcg(reinterpret_cast<const float4*>(st.qkv + q_size + static_cast<long long>(h) * d + 4 * lane));
-            k_new = norm_rope(k_new, kn, cs, sn, m.eps, lane);
+            k_new = norm_rope_with(k_new, head_consts(consts_s + d, consts_s + 2 * d, consts_s + 5 * d / 2, lane),
+                                   true, true, m.eps, lane);
             store4<KV>(kc + static_cast<long long>(pos) * d + 4 * lane, k_new);
         }
-        if (warp == groups - 1) {
-            v_new = __ldcg(reinterpret_cast<const float4*>(st.qkv + q_size + kv_size + static_cast<long long>(h) * d +
-                                                            4 * lane));
-            store4<KV>(vc + static_cast<long long>(pos) * d + 4 * lane, v_new);
-        }
+        if (warp == groups - 1) store4<KV>(vc + static_cast<long long>(pos) * d + 4 * lane, v_new);
     }
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(d)));
-    constexpr int kRowVecs = kHeadDim * sizeof(KV) / 16;
     float mrun = -INFINITY, l_run = 0.f;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int base = t0; base < t1; base += kSubTile) {
         const int n = min(kSubTile, t1 - base);
-        named_sync(1, kMkConsumers);
-        for (int i = threadIdx.x; i < 2 * n * kRowVecs; i += kMkConsumers) {
-            const int which = i / (n * kRowVecs), rest = i % (n * kRowVecs);
-            const int r = rest / kRowVecs, piece = rest % kRowVecs;
-            if (base + r == pos && owns_new) continue;
-            const KV* src = (which ? vc : kc) + static_cast<long long>(base + r) * d;
-            reinterpret_cast<uint4*>((which ? vs : ks) + r * kHeadDim)[piece] =
-                __ldcg(reinterpret_cast<const uint4*>(src) + piece);
+        if (base != t0) {
+            named_sync(1, kMkConsumers);  // the previous sub-tile is consumed
+            stage_subtile<KV>(kc, vc, d, base, n, owns_new ? pos : -1, ks, vs, threadIdx.x, kMkConsumers);
         }
         if (owns_new && pos >= base && pos < base + n) {
             if (warp == 0) store4<KV>(ks + (pos - base) * kHeadDim + 4 * lane, k_new);
             if (warp == groups - 1) store4<KV>(vs + (pos - base) * kHeadDim + 4 * lane, v_new);
         }
+        async_copy_wait_all();
         named_sync(1, kMkConsumers);
-        if (head_warp) {
-            float p_round[2];
-            float mt = -INFINITY;
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                if (32 * r >= n) {
-                    p_round[r] = -INFINITY;
-                    continue;
-                }
-                float part[32];
-#pragma unroll
-                for (int t = 0; t < 32; ++t) {
-                    const int tt = min(32 * r + t, n - 1);
-                    part[t] = dot4(q, load4<KV>(ks + tt * kHeadDim + 4 * lane));
-                }
-                const float sc = __fmul_rn(transpose_reduce32(part, lane), scale);
-                p_round[r] = (32 * r + lane < n) ? sc : -INFINITY;
-                mt = fmaxf(mt, p_round[r]);
-            }
-            mt = warp_max(mt);
-#pragma unroll
-            for (int r = 0; r < 2; ++r) p_round[r] = (32 * r + lane < n) ? exp_cw(p_round[r] - mt) : 0.f;
-            const float lt = warp_sum(p_round[0] + p_round[1]);
-            float4 ot = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int t = 0; t < n; ++t) {
-                const float p = __shfl_sync(0xffffffffu, p_round[t >> 5], t & 31);
-                const float4 v = load4<KV>(vs + t * kHeadDim + 4 * lane);
-                ot.x = __fmaf_rn(p, v.x, ot.x);
-                ot.y = __fmaf_rn(p, v.y, ot.y);
-                ot.z = __fmaf_rn(p, v.z, ot.z);
-                ot.w = __fmaf_rn(p, v.w, ot.w);
-            }
-            const float mn = fmaxf(mrun, mt);
-            const float c_old = exp_cw(mrun - mn), c_new = exp_cw(mt - mn);
-            l_run = __fmaf_rn(l_run, c_old, __fmul_rn(lt, c_new));
-            o.x = __fmaf_rn(o.x, c_old, __fmul_rn(ot.x, c_new));
-            o.y = __fmaf_rn(o.y, c_old, __fmul_rn(ot.y, c_new));
-            o.z = __fmaf_rn(o.z, c_old, __fmul_rn(ot.z, c_new));
-            o.w = __fmaf_rn(o.w, c_old, __fmul_rn(ot.w, c_new));
-            mrun = mn;
-        }
+        if (l == 1) H4B_TRACE(1502);
+        if (head_warp) attend_subtile<KV>(q, ks, vs, n, scale, lane, mrun, l_run, o);
     }
+    if (l == 1) H4B_TRACE(1503);
 
     float4 result = make_float4(0.f, 0.f, 0.f, 0.f);
-    bool merged = false;
+    const long long pstride = kPartialStride;
+    unsigned long long* part = xw + a.x.part + static_cast<long long>(h) * kMkSplitCap * groups * pstride;
+    if (splits > 1 && split != 0) {
+        if (head_warp) {
+            unsigned long long* mine = part + (static_cast<long long>(split) * groups + warp) * pstride;
+            ll_store2(mine + 4 * lane, o.x, o.y, tag_part);
+            ll_store2(mine + 4 * lane + 2, o.z, o.w, tag_part);
+            if (lane == 0) ll_store2(mine + kHeadDim, mrun, l_run, tag_part);
+        }
+        return true;
+    }
     if (splits == 1) {
         if (head_warp) {
             const float inv = __fdiv_rn(1.0f, l_run);
             result = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
         }
-        merged = true;
-    } else {
-        const int stride = kPartialStride;
-        float* base = st.attn_partials + static_cast<long long>(h) * a.max_splits * groups * stride;
-        if (head_warp) {
-            float* mine = base + (static_cast<long long>(split) * groups + warp) * stride;
-            __stcg(reinterpret_cast<float4*>(mine + 4 * lane), o);
-            if (lane == 0) {
-                __stcg(mine + kHeadDim, mrun);
-                __stcg(mine + kHeadDim + 1, l_run);
+    } else if (head_warp) {
+        // Merge, split 0 from registers, the others polled: lane s holds
+        // (m, l) of splits s and s + 32.
+        const unsigned long long* mine = part + warp * pstride;
+        float ms[2] = {-INFINITY, -INFINITY}, ls[2] = {0.f, 0.f};
+        PollClock clk;
+        for (int r = 0; r < 2; ++r) {
+            const int sidx = lane + 32 * r;
+            if (sidx == 0) {
+                ms[r] = mrun;
+                ls[r] = l_run;
+            } else if (sidx < splits) {
+                const unsigned long long* p = mine + static_cast<long long>(sidx) * groups * pstride + kHeadDim;
+                ulonglong2 w = ll_load2(p);
+                while (ll_tag(w.x) != tag_part || ll_tag(w.y) != tag_part) {
+                    if (poll_expired(clk)) {
+                        ok = false;
+                        break;
+                    }
+                    w = ll_load2(p);
+                }
+                ms[r] = ll_value(w.x);
+                ls[r] = ll_value(w.y);
             }
         }
-        named_sync(1, kMkConsumers);
-        if (threadIdx.x == 0) {
-            __threadfence();
-            const uint32_t prev = atomicAdd(&a.attn_count[l * m.kv_heads + h], 1u);
-            flags[3] = (prev == static_cast<uint32_t>(splits - 1));
+        const float mmax = warp_max(fmaxf(ms[0], ms[1]));
+        float lsum = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        constexpr int kBatch = 4;
+        for (int s0 = 0; s0 < splits; s0 += kBatch) {
+            float4 ov[kBatch];
+            unsigned pending = 0;
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                const int sidx = s0 + j;
+                if (sidx == 0) ov[j] = o;
+                else if (sidx < splits) pending |= 1u << j;
+            }
+            PollClock oclk;
+            while (pending) {
+                ulonglong2 raw[kBatch][2];
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    if (pending & (1u << j)) {
+                        const unsigned long long* p = mine + static_cast<long long>(s0 + j) * groups * pstride + 4 * lane;
+                        raw[j][0] = ll_load2(p);
+                        raw[j][1] = ll_load2(p + 2);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < kBatch; ++j) {
+                    if ((pending & (1u << j)) && ll_tag(raw[j][0].x) == tag_part && ll_tag(raw[j][0].y) == tag_part &&
+                        ll_tag(raw[j][1].x) == tag_part && ll_tag(raw[j][1].y) == tag_part) {
+                        ov[j] = make_float4(ll_value(raw[j][0].x), ll_value(raw[j][0].y), ll_value(raw[j][1].x),
+                                            ll_value(raw[j][1].y));
+                        pending &= ~(1u << j);
+                    }
+                }
+                if (pending && poll_expired(oclk)) {
+                    ok = false;
+#pragma unroll
+                    for (int j = 0; j < kBatch; ++j)
+                        if (pending & (1u << j)) ov[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    break;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                const int sidx = s0 + j;
+                if (sidx >= splits) break;
+                const float lsj = __shfl_sync(0xffffffffu, sidx < 32 ? ls[0] : ls[1], sidx & 31);
+                const float msj = __shfl_sync(0xffffffffu, sidx < 32 ? ms[0] : ms[1], sidx & 31);
+                if (lsj == 0.f) continue;
+                const float w = exp_cw(msj - mmax);
+                lsum = __fmaf_rn(lsj, w, lsum);
+                acc.x = __fmaf_rn(ov[j].x, w, acc.x);
+                acc.y = __fmaf_rn(ov[j].y, w, acc.y);
+                acc.z = __fmaf_rn(ov[j].z, w, acc.z);
+                acc.w = __fmaf_rn(ov[j].w, w, acc.w);
+            }
         }
-        named_sync(1, kMkConsumers);
-        if (flags[3]) {
-            __threadfence();
-            if (head_warp) result = merge_splits(base + warp * stride, splits, groups * stride, lane);
-            merged = true;
-        }
+        const float inv = __fdiv_rn(1.0f, lsum);
+        result = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
     }
-    if (!merged) return;
+    if (mk_stop(flags, !ok)) return false;
+    if (l == 1) H4B_TRACE(1504);
     float mx = 0.f;
     if (head_warp) {
-        __stcg(reinterpret_cast<float4*>(st.attended + static_cast<long long>(qh) * d + 4 * lane), result);
+        unsigned long long* att = xw + a.x.att + static_cast<long long>(qh) * d + 4 * lane;
+        ll_store2(att, result.x, result.y, tag_att);
+        ll_store2(att + 2, result.z, result.w, tag_att);
         mx = warp_max(fmaxf(fmaxf(fabsf(result.x), fabsf(result.y)), fmaxf(fabsf(result.z), fabsf(result.w))));
     }
     if (lane == 0) red[warp] = head_warp ? mx : 0.f;
@@ -462,13 +725,15 @@ __device__ void mk_attention(const MkArgs& a, int l, int h, int split, int split
     if (threadIdx.x == 0) {
         float t = red[0];
         for (int w = 1; w < kMkWarps; ++w) t = fmaxf(t, red[w]);
-        atomic_max_nonneg(st.absmax + 2 * l, t);
+        ll_store(xw + a.x.att_max + h, t, tag_att);
     }
-    mk_signal(&a.ready[ph_attn(l)]);
+    named_sync(1, kMkConsumers);  // red is reused by the next phase
+    if (l == 1) H4B_TRACE(1505);
+    return true;
 }
 
 struct MkSmem {
-    int bars, red, xq, gamma, acc, scale, att, ring, total;
+    int bars, red, xq, gamma, consts, acc, scale, xo, att, ring, total;
 };
 
 __host__ __device__ inline MkSmem mk_smem_layout(int xq_bytes, int hidden, int rows_cap, int kv_bytes, int stages,
@@ -478,13 +743,79 @@ __host__ __device__ inline MkSmem mk_smem_layout(int xq_bytes, int hidden, int r
     s.red = 2 * kMkMaxStages * 8;
     s.xq = s.red + 64 * 4;
     s.gamma = s.xq + xq_region(xq_bytes);
-    s.acc = s.gamma + ((hidden * 4 + 127) & ~127);
-    s.scale = s.acc + rows_cap * 4;
-    s.att = (s.scale + rows_cap * 4 + 127) & ~127;
+    s.consts = s.gamma + ((hidden * 4 + 127) & ~127);  // attention's q/k norm weights + RoPE row
+    s.acc = s.consts + 3 * kHeadDim * 4;
+    s.scale = s.acc + rows_cap * 4;    // two buffers: this phase's row scales and the next one's
+    s.xo = s.scale + 2 * rows_cap * 4;  // this CTA's rows of x, kept across phases
+    s.att = (s.xo + rows_cap * 4 + 127) & ~127;
     const int att_bytes = 2 * kSubTile * kHeadDim * kv_bytes;
     s.ring = (s.att + (att_bytes > hidden * 4 ? att_bytes : hidden * 4) + 127) & ~127;
     s.total = s.ring + stages * slot_bytes + 512;  // slot loads may run up to 496 B past a tile
     return s;
+}
+
+// LM-head epilogue: logits, this CTA's greedy key as two exchange words,
+// then CTA 0 takes the max over every CTA's key and writes the step's token
+// and position (cpu_lightspark.py:704-705).
+__device__ void mk_finish_token(const MkArgs& a, const Seg& sg, const float* sc_s, float act, int32_t* acc_s,
+                                unsigned long long* xw, uint32_t tag_final, int pos, int* flags) {
+    const h4b_state& st = a.s;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int cta = blockIdx.x, nctas = gridDim.x;
+    unsigned long long best = 0ull;
+    for (int i = tid; i < sg.nrows; i += kMkConsumers) {
+        const float v = mk_value(acc_s, sc_s, i, act);
+        __stcg(st.logits + sg.r0 + i, v);
+        const unsigned long long k = argmax_key(v, static_cast<uint32_t>(sg.r0 + i));
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(acc_s);
+    named_sync(1, kMkConsumers);
+    if (lane == 0) keys[warp] = best;
+    named_sync(1, kMkConsumers);
+    if (tid == 0) {
+        for (int w = 0; w < kMkWarps; ++w) best = keys[w] > best ? keys[w] : best;
+        ll_store_raw2(xw + a.x.keys + 2 * cta, (static_cast<unsigned long long>(tag_final) << 32) | (best >> 32),
+                      (static_cast<unsigned long long>(tag_final) << 32) | (best & 0xFFFFFFFFull));
+    }
+    if (cta != 0) return;
+    named_sync(1, kMkConsumers);
+    bool failed = false;
+    best = 0ull;
+    for (int c = tid; c < nctas; c += kMkConsumers) {
+        const unsigned long long* p = xw + a.x.keys + 2 * c;
+        PollClock clk;
+        ulonglong2 w = ll_load2(p);
+        while (ll_tag(w.x) != tag_final || ll_tag(w.y) != tag_final) {
+            if (poll_expired(clk)) {
+                failed = true;
+                break;
+            }
+            w = ll_load2(p);
+        }
+        const unsigned long long k = ((w.x & 0xFFFFFFFFull) << 32) | (w.y & 0xFFFFFFFFull);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if (lane == 0) keys[warp] = best;
+    if (mk_stop(flags, failed)) return;
+    if (tid == 0) {
+        for (int w = 0; w < kMkWarps; ++w) best = keys[w] > best ? keys[w] : best;
+        *st.argmax_key = best;
+        const int32_t id = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
+        *st.next_token = id;
+        *st.token = id;
+        *st.position = pos + 1;
+    }
 }
 
 template <typename KV>
@@ -496,30 +827,39 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
     uint64_t* empty = full + kMkMaxStages;
     float* red = reinterpret_cast<float*>(smem + L.red);
-    int* flags = reinterpret_cast<int*>(red + 32);  // [0] stop request, [1] consumers' snapshot, [3] last split
+    int* flags = reinterpret_cast<int*>(red + 32);  // [0] stop request, [1] consumers' snapshot, [2] tag base
     int8_t* xq = reinterpret_cast<int8_t*>(smem + L.xq);
     float* gamma_s = reinterpret_cast<float*>(smem + L.gamma);
     int32_t* acc_s = reinterpret_cast<int32_t*>(smem + L.acc);
-    float* sc_s = reinterpret_cast<float*>(smem + L.scale);
+    float* sc_base = reinterpret_cast<float*>(smem + L.scale);
+    float* consts_s = reinterpret_cast<float*>(smem + L.consts);
+    float* xo = reinterpret_cast<float*>(smem + L.xo);
     KV* ks = reinterpret_cast<KV*>(smem + L.att);
     KV* vs = ks + kSubTile * kHeadDim;
     float* xs = reinterpret_cast<float*>(smem + L.att);  // embedding row, before any attention
     uint8_t* ring = smem + L.ring;
+    unsigned long long* xw = st.exchange;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int cta = blockIdx.x, nctas = gridDim.x;
     const int L_layers = m.layers, H = m.hidden;
     const int pos = *st.position;
     const int token = *st.token;
+    H4B_TRACE(0);
 
     if (tid == 0) {
+        // This CTA's launch counter advances on every launch, whatever happens
+        // later, so the tags of all CTAs stay in step.
+        unsigned long long* gen = xw + a.x.gen + cta;
+        const uint32_t g = static_cast<uint32_t>(*gen);
+        *gen = g + 1u;
+        flags[2] = static_cast<int>(mk_tag_base(g, L_layers));
         for (int s = 0; s < a.stages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);  // released by the owning consumer warp
         }
         flags[0] = wait_failed_before() ? 1 : 0;
         flags[1] = 0;
-        flags[3] = 0;
         if (pos < 0 || pos >= st.capacity) {
             if (cta == 0) report(kStatusBadPosition);
             flags[0] = 1;
@@ -528,6 +868,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
     }
     __syncthreads();
     if (flags[0]) return;  // before any bulk copy is issued
+    const uint32_t tbase = static_cast<uint32_t>(flags[2]);
 
     if (warp == kMkWarps) {
         // ---------------- producer warp: the whole token's weights ----------------
@@ -562,11 +903,15 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
     }
 
     // ---------------- consumer warps ----------------
+    // One pass per GEMV segment g (per layer: qkv, o, gate/up, down; then the
+    // LM head): prologue (RMSNorm or quantisation of the polled input), this
+    // segment's ring tiles, epilogue. Each routine has one call site.
     uint32_t seq = 0;
     const float eps = m.eps;
-    // Embedding (cpu_lightspark.py:341-349), computed by every CTA; the rows
-    // this CTA later updates (its o/down partition) also go to global x.
+    // Embedding (cpu_lightspark.py:341-349), computed by every CTA into xs;
+    // the rows this CTA owns in the o/down partition start its copy of x.
     {
+        const Seg so = mk_segment(a, SEG_O, cta, nctas);
         const bool ok = token >= 0 && token < m.vocab;
         if (!ok && cta == 0 && tid == 0) report(kStatusBadToken);
         const float scale = ok ? m.s_embed[token] : 0.f;
@@ -577,130 +922,80 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
             xs[2 * j + 1] = ok ? __fmul_rn(static_cast<float>(byte >> 4), scale) : 0.f;
         }
         mk_fetch_gamma(m.norm_in, gamma_s, H);
+        mk_fetch_scales(mk_segment(a, SEG_QKV, cta, nctas), sc_base);
         named_sync(1, kMkConsumers);
-        const Seg so = mk_segment(a, SEG_O, cta, nctas);
-        for (int i = tid; i < so.nrows; i += kMkConsumers) __stcg(st.x + so.r0 + i, xs[so.r0 + i]);
+        for (int i = tid; i < so.nrows; i += kMkConsumers) xo[i] = xs[so.r0 + i];
     }
 
-    const int kv_heads = m.kv_heads;
     const int ctx = pos + 1;
     const int splits = max(1, min(a.max_splits, (ctx + a.attn_chunk - 1) / a.attn_chunk));
-    const int items = kv_heads * splits;
+    const int items = m.kv_heads * splits;
+    const int last = 4 * L_layers;
 
-    for (int l = 0; l < L_layers; ++l) {
-        // ---- qkv: RMSNorm(x) -> quantise -> GEMV ----
-        Seg sg = mk_segment(a, 4 * l + SEG_QKV, cta, nctas);
-        mk_fetch_scales(sg, sc_s);
-        if (l > 0) {
-            mk_fetch_gamma(m.norm_in + static_cast<size_t>(l) * H, gamma_s, H);
-            if (!mk_wait(&a.ready[ph_down(l - 1)], nctas, flags)) return;
+    for (int g = 0; g <= last; ++g) {
+        const int l = g >> 2;
+        const int kind = g == last ? 4 : (g & 3);  // SEG_* or 4 = LM head
+        const uint32_t tl = tbase + kTagsPerLayer * l;
+        const Seg sg = mk_segment(a, g, cta, nctas);
+        const float* sc_s = sc_base + (g & 1) * a.rows_cap;
+        H4B_TRACE(8 + 3 * g);
+        async_copy_wait_all();  // this segment's scales (and gamma), fetched a segment ago
+
+        // ---- prologue ----
+        float act;
+        if (kind == SEG_O || kind == SEG_DOWN) {
+            const bool o = kind == SEG_O;
+            act = mk_prologue_quant(xw + (o ? a.x.att : a.x.act), xw + (o ? a.x.att_max : a.x.act_max),
+                                    o ? m.kv_heads : nctas, tl + (o ? TAG_ATT : TAG_ACT),
+                                    o ? m.heads * m.head_dim : m.intermediate, xq, red, flags);
+        } else {
+            // qkv reads x after the previous layer's down (layer 0: the
+            // embedding in xs), gate/up after this layer's o, the head after
+            // the last down.
+            const bool from_xs = g == 0;
+            const unsigned long long* src = xw + (kind == SEG_GATE_UP ? a.x.x_o : a.x.x_down);
+            const uint32_t tag = kind == SEG_GATE_UP ? tl + TAG_XO : tl - kTagsPerLayer + TAG_XDOWN;
+            act = mk_prologue_rms(from_xs ? xs : nullptr, from_xs ? nullptr : src, tag, gamma_s, H, eps, xq, red,
+                                  flags);
         }
-        async_copy_wait_all();
-        named_sync(1, kMkConsumers);
-        float act = mk_prologue_rms(l == 0 ? xs : st.x, l == 0, gamma_s, H, eps, xq, red);
+        mk_prefetch_next(a, g, cta, nctas, sc_base, gamma_s);
+        H4B_TRACE(8 + 3 * g + 1);
+
+        // ---- tiles ----
         mk_run_tiles(sg, seq, a.stages, a.slot_bytes, ring, full, empty, xq, acc_s, flags);
         seq += sg.ntiles;
+        H4B_TRACE(8 + 3 * g + 2);
         if (mk_stop(flags)) return;
-        for (int i = tid; i < sg.nrows; i += kMkConsumers) __stcg(st.qkv + sg.r0 + i, mk_value(acc_s, sc_s, i, act));
-        mk_signal(&a.ready[ph_qkv(l)]);
 
-        // ---- attention ----
-        if (!mk_wait(&a.ready[ph_qkv(l)], nctas, flags)) return;
-        if (cta < items) mk_attention<KV>(a, l, cta / splits, cta % splits, splits, pos, ks, vs, red, flags);
-
-        // ---- o: quantise(attended) -> GEMV -> residual ----
-        sg = mk_segment(a, 4 * l + SEG_O, cta, nctas);
-        mk_fetch_scales(sg, sc_s);
-        if (!mk_wait(&a.ready[ph_attn(l)], kv_heads, flags)) return;
-        async_copy_wait_all();
-        act = mk_prologue_quant(st.attended, st.absmax + 2 * l, m.heads * m.head_dim, xq);
-        mk_run_tiles(sg, seq, a.stages, a.slot_bytes, ring, full, empty, xq, acc_s, flags);
-        seq += sg.ntiles;
-        if (mk_stop(flags)) return;
-        for (int i = tid; i < sg.nrows; i += kMkConsumers)
-            __stcg(st.x + sg.r0 + i, __fadd_rn(__ldcg(st.x + sg.r0 + i), mk_value(acc_s, sc_s, i, act)));
-        mk_signal(&a.ready[ph_o(l)]);
-
-        // ---- gate/up: RMSNorm(x) -> quantise -> GEMV -> SwiGLU ----
-        sg = mk_segment(a, 4 * l + SEG_GATE_UP, cta, nctas);
-        mk_fetch_scales(sg, sc_s);
-        mk_fetch_gamma(m.norm_post + static_cast<size_t>(l) * H, gamma_s, H);
-        if (!mk_wait(&a.ready[ph_o(l)], nctas, flags)) return;
-        async_copy_wait_all();
-        named_sync(1, kMkConsumers);
-        act = mk_prologue_rms(st.x, false, gamma_s, H, eps, xq, red);
-        mk_run_tiles(sg, seq, a.stages, a.slot_bytes, ring, full, empty, xq, acc_s, flags);
-        seq += sg.ntiles;
-        if (mk_stop(flags)) return;
-        {
+        // ---- epilogue ----
+        if (kind == SEG_QKV) {
+            for (int i = tid; i < sg.nrows; i += kMkConsumers)
+                ll_store(xw + a.x.qkv + sg.r0 + i, mk_value(acc_s, sc_s, i, act), tl + TAG_QKV);
+            if (cta < items &&
+                !mk_attention<KV>(a, xw, tbase, l, cta / splits, cta % splits, splits, pos, ks, vs, consts_s, red,
+                                  flags))
+                return;
+        } else if (kind == SEG_O || kind == SEG_DOWN) {
+            const long long dst = kind == SEG_O ? a.x.x_o : a.x.x_down;
+            const uint32_t tag = tl + (kind == SEG_O ? TAG_XO : TAG_XDOWN);
+            for (int i = tid; i < sg.nrows; i += kMkConsumers) {
+                xo[i] = __fadd_rn(xo[i], mk_value(acc_s, sc_s, i, act));
+                ll_store(xw + dst + sg.r0 + i, xo[i], tag);
+            }
+        } else if (kind == SEG_GATE_UP) {
             float local = 0.f;
             for (int p = tid; p < (sg.nrows >> 1); p += kMkConsumers) {
                 const int b = p / kSwigluBlock, j = p % kSwigluBlock;
                 const int gi = 2 * kSwigluBlock * b + j;
                 const float gte = mk_value(acc_s, sc_s, gi, act), u = mk_value(acc_s, sc_s, gi + kSwigluBlock, act);
                 const float y = __fmul_rn(__fdiv_rn(gte, __fadd_rn(1.0f, exp_cw(-gte))), u);
-                __stcg(st.act + (sg.r0 >> 1) + p, y);
+                ll_store(xw + a.x.act + (sg.r0 >> 1) + p, y, tl + TAG_ACT);
                 local = fmaxf(local, fabsf(y));
             }
             const float mx = group_max(local, red, kMkWarps, 1);
-            if (tid == 0) atomic_max_nonneg(st.absmax + 2 * l + 1, mx);
-        }
-        mk_signal(&a.ready[ph_gate_up(l)]);
-
-        // ---- down: quantise(act) -> GEMV -> residual ----
-        sg = mk_segment(a, 4 * l + SEG_DOWN, cta, nctas);
-        mk_fetch_scales(sg, sc_s);
-        if (!mk_wait(&a.ready[ph_gate_up(l)], nctas, flags)) return;
-        async_copy_wait_all();
-        act = mk_prologue_quant(st.act, st.absmax + 2 * l + 1, m.intermediate, xq);
-        mk_run_tiles(sg, seq, a.stages, a.slot_bytes, ring, full, empty, xq, acc_s, flags);
-        seq += sg.ntiles;
-        if (mk_stop(flags)) return;
-        for (int i = tid; i < sg.nrows; i += kMkConsumers)
-            __stcg(st.x + sg.r0 + i, __fadd_rn(__ldcg(st.x + sg.r0 + i), mk_value(acc_s, sc_s, i, act)));
-        mk_signal(&a.ready[ph_down(l)]);
-    }
-
-    // ---- LM head: RMSNorm(x) -> quantise -> GEMV -> logits + argmax ----
-    const Seg sg = mk_segment(a, 4 * L_layers, cta, nctas);
-    mk_fetch_scales(sg, sc_s);
-    mk_fetch_gamma(m.norm_final, gamma_s, H);
-    if (!mk_wait(&a.ready[ph_down(L_layers - 1)], nctas, flags)) return;
-    async_copy_wait_all();
-    named_sync(1, kMkConsumers);
-    const float act = mk_prologue_rms(st.x, false, gamma_s, H, eps, xq, red);
-    mk_run_tiles(sg, seq, a.stages, a.slot_bytes, ring, full, empty, xq, acc_s, flags);
-    if (mk_stop(flags)) return;
-    unsigned long long best = 0ull;
-    for (int i = tid; i < sg.nrows; i += kMkConsumers) {
-        const float v = mk_value(acc_s, sc_s, i, act);
-        __stcg(st.logits + sg.r0 + i, v);
-        const unsigned long long k = argmax_key(v, static_cast<uint32_t>(sg.r0 + i));
-        best = k > best ? k : best;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-        best = other > best ? other : best;
-    }
-    unsigned long long* keys = reinterpret_cast<unsigned long long*>(acc_s);
-    named_sync(1, kMkConsumers);
-    if (lane == 0) keys[warp] = best;
-    named_sync(1, kMkConsumers);
-    if (tid == 0) {
-        for (int w = 0; w < kMkWarps; ++w) best = keys[w] > best ? keys[w] : best;
-        atomicMax(st.argmax_key, best);
-    }
-    const int final_phase = 5 * L_layers;
-    mk_signal(&a.ready[final_phase]);
-    if (cta == 0) {
-        if (!mk_wait(&a.ready[final_phase], nctas, flags)) return;
-        if (tid == 0) {
-            const unsigned long long key = atomicAdd(st.argmax_key, 0ull);
-            const int32_t id = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
-            *st.next_token = id;
-            *st.token = id;
-            *st.position = pos + 1;
+            if (tid == 0) ll_store(xw + a.x.act_max + cta, mx, tl + TAG_ACT);
+        } else {
+            mk_finish_token(a, sg, sc_s, act, acc_s, xw, tl, pos, flags);
         }
     }
 }
@@ -717,21 +1012,21 @@ int mk_splits_max(const h4b_model* m) {
 static int plan_persistent(const h4b_model* m, const h4b_state* s, MkPlan* p) {
     int rc = validate(m, s);
     if (rc) return rc;
-    if (!s->sync || (reinterpret_cast<uintptr_t>(s->sync) & 15) || !s->attn_partials) return H4B_EINVAL;
-    if (m->hidden > kMkMaxHidden) return H4B_EUNSUPPORTED;
+    if (!s->exchange || (reinterpret_cast<uintptr_t>(s->exchange) & 15)) return H4B_EINVAL;
+    if (m->hidden > kMkMaxHidden || m->hidden % 8 || m->intermediate % 8) return H4B_EUNSUPPORTED;
     const int q_size = m->heads * m->head_dim;
     const int max_width = std::max(m->hidden, std::max(q_size, m->intermediate));
     if (max_width > kMkMaxWidth) return H4B_EUNSUPPORTED;
+    const int nctas = sm_count();
+    if (nctas > kMkMaxCtas) return H4B_EUNSUPPORTED;
     MkArgs& a = p->args;
     a = MkArgs{};
     a.m = *m;
     a.s = *s;
-    a.ready = s->sync;
-    a.attn_count = s->sync + 5 * m->layers + 2;
+    a.x = x_layout(*m);
     a.attn_chunk = 32;
     a.max_splits = mk_splits_max(m);
     a.xq_bytes = max_width;
-    const int nctas = sm_count();
     // Rows one CTA owns in any segment, plus one partition unit of slack.
     const int biggest = std::max({m->vocab, 2 * m->intermediate, q_size + 2 * m->kv_heads * m->head_dim, m->hidden});
     a.rows_cap = ((biggest + nctas - 1) / nctas + 2 * kSwigluBlock + 31) & ~31;
@@ -761,10 +1056,6 @@ int decode_persistent(const h4b_model* m, const h4b_state* s, cudaStream_t strea
     MkPlan p;
     int rc = plan_persistent(m, s, &p);
     if (rc) return rc;
-    const size_t sync_words = static_cast<size_t>(5 * m->layers + 2) + static_cast<size_t>(m->layers) * m->kv_heads;
-    H4B_CUDA_TRY(cudaMemsetAsync(s->sync, 0, sync_words * sizeof(uint32_t), stream));
-    H4B_CUDA_TRY(cudaMemsetAsync(s->absmax, 0, 2 * m->layers * sizeof(float), stream));
-    H4B_CUDA_TRY(cudaMemsetAsync(s->argmax_key, 0, sizeof(unsigned long long), stream));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sm_count());
     cfg.blockDim = dim3(kMkThreads);
@@ -782,6 +1073,20 @@ int decode_persistent(const h4b_model* m, const h4b_state* s, cudaStream_t strea
 
 }  // namespace h4b
 
+#ifdef H4B_PHASE_TRACE
+// Copies the phase timeline (3 x 2048 u64) of the last traced launch to host.
+extern "C" int h4b_phase_trace(unsigned long long* host) {
+    H4B_CUDA_TRY(cudaDeviceSynchronize());
+    H4B_CUDA_TRY(cudaMemcpyFromSymbol(host, h4b::g_phase_trace, sizeof(unsigned long long) * 3 * 2048));
+    return 0;
+}
+#endif
+
 extern "C" int h4b_decode_persistent(const h4b_model* model, const h4b_state* state, void* stream) {
     return h4b::decode_persistent(model, state, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" long long h4b_persistent_exchange_words(const h4b_model* model) {
+    if (!model || model->layers < 1 || model->kv_heads < 1 || model->heads % model->kv_heads) return H4B_EINVAL;
+    return h4b::x_layout(*model).total;
 }

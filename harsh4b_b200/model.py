@@ -82,7 +82,7 @@ class CudaDecodeState:
         self.k_cache = torch.zeros(shape, dtype=kv_torch, device=dev)
         self.v_cache = torch.zeros(shape, dtype=kv_torch, device=dev)
         self.splits = int(attn_splits or model.attn_splits)
-        partial_splits = max(self.splits, model.max_persistent_splits)
+        partial_splits = self.splits
         i32 = dict(dtype=torch.int32, device=dev)
         f32 = dict(dtype=torch.float32, device=dev)
         self.position_dev = torch.zeros(1, **i32)
@@ -97,11 +97,14 @@ class CudaDecodeState:
         self.argmax_key = torch.zeros(1, dtype=torch.int64, device=dev)
         self.partials = torch.zeros(model.kv_heads * partial_splits * model.groups * (model.head_dim + 4), **f32)
         self.counters = torch.zeros(model.kv_heads, **i32)
-        self.sync = torch.zeros(5 * model.n_layers + 2 + model.n_layers * model.kv_heads, **i32)
+        words = lib().h4b_persistent_exchange_words(ctypes.byref(model.desc))
+        if words < 0:
+            check(int(words), "h4b_persistent_exchange_words")
+        self.exchange = torch.zeros(int(words), dtype=torch.int64, device=dev)
         self.desc = StateDesc(self.capacity, code, self.splits, *[t.data_ptr() for t in (
             self.k_cache, self.v_cache, self.position_dev, self.token_dev, self.next_token_dev, self.x, self.qkv,
             self.attended, self.act, self.logits, self.absmax, self.argmax_key, self.partials, self.counters,
-            self.sync)])
+            self.exchange)])
         check(lib().h4b_validate(ctypes.byref(model.desc), ctypes.byref(self.desc)), "h4b_validate")
         self.stream = torch.cuda.Stream(device=dev)
         self._token_host = torch.zeros(1, dtype=torch.int32).pin_memory()
@@ -160,6 +163,7 @@ class CudaDecodeState:
         self.stream.synchronize()
         self.position = 0
         self.position_dev.zero_()
+        self.exchange.zero_()  # also recovers the persistent step after a failed token
         torch.cuda.synchronize(self.model.device)
 
 

@@ -150,9 +150,10 @@ typedef struct h4b_state {
     unsigned long long *argmax_key;
     float *attn_partials;
     int *attn_counters;
-    /* Persistent decode only: (5 * layers + 2) + layers * kv_heads uint32
-     * phase counters, zeroed by the step itself before each token. */
-    uint32_t *sync;
+    /* Persistent decode only: h4b_persistent_exchange_words(model) 64-bit
+     * words, 16-byte aligned, zeroed when the session is created and never
+     * cleared afterwards (they carry their own tags). */
+    unsigned long long *exchange;
 } h4b_state;
 
 /* Checks the shapes/pointers of a model + state pair against what the
@@ -172,14 +173,20 @@ int h4b_decode_step(const h4b_model *model, const h4b_state *state, void *stream
  * argmax, 7 finalize (next_token, position += 1). */
 int h4b_decode_stage(const h4b_model *model, const h4b_state *state, int stage, int layer, void *stream);
 
-/* The same token as ONE cooperative kernel, one CTA per SM (preceded by a
- * memset of state->sync, absmax and argmax_key). A producer warp per SM
- * streams that SM's rows of every weight matrix for the whole token through
- * a shared-memory ring with bulk copies, never waiting on activations;
- * consumer warps wait on release/acquire phase counters between the 5 phases
- * of each layer (bounded waits: a timeout sets status bit 1 and every CTA
- * stops). Needs state->sync. Capturable in a CUDA graph. */
+/* The same token as ONE cooperative kernel, one CTA per SM, with no other
+ * launch or memset. A producer warp per SM streams that SM's rows of every
+ * weight matrix for the whole token through a shared-memory ring with bulk
+ * copies, never waiting on activations. Consumer warps hand activations to
+ * each other through state->exchange: every value is a 64-bit word
+ * {tag, fp32} stored without a fence, and readers poll the words until the
+ * tag of this launch and phase appears (bounded: a timeout sets status bit 1
+ * and every CTA stops; after a failed step re-zero the exchange). Attention
+ * splits merge the same way. Capturable in a CUDA graph. */
 int h4b_decode_persistent(const h4b_model *model, const h4b_state *state, void *stream);
+
+/* Size in 64-bit words of state->exchange for h4b_decode_persistent
+ * (< 0: H4B_EINVAL for an inconsistent model). */
+long long h4b_persistent_exchange_words(const h4b_model *model);
 
 /* Captures h4b_decode_step into a CUDA graph bound to (model, state) and
  * instantiates it; *graph_out is an opaque handle. */

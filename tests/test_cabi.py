@@ -13,7 +13,7 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "harsh4b_b200.h"
 
 def declared_functions():
     text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
-    return sorted(set(re.findall(r"^\s*int\s+(h4b_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|long long)\s+(h4b_\w+)\s*\(", text, flags=re.M)))
 
 
 def test_header_declares_the_bound_entry_points():
