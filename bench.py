@@ -33,9 +33,12 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "batch-1 decode tok/s Qwen3-4B int4; body-GEMV HBM GB/s vs ~8 TB/s"
 PROMPT = 128
-# dram__bytes_read.sum + dram__bytes_write.sum per body-GEMV launch from the
-# ncu capture summarised in profiles/gemv_body_config0.md (None until captured).
-NCU_TRAFFIC_PER_BYTE = None
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic
+# byte, from the ncu captures summarised under profiles/: the persistent
+# decode kernel on a 4-layer Qwen3-4B-shaped model (weights + LM head +
+# KV), and the body GEMV kernel. Traffic grows in proportion to the bytes
+# streamed, so the ratio scales a launch of the full model.
+NCU_TRAFFIC_PER_BYTE = {"persistent": 1.0213, "gemv": None}
 
 
 def parse_args():
@@ -155,8 +158,8 @@ def body_gemv_roofline(torch, model, state, peak_gbs) -> dict:
     launches = 4 * model.n_layers
     achieved = body_bytes / body_s / 1e9
     traffic = None
-    if NCU_TRAFFIC_PER_BYTE is not None:
-        traffic = round(body_bytes / launches * NCU_TRAFFIC_PER_BYTE)
+    if NCU_TRAFFIC_PER_BYTE["gemv"] is not None:
+        traffic = round(body_bytes / launches * NCU_TRAFFIC_PER_BYTE["gemv"])
     return {"bound": "hbm", "kernel": "gemv_kernel (body: qkv, o, gate/up, down)",
             "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s", "frac": round(achieved / peak_gbs, 4),
             "traffic": traffic, "bytes_per_launch": round(body_bytes / launches),
@@ -320,8 +323,7 @@ def run_ours(args, rank, world, local_rank, dist) -> int:
     roof_state = model.new_state(capacity)
     for token_id in prompt[:4]:
         model.forward_token(token_id, roof_state)
-    roofline = body_gemv_roofline(torch, model, roof_state, peaks["hbm_gbs"])
-    roofline["peak_source"] = peaks["source"]
+    gemv_alone = body_gemv_roofline(torch, model, roof_state, peaks["hbm_gbs"])
     state.close(); e2e_state.close(); roof_state.close()
 
     times = torch.tensor([elapsed, e2e_elapsed], dtype=torch.float64, device=device)
@@ -331,7 +333,20 @@ def run_ours(args, rank, world, local_rank, dist) -> int:
     if rank != 0:
         return 0
     value = world * args.steps / elapsed
-    bytes_per_token = model.weight_bytes + model.n_layers * 2 * model.kv_size * 2 * (PROMPT + args.warmup + args.steps // 2)
+    kv_bytes = 2 if args.kv_dtype == "float16" else 4
+    bytes_per_token = model.weight_bytes + model.n_layers * 2 * model.kv_size * kv_bytes * (
+        PROMPT + args.warmup + args.steps // 2)
+    if args.mode == "persistent":
+        # One kernel launch per token: its algorithmic bytes over its event-timed duration.
+        achieved = bytes_per_token * args.steps / elapsed / 1e9
+        ratio = NCU_TRAFFIC_PER_BYTE["persistent"]
+        roofline = {"bound": "hbm", "kernel": "decode_persistent_kernel (whole token)", "achieved": round(achieved, 1),
+                    "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                    "traffic": round(bytes_per_token * ratio) if ratio else None, "bytes_per_launch": bytes_per_token,
+                    "avg_launch_us": round(elapsed / args.steps * 1e6, 2), "launches": args.steps,
+                    "peak_source": peaks["source"], "gemv_isolated": gemv_alone}
+    else:
+        roofline = dict(gemv_alone, peak_source=peaks["source"])
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1000, 4), "higher_is_better": True,

@@ -27,11 +27,31 @@
 
 namespace h4b {
 
+// Timeline points inside the sub-tile math (phase-trace builds only; the
+// persistent kernel sets g_trace_attn around one layer's attention).
+#ifdef H4B_PHASE_TRACE
+__device__ int g_trace_attn;
+#define H4B_TRACE_ATTN(ev) do { if (g_trace_attn) H4B_TRACE(ev); } while (0)
+#else
+#define H4B_TRACE_ATTN(ev) do { } while (0)
+#endif
+
 constexpr int kHeadDim = 128;  // 4 values per lane
 // One split result per q head: o[128], m, l, 2 pad floats, so every float4
 // store stays 16-byte aligned.
 constexpr int kPartialStride = kHeadDim + 4;
 constexpr int kSubTile = 64;  // tokens staged per pass
+constexpr int kMaxGroups = 8;  // q heads per kv head (one warp each)
+
+// Staged K/V rows are padded by 16 bytes so that lanes reading different
+// rows at the same column (one token per lane) hit different bank groups.
+template <typename KV>
+__host__ __device__ constexpr int kv_row_stride() { return kHeadDim + 16 / static_cast<int>(sizeof(KV)); }
+// Shared memory of one staged sub-tile: K and V rows, then one q head per warp.
+template <typename KV>
+__host__ __device__ constexpr int subtile_smem_bytes() {
+    return 2 * kSubTile * kv_row_stride<KV>() * static_cast<int>(sizeof(KV)) + kMaxGroups * kHeadDim * 4;
+}
 
 struct AttnArgs {
     const float* q;       // [batch][q_heads][d]  (qkv buffer in the decode path)
@@ -85,6 +105,25 @@ __device__ __forceinline__ void store4<__half>(__half* p, float4 v) {
     raw.x = *reinterpret_cast<const uint32_t*>(&a);
     raw.y = *reinterpret_cast<const uint32_t*>(&b);
     *reinterpret_cast<uint2*>(p) = raw;
+}
+
+// Eight consecutive K values (16 bytes) as two float4s.
+template <typename KV>
+__device__ __forceinline__ void load8kv(const KV* p, float4& a, float4& b);
+template <>
+__device__ __forceinline__ void load8kv<float>(const float* p, float4& a, float4& b) {
+    a = *reinterpret_cast<const float4*>(p);
+    b = *reinterpret_cast<const float4*>(p + 4);
+}
+template <>
+__device__ __forceinline__ void load8kv<__half>(const __half* p, float4& a, float4& b) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const float2 x0 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+    const float2 x1 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+    const float2 x2 = __half22float2(*reinterpret_cast<const __half2*>(&raw.z));
+    const float2 x3 = __half22float2(*reinterpret_cast<const __half2*>(&raw.w));
+    a = make_float4(x0.x, x0.y, x1.x, x1.y);
+    b = make_float4(x2.x, x2.y, x3.x, x3.y);
 }
 
 __device__ __forceinline__ float dot4(float4 a, float4 b) {
@@ -213,20 +252,34 @@ __device__ __forceinline__ void stage_subtile(const KV* kc, const KV* vc, long l
         const int r = rest / kRowVecs, piece = rest % kRowVecs;
         if (base + r == skip) continue;
         const KV* src = (which ? vc : kc) + static_cast<long long>(base + r) * time_stride;
-        async_copy16(reinterpret_cast<uint4*>((which ? vs : ks) + r * kHeadDim) + piece,
+        async_copy16(reinterpret_cast<uint4*>((which ? vs : ks) + r * kv_row_stride<KV>()) + piece,
                      reinterpret_cast<const uint4*>(src) + piece);
     }
 }
 
-// Folds one staged sub-tile (n <= kSubTile tokens in ks/vs) into a q head's
-// running (m, l, o): scores 32 tokens per round (lane l ends with token
-// 32 r + l), a two-pass softmax over the sub-tile, p * v accumulated in token
-// order, then the running merge. The p * v loop is unrolled over whole
-// rounds; tokens past n add p = 0 times a staged row, which leaves every
-// partial sum unchanged.
+// Folds one staged sub-tile (n <= kSubTile tokens in ks/vs, rows padded to
+// kv_row_stride) into a q head's running (m, l, o).
+//
+// Scores: the score of a token is the sum of 32 dot4 partials (dims
+// 4c..4c+3) added in the pairing order of a warp butterfly sum. Here lane
+// (i = lane / 8, t = lane % 8) keeps the 8 q groups c = i + 4j in registers
+// and, for token 8 s + t of each step s, forms the partials of its groups,
+// adds them through the first three butterfly levels (c^16, c^8, c^4 stay
+// inside the lane), and finishes the last two (c^2, c^1) with shuffles
+// across lanes 16 and 8 apart -- the same bits as 32 lanes holding one
+// group each, with 8x less shared-memory traffic for q. Lane l of round r
+// ends with token 32 r + l. Then a two-pass softmax over the sub-tile,
+// p * v accumulated in token order (4 dims per lane) and the running merge.
+// Tokens past n add p = 0 times a staged row, which leaves every partial
+// sum unchanged.
 template <typename KV>
-__device__ __forceinline__ void attend_subtile(float4 q, const KV* ks, const KV* vs, int n, float scale, int lane,
-                                               float& m, float& l, float4& o) {
+__device__ __forceinline__ void attend_subtile(const float* qs, const KV* ks, const KV* vs, int n, float scale,
+                                               int lane, float& m, float& l, float4& o) {
+    constexpr int S = kv_row_stride<KV>();
+    const int qi = lane >> 3, tl = lane & 7;
+    float4 qv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) qv[j] = *reinterpret_cast<const float4*>(qs + 4 * (qi + 4 * j));
     float p_round[2];
     float mt = -INFINITY;
 #pragma unroll
@@ -235,20 +288,28 @@ __device__ __forceinline__ void attend_subtile(float4 q, const KV* ks, const KV*
             p_round[r] = -INFINITY;
             continue;
         }
-        float part[32];
+        float mine = 0.f;
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-            const int tt = min(32 * r + t, n - 1);
-            part[t] = dot4(q, load4<KV>(ks + tt * kHeadDim + 4 * lane));
+        for (int st = 0; st < 4; ++st) {
+            const KV* krow = ks + min(32 * r + 8 * st + tl, n - 1) * S + 4 * qi;
+            float p[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) p[j] = dot4(qv[j], load4<KV>(krow + 16 * j));
+            const float s3 = ((p[0] + p[4]) + (p[2] + p[6])) + ((p[1] + p[5]) + (p[3] + p[7]));
+            const float s4 = s3 + __shfl_xor_sync(0xffffffffu, s3, 16);
+            const float s5 = s4 + __shfl_xor_sync(0xffffffffu, s4, 8);
+            if (st == qi) mine = s5;
         }
-        const float sc = __fmul_rn(transpose_reduce32(part, lane), scale);
+        const float sc = __fmul_rn(mine, scale);
         p_round[r] = (32 * r + lane < n) ? sc : -INFINITY;
         mt = fmaxf(mt, p_round[r]);
     }
+    H4B_TRACE_ATTN(1510);
     mt = warp_max(mt);
 #pragma unroll
     for (int r = 0; r < 2; ++r) p_round[r] = (32 * r + lane < n) ? exp_cw(p_round[r] - mt) : 0.f;
     const float lt = warp_sum(p_round[0] + p_round[1]);
+    H4B_TRACE_ATTN(1511);
     float4 ot = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
@@ -256,13 +317,14 @@ __device__ __forceinline__ void attend_subtile(float4 q, const KV* ks, const KV*
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
             const float p = __shfl_sync(0xffffffffu, p_round[r], t);
-            const float4 v = load4<KV>(vs + min(32 * r + t, n - 1) * kHeadDim + 4 * lane);
+            const float4 v = load4<KV>(vs + min(32 * r + t, n - 1) * S + 4 * lane);
             ot.x = __fmaf_rn(p, v.x, ot.x);
             ot.y = __fmaf_rn(p, v.y, ot.y);
             ot.z = __fmaf_rn(p, v.z, ot.z);
             ot.w = __fmaf_rn(p, v.w, ot.w);
         }
     }
+    H4B_TRACE_ATTN(1512);
     const float mn = fmaxf(m, mt);
     const float c_old = exp_cw(m - mn), c_new = exp_cw(mt - mn);
     l = __fmaf_rn(l, c_old, __fmul_rn(lt, c_new));
@@ -277,7 +339,8 @@ template <typename KV>
 __global__ void __launch_bounds__(256) gqa_split_kernel(const AttnArgs a) {
     extern __shared__ __align__(16) uint8_t attn_smem[];
     KV* ks = reinterpret_cast<KV*>(attn_smem);
-    KV* vs = ks + kSubTile * kHeadDim;
+    KV* vs = ks + kSubTile * kv_row_stride<KV>();
+    float* qs = reinterpret_cast<float*>(vs + kSubTile * kv_row_stride<KV>()) + (threadIdx.x >> 5) * kHeadDim;
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = kvh * a.groups + warp;
@@ -300,6 +363,7 @@ __global__ void __launch_bounds__(256) gqa_split_kernel(const AttnArgs a) {
     const float* sn = a.rope_sin ? a.rope_sin + static_cast<long long>(pos) * (kHeadDim / 2) : nullptr;
     float4 q = *reinterpret_cast<const float4*>(qb + static_cast<long long>(h) * kHeadDim + 4 * lane);
     q = norm_rope(q, a.q_norm, cs, sn, a.eps, lane);
+    *reinterpret_cast<float4*>(qs + 4 * lane) = q;  // read by every lane in attend_subtile
 
     KV* kc = static_cast<KV*>(a.kcache) + b * a.batch_stride + kvh * a.head_stride;
     KV* vc = static_cast<KV*>(a.vcache) + b * a.batch_stride + kvh * a.head_stride;
@@ -328,12 +392,12 @@ __global__ void __launch_bounds__(256) gqa_split_kernel(const AttnArgs a) {
         __syncthreads();  // the previous sub-tile is consumed
         stage_subtile<KV>(kc, vc, a.time_stride, base, n, owns_new ? pos : -1, ks, vs, threadIdx.x, blockDim.x);
         if (owns_new && pos >= base && pos < base + n) {
-            if (warp == 0) store4<KV>(ks + (pos - base) * kHeadDim + 4 * lane, k_new);
-            if (warp == a.groups - 1) store4<KV>(vs + (pos - base) * kHeadDim + 4 * lane, v_new);
+            if (warp == 0) store4<KV>(ks + (pos - base) * kv_row_stride<KV>() + 4 * lane, k_new);
+            if (warp == a.groups - 1) store4<KV>(vs + (pos - base) * kv_row_stride<KV>() + 4 * lane, v_new);
         }
         async_copy_wait_all();
         __syncthreads();
-        attend_subtile<KV>(q, ks, vs, n, scale, lane, m, l, o);
+        attend_subtile<KV>(qs, ks, vs, n, scale, lane, m, l, o);
     }
 
     float* out_h = a.out + b * a.out_batch_stride + static_cast<long long>(h) * kHeadDim;
@@ -401,11 +465,11 @@ __global__ void __launch_bounds__(256) gqa_merge_kernel(const AttnArgs a) {
 }
 
 int launch_attention(const AttnArgs& a, int kv_dtype, int batch, cudaStream_t stream, bool pdl) {
-    if (a.groups < 1 || a.groups > 8 || a.splits < 1 || a.kv_heads < 1 || batch < 1) return H4B_EINVAL;
+    if (a.groups < 1 || a.groups > kMaxGroups || a.splits < 1 || a.kv_heads < 1 || batch < 1) return H4B_EINVAL;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.splits, a.kv_heads, batch);
     cfg.blockDim = dim3(32 * a.groups);
-    cfg.dynamicSmemBytes = 2 * kSubTile * kHeadDim * (kv_dtype == 0 ? 4 : 2);
+    cfg.dynamicSmemBytes = kv_dtype == 0 ? subtile_smem_bytes<float>() : subtile_smem_bytes<__half>();
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

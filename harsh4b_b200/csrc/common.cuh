@@ -57,12 +57,19 @@ __device__ __forceinline__ int trace_slot() {
     do {                                             \
         if (threadIdx.x == 0) H4B_TRACE_ANY(ev);     \
     } while (0)
+// Per-CTA timestamps (all CTAs): g_phase_all[cta][ev], ev < 16.
+__device__ unsigned long long g_phase_all[1024][16];
+#define H4B_TRACE_CTA(ev)                                                                    \
+    do {                                                                                     \
+        if (threadIdx.x == 0) ::h4b::g_phase_all[blockIdx.x][(ev)] = ::h4b::globaltimer_ns(); \
+    } while (0)
 #define H4B_TRACE_VAL(ev, val)                                                           \
     do {                                                                                 \
         const int _s = ::h4b::trace_slot();                                              \
         if (_s >= 0) ::h4b::g_phase_trace[_s][(ev)] = static_cast<unsigned long long>(val); \
     } while (0)
 #else
+#define H4B_TRACE_CTA(ev) do { } while (0)
 #define H4B_TRACE_VAL(ev, val) do { } while (0)
 #define H4B_TRACE_ANY(ev) do { } while (0)
 #define H4B_TRACE(ev) do { } while (0)

@@ -238,7 +238,7 @@ int prepare_other_kernels() {
     int r = 0;
     if ((r = prepare_persistent())) return r;
     if ((r = cudaFuncSetAttribute(gqa_split_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  2 * kSubTile * kHeadDim * 4)))
+                                  subtile_smem_bytes<float>())))
         return r;
     if ((r = set_carveout(gqa_split_kernel<float>)) || (r = set_carveout(gqa_split_kernel<__half>)) ||
         (r = set_carveout(gqa_merge_kernel)) || (r = set_carveout(embed_kernel)) ||

@@ -85,6 +85,7 @@ struct MkArgs {
     int slot_bytes;        // ring slot size (a tile is at most one slot)
     int attn_chunk;        // target tokens per attention split
     int max_splits;        // splits per kv head at most
+    int stage_splits;      // splits whose partials fit the K/V staging area
     int xq_bytes, rows_cap;
 };
 
@@ -165,26 +166,6 @@ __device__ void mk_poll_lane(const unsigned long long* w, int lane_id, int group
         if (lane_id + k * kRmsLanes < groups) pending |= 1u << k;
     PollClock clk;
     while (pending) {
-        if (clk.rounds != 0) {
-            // Data not complete yet: watch one word per pending group
-            // (little L2 traffic) before loading the groups again.
-            bool seen = true;
-#pragma unroll
-            for (int k = 0; k < G; ++k)
-                if (pending & (1u << k)) seen = seen && ll_tag(ll_load(w + 8 * (lane_id + k * kRmsLanes) + 7)) == tag;
-            if (!seen) {
-                if (poll_expired(clk)) {
-                    atomicOr(&flags[0], 1);
-#pragma unroll
-                    for (int k = 0; k < G; ++k)
-                        if (pending & (1u << k))
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) v[k][e] = 0.f;
-                    return;
-                }
-                continue;
-            }
-        }
         ulonglong2 raw[G][4];
 #pragma unroll
         for (int k = 0; k < G; ++k) {
@@ -251,7 +232,7 @@ __device__ float mk_poll_max(const unsigned long long* w, int n, uint32_t tag, i
 // embedding row in shared memory (xs) or exchange words carrying `tag`.
 template <int G>
 __device__ float mk_prologue_rms_g(const float* xs, const unsigned long long* xw, uint32_t tag, const float* gamma_s,
-                                   int n, float eps, int8_t* xq, float* red, int* flags) {
+                                   int n, float eps, int8_t* xq, float* red, int* flags, int trace_ev) {
     const int tid = threadIdx.x, warp = tid >> 5;
     const int groups = n >> 3;
     const bool extra = tid + kMkConsumers < kRmsLanes;  // warp 0: also lane tid + kMkConsumers
@@ -262,6 +243,7 @@ __device__ float mk_prologue_rms_g(const float* xs, const unsigned long long* xw
         if (r == 1 && !extra) break;
         if (xw) {
             mk_poll_lane<G>(xw, lane_id, groups, tag, v[r], flags);
+            if (trace_ev >= 0) H4B_TRACE_ANY(trace_ev);
         } else {
 #pragma unroll
             for (int k = 0; k < G; ++k) {
@@ -333,72 +315,71 @@ __device__ float mk_prologue_rms_g(const float* xs, const unsigned long long* xw
 }
 
 __device__ float mk_prologue_rms(const float* xs, const unsigned long long* xw, uint32_t tag, const float* gamma_s,
-                                 int n, float eps, int8_t* xq, float* red, int* flags) {
-    return mk_prologue_rms_g<kMkMaxHidden / (8 * kRmsLanes)>(xs, xw, tag, gamma_s, n, eps, xq, red, flags);
+                                 int n, float eps, int8_t* xq, float* red, int* flags, int trace_ev = -1) {
+    return mk_prologue_rms_g<kMkMaxHidden / (8 * kRmsLanes)>(xs, xw, tag, gamma_s, n, eps, xq, red, flags, trace_ev);
 }
 
 // Quantisation of n exchange words carrying `tag` with the absmax over the
-// nmax partial maxima its producers published (also tagged `tag`). Groups
-// g = tid + k * kMkConsumers of 8 words are loaded kMkQuantGroups at a time
-// and quantised as soon as their tags check.
-constexpr int kMkQuantGroups = 4;
+// nmax partial maxima its producers published (also tagged `tag`). Each
+// thread loads its maxima word(s) and all its 8-word groups
+// (g = tid + k * kMkConsumers, k < kMkQuantGroups) in every polling round,
+// so the whole handoff costs one L2 round trip once the data is there.
+constexpr int kMkQuantGroups = 6;  // covers 6 * 8 * 224 = 10752 values
 __device__ float mk_prologue_quant(const unsigned long long* vw, const unsigned long long* maxw, int nmax, uint32_t tag,
-                                   int n, int8_t* xq, float* red, int* flags) {
+                                   int n, int8_t* xq, float* red, int* flags, int trace_ev = -1) {
     const int tid = threadIdx.x;
     const int groups = n >> 3;
-    const float m = group_max(mk_poll_max(maxw, nmax, tag, flags), red, kMkWarps, 1);
+    unsigned pending = 0;
+#pragma unroll
+    for (int k = 0; k < kMkQuantGroups; ++k)
+        if (tid + k * kMkConsumers < groups) pending |= 1u << k;
+    const bool has_max = tid < nmax;  // nmax <= kMkConsumers (checked on the host)
+    bool max_done = !has_max;
+    float mx = 0.f;
+    ulonglong2 raw[kMkQuantGroups][4];  // the words themselves hold the values once their tags check
+    PollClock clk;
+    while (pending || !max_done) {
+        unsigned long long mword = 0;
+        if (!max_done) mword = ll_load(maxw + tid);
+#pragma unroll
+        for (int k = 0; k < kMkQuantGroups; ++k) {
+            if (pending & (1u << k)) {
+                const unsigned long long* p = vw + 8 * (tid + k * kMkConsumers);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) raw[k][j] = ll_load2(p + 2 * j);
+            }
+        }
+        if (!max_done && ll_tag(mword) == tag) {
+            mx = ll_value(mword);
+            max_done = true;
+        }
+#pragma unroll
+        for (int k = 0; k < kMkQuantGroups; ++k) {
+            if (!(pending & (1u << k))) continue;
+            bool ok = true;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ok = ok && ll_tag(raw[k][j].x) == tag && ll_tag(raw[k][j].y) == tag;
+            if (ok) pending &= ~(1u << k);
+        }
+        if ((pending || !max_done) && poll_expired(clk)) {
+            atomicOr(&flags[0], 1);
+            break;
+        }
+    }
+    if (trace_ev >= 0) H4B_TRACE_ANY(trace_ev + 1);
+    const float m = group_max(mx, red, kMkWarps, 1);
     const float qs = quant_multiplier(m);
-    for (int g0 = tid; g0 < groups; g0 += kMkQuantGroups * kMkConsumers) {
-        unsigned pending = 0;
 #pragma unroll
-        for (int k = 0; k < kMkQuantGroups; ++k)
-            if (g0 + k * kMkConsumers < groups) pending |= 1u << k;
-        PollClock clk;
-        while (pending) {
-            if (clk.rounds != 0) {
-                bool seen = true;
+    for (int k = 0; k < kMkQuantGroups; ++k) {
+        const int g = tid + k * kMkConsumers;
+        if (g < groups) {
+            int q[8];
 #pragma unroll
-                for (int k = 0; k < kMkQuantGroups; ++k)
-                    if (pending & (1u << k))
-                        seen = seen && ll_tag(ll_load(vw + 8 * (g0 + k * kMkConsumers) + 7)) == tag;
-                if (!seen) {
-                    if (poll_expired(clk)) {
-                        atomicOr(&flags[0], 1);
-                        break;
-                    }
-                    continue;
-                }
+            for (int j = 0; j < 4; ++j) {
+                q[2 * j] = quantize_one(ll_value(raw[k][j].x), qs);
+                q[2 * j + 1] = quantize_one(ll_value(raw[k][j].y), qs);
             }
-            ulonglong2 raw[kMkQuantGroups][4];
-#pragma unroll
-            for (int k = 0; k < kMkQuantGroups; ++k) {
-                if (pending & (1u << k)) {
-                    const unsigned long long* p = vw + 8 * (g0 + k * kMkConsumers);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) raw[k][j] = ll_load2(p + 2 * j);
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < kMkQuantGroups; ++k) {
-                if (!(pending & (1u << k))) continue;
-                bool ok = true;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) ok = ok && ll_tag(raw[k][j].x) == tag && ll_tag(raw[k][j].y) == tag;
-                if (ok) {
-                    int q[8];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        q[2 * j] = quantize_one(ll_value(raw[k][j].x), qs);
-                        q[2 * j + 1] = quantize_one(ll_value(raw[k][j].y), qs);
-                    }
-                    store_group(xq, g0 + k * kMkConsumers, q);
-                    pending &= ~(1u << k);
-                }
-            }
-            if (pending && poll_expired(clk)) {
-                atomicOr(&flags[0], 1);
-                break;
-            }
+            store_group(xq, g, q);
         }
     }
     zero_xq_tail(xq, n, tid, kMkConsumers);
@@ -481,9 +462,10 @@ __device__ __forceinline__ void mk_fetch_scales(const Seg& sg, float* sc_s) {
     for (int i = threadIdx.x; i < sg.nrows; i += kMkConsumers) async_copy4(sc_s + i, sg.ws + sg.r0 + i);
 }
 
-// Starts the async copy of an RMSNorm weight (n floats) into gamma_s.
+// Starts the async copy of an RMSNorm weight (n floats, n % 4 == 0, 16-byte
+// aligned) into gamma_s.
 __device__ __forceinline__ void mk_fetch_gamma(const float* gamma, float* gamma_s, int n) {
-    for (int i = threadIdx.x; i < n; i += kMkConsumers) async_copy4(gamma_s + i, gamma + i);
+    for (int i = threadIdx.x; i < (n >> 2); i += kMkConsumers) async_copy16(gamma_s + 4 * i, gamma + 4 * i);
 }
 
 // Starts fetching what GEMV segment g + 1 needs while segment g's tiles run:
@@ -519,6 +501,65 @@ __device__ __forceinline__ bool mk_poll_head(const unsigned long long* w, int la
             return false;
         }
     }
+}
+
+// merge_splits over exchange words for long contexts (more splits than one
+// staging batch): split 0 from registers, each other split polled in turn.
+__device__ float4 mk_merge_direct(const unsigned long long* base, int splits, long long stride, uint32_t tag,
+                                  float m0, float l0, float4 o0, int lane, bool& ok) {
+    float mmax = -INFINITY;
+    for (int s = lane; s < splits; s += 32) {
+        float mv = m0;
+        if (s != 0) {
+            PollClock clk;
+            unsigned long long w = ll_load(base + s * stride + kHeadDim);
+            while (ll_tag(w) != tag) {
+                if (poll_expired(clk)) {
+                    ok = false;
+                    break;
+                }
+                w = ll_load(base + s * stride + kHeadDim);
+            }
+            mv = ll_value(w);
+        }
+        mmax = fmaxf(mmax, mv);
+    }
+    mmax = warp_max(mmax);
+    float l = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < splits; ++s) {
+        float ms = m0, ls = l0;
+        float4 ov = o0;
+        if (s != 0) {
+            const unsigned long long* p = base + s * stride;
+            PollClock clk;
+            while (true) {
+                const ulonglong2 a = ll_load2(p + 4 * lane), b = ll_load2(p + 4 * lane + 2);
+                const ulonglong2 c = ll_load2(p + kHeadDim);
+                const bool good = ll_tag(a.x) == tag && ll_tag(a.y) == tag && ll_tag(b.x) == tag &&
+                                  ll_tag(b.y) == tag && ll_tag(c.x) == tag && ll_tag(c.y) == tag;
+                if (__all_sync(0xffffffffu, good)) {
+                    ov = make_float4(ll_value(a.x), ll_value(a.y), ll_value(b.x), ll_value(b.y));
+                    ms = ll_value(c.x);
+                    ls = ll_value(c.y);
+                    break;
+                }
+                if (poll_expired(clk)) {
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (ls == 0.f) continue;
+        const float w = exp_cw(ms - mmax);
+        l = __fmaf_rn(ls, w, l);
+        acc.x = __fmaf_rn(ov.x, w, acc.x);
+        acc.y = __fmaf_rn(ov.y, w, acc.y);
+        acc.z = __fmaf_rn(ov.z, w, acc.z);
+        acc.w = __fmaf_rn(ov.w, w, acc.w);
+    }
+    const float inv = __fdiv_rn(1.0f, l);
+    return make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
 }
 
 // One attention split (kv head h, split `split` of `splits`) for layer l,
@@ -580,8 +621,11 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
     if (l == 1) H4B_TRACE(1501);
     async_copy_wait_all();
     named_sync(1, kMkConsumers);  // consts_s (and the first sub-tile) landed
-    if (head_warp) q = norm_rope_with(q, head_consts(consts_s, consts_s + 2 * d, consts_s + 5 * d / 2, lane), true,
-                                      true, m.eps, lane);
+    if (head_warp) {
+        q = norm_rope_with(q, head_consts(consts_s, consts_s + 2 * d, consts_s + 5 * d / 2, lane), true, true, m.eps,
+                           lane);
+        *reinterpret_cast<float4*>(consts_s + (3 + warp) * d + 4 * lane) = q;  // this warp's staged q head
+    }
     if (owns_new) {
         if (warp == 0) {
             k_new = norm_rope_with(k_new, head_consts(consts_s + d, consts_s + 2 * d, consts_s + 5 * d / 2, lane),
@@ -600,13 +644,16 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
             stage_subtile<KV>(kc, vc, d, base, n, owns_new ? pos : -1, ks, vs, threadIdx.x, kMkConsumers);
         }
         if (owns_new && pos >= base && pos < base + n) {
-            if (warp == 0) store4<KV>(ks + (pos - base) * kHeadDim + 4 * lane, k_new);
-            if (warp == groups - 1) store4<KV>(vs + (pos - base) * kHeadDim + 4 * lane, v_new);
+            if (warp == 0) store4<KV>(ks + (pos - base) * kv_row_stride<KV>() + 4 * lane, k_new);
+            if (warp == groups - 1) store4<KV>(vs + (pos - base) * kv_row_stride<KV>() + 4 * lane, v_new);
         }
         async_copy_wait_all();
         named_sync(1, kMkConsumers);
         if (l == 1) H4B_TRACE(1502);
-        if (head_warp) attend_subtile<KV>(q, ks, vs, n, scale, lane, mrun, l_run, o);
+#ifdef H4B_PHASE_TRACE
+        if (threadIdx.x == 0) g_trace_attn = (l == 1);
+#endif
+        if (head_warp) attend_subtile<KV>(consts_s + (3 + warp) * d, ks, vs, n, scale, lane, mrun, l_run, o);
     }
     if (l == 1) H4B_TRACE(1503);
 
@@ -627,89 +674,70 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
             const float inv = __fdiv_rn(1.0f, l_run);
             result = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
         }
-    } else if (head_warp) {
-        // Merge, split 0 from registers, the others polled: lane s holds
-        // (m, l) of splits s and s + 32.
-        const unsigned long long* mine = part + warp * pstride;
-        float ms[2] = {-INFINITY, -INFINITY}, ls[2] = {0.f, 0.f};
+    } else if (splits <= a.stage_splits) {
+        // Merge in split order (merge_splits' arithmetic), split 0 from
+        // registers. The other splits' partials are copied as raw exchange
+        // words into the K/V staging area (free once the math is done) and
+        // re-copied until every word carries tag_part: one L2 round trip per
+        // polling round, and the poll holds no registers.
+        constexpr int kPieces = kPartialStride / 2;  // 16-byte pieces per (split, head) partial
+        unsigned long long* stage = reinterpret_cast<unsigned long long*>(ks);  // [split][groups][kPartialStride]
+        int* stale_s = reinterpret_cast<int*>(red + 16);
+        const int total = splits * groups * kPieces;
+        named_sync(1, kMkConsumers);  // every head warp is done reading the K/V sub-tile
         PollClock clk;
-        for (int r = 0; r < 2; ++r) {
-            const int sidx = lane + 32 * r;
-            if (sidx == 0) {
-                ms[r] = mrun;
-                ls[r] = l_run;
-            } else if (sidx < splits) {
-                const unsigned long long* p = mine + static_cast<long long>(sidx) * groups * pstride + kHeadDim;
-                ulonglong2 w = ll_load2(p);
-                while (ll_tag(w.x) != tag_part || ll_tag(w.y) != tag_part) {
-                    if (poll_expired(clk)) {
-                        ok = false;
-                        break;
-                    }
-                    w = ll_load2(p);
-                }
-                ms[r] = ll_value(w.x);
-                ls[r] = ll_value(w.y);
+        for (bool first = true;; first = false) {
+            for (int i = threadIdx.x; i < total; i += kMkConsumers) {
+                const int piece = i % kPieces, sh = i / kPieces;  // sh = split * groups + head warp
+                if (sh < groups) continue;  // split 0 is this CTA
+                unsigned long long* dst = stage + static_cast<long long>(sh) * pstride + 2 * piece;
+                if (!first && ll_tag(dst[0]) == tag_part && ll_tag(dst[1]) == tag_part) continue;
+                async_copy16(dst, part + static_cast<long long>(sh) * pstride + 2 * piece);
             }
+            async_copy_wait_all();
+            if (threadIdx.x == 0) *stale_s = 0;
+            named_sync(1, kMkConsumers);
+            bool stale = false;
+            for (int i = threadIdx.x; i < total; i += kMkConsumers) {
+                const int piece = i % kPieces, sh = i / kPieces;
+                if (sh < groups || piece == kPieces - 1) continue;  // the last piece holds 2 pad words
+                const unsigned long long* w = stage + static_cast<long long>(sh) * pstride + 2 * piece;
+                stale = stale || ll_tag(w[0]) != tag_part || ll_tag(w[1]) != tag_part;
+            }
+            if (stale) *stale_s = 1;
+            named_sync(1, kMkConsumers);
+            if (!*stale_s) break;
+            if (mk_stop(flags, threadIdx.x == 0 && poll_expired(clk))) return false;
         }
-        const float mmax = warp_max(fmaxf(ms[0], ms[1]));
-        float lsum = 0.f;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        constexpr int kBatch = 4;
-        for (int s0 = 0; s0 < splits; s0 += kBatch) {
-            float4 ov[kBatch];
-            unsigned pending = 0;
-#pragma unroll
-            for (int j = 0; j < kBatch; ++j) {
-                const int sidx = s0 + j;
-                if (sidx == 0) ov[j] = o;
-                else if (sidx < splits) pending |= 1u << j;
+        if (head_warp) {
+            const unsigned long long* mine = stage + warp * pstride;
+            float mm = -INFINITY;
+            for (int s = lane; s < splits; s += 32)
+                mm = fmaxf(mm, s == 0 ? mrun : ll_value(mine[static_cast<long long>(s) * groups * pstride + kHeadDim]));
+            mm = warp_max(mm);
+            float lsum = 0.f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s = 0; s < splits; ++s) {
+                const unsigned long long* w = mine + static_cast<long long>(s) * groups * pstride;
+                const float ls = s == 0 ? l_run : ll_value(w[kHeadDim + 1]);
+                if (ls == 0.f) continue;
+                const float ms = s == 0 ? mrun : ll_value(w[kHeadDim]);
+                const float4 ov = s == 0 ? o
+                                         : make_float4(ll_value(w[4 * lane]), ll_value(w[4 * lane + 1]),
+                                                       ll_value(w[4 * lane + 2]), ll_value(w[4 * lane + 3]));
+                const float wgt = exp_cw(ms - mm);
+                lsum = __fmaf_rn(ls, wgt, lsum);
+                acc.x = __fmaf_rn(ov.x, wgt, acc.x);
+                acc.y = __fmaf_rn(ov.y, wgt, acc.y);
+                acc.z = __fmaf_rn(ov.z, wgt, acc.z);
+                acc.w = __fmaf_rn(ov.w, wgt, acc.w);
             }
-            PollClock oclk;
-            while (pending) {
-                ulonglong2 raw[kBatch][2];
-#pragma unroll
-                for (int j = 0; j < kBatch; ++j) {
-                    if (pending & (1u << j)) {
-                        const unsigned long long* p = mine + static_cast<long long>(s0 + j) * groups * pstride + 4 * lane;
-                        raw[j][0] = ll_load2(p);
-                        raw[j][1] = ll_load2(p + 2);
-                    }
-                }
-#pragma unroll
-                for (int j = 0; j < kBatch; ++j) {
-                    if ((pending & (1u << j)) && ll_tag(raw[j][0].x) == tag_part && ll_tag(raw[j][0].y) == tag_part &&
-                        ll_tag(raw[j][1].x) == tag_part && ll_tag(raw[j][1].y) == tag_part) {
-                        ov[j] = make_float4(ll_value(raw[j][0].x), ll_value(raw[j][0].y), ll_value(raw[j][1].x),
-                                            ll_value(raw[j][1].y));
-                        pending &= ~(1u << j);
-                    }
-                }
-                if (pending && poll_expired(oclk)) {
-                    ok = false;
-#pragma unroll
-                    for (int j = 0; j < kBatch; ++j)
-                        if (pending & (1u << j)) ov[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    break;
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < kBatch; ++j) {
-                const int sidx = s0 + j;
-                if (sidx >= splits) break;
-                const float lsj = __shfl_sync(0xffffffffu, sidx < 32 ? ls[0] : ls[1], sidx & 31);
-                const float msj = __shfl_sync(0xffffffffu, sidx < 32 ? ms[0] : ms[1], sidx & 31);
-                if (lsj == 0.f) continue;
-                const float w = exp_cw(msj - mmax);
-                lsum = __fmaf_rn(lsj, w, lsum);
-                acc.x = __fmaf_rn(ov[j].x, w, acc.x);
-                acc.y = __fmaf_rn(ov[j].y, w, acc.y);
-                acc.z = __fmaf_rn(ov[j].z, w, acc.z);
-                acc.w = __fmaf_rn(ov[j].w, w, acc.w);
-            }
+            const float inv = __fdiv_rn(1.0f, lsum);
+            result = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
         }
-        const float inv = __fdiv_rn(1.0f, lsum);
-        result = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    } else if (head_warp) {
+        // More splits than the staging area holds: poll them in turn.
+        result = mk_merge_direct(part + warp * pstride, splits, groups * pstride, tag_part, mrun, l_run, o, lane, ok);
     }
     if (mk_stop(flags, !ok)) return false;
     if (l == 1) H4B_TRACE(1504);
@@ -744,11 +772,11 @@ __host__ __device__ inline MkSmem mk_smem_layout(int xq_bytes, int hidden, int r
     s.xq = s.red + 64 * 4;
     s.gamma = s.xq + xq_region(xq_bytes);
     s.consts = s.gamma + ((hidden * 4 + 127) & ~127);  // attention's q/k norm weights + RoPE row
-    s.acc = s.consts + 3 * kHeadDim * 4;
+    s.acc = s.consts + (3 + kMaxGroups) * kHeadDim * 4;  // + one staged q head per warp
     s.scale = s.acc + rows_cap * 4;    // two buffers: this phase's row scales and the next one's
     s.xo = s.scale + 2 * rows_cap * 4;  // this CTA's rows of x, kept across phases
     s.att = (s.xo + rows_cap * 4 + 127) & ~127;
-    const int att_bytes = 2 * kSubTile * kHeadDim * kv_bytes;
+    const int att_bytes = 2 * kSubTile * (kHeadDim + 16 / kv_bytes) * kv_bytes;
     s.ring = (s.att + (att_bytes > hidden * 4 ? att_bytes : hidden * 4) + 127) & ~127;
     s.total = s.ring + stages * slot_bytes + 512;  // slot loads may run up to 496 B past a tile
     return s;
@@ -835,7 +863,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
     float* consts_s = reinterpret_cast<float*>(smem + L.consts);
     float* xo = reinterpret_cast<float*>(smem + L.xo);
     KV* ks = reinterpret_cast<KV*>(smem + L.att);
-    KV* vs = ks + kSubTile * kHeadDim;
+    KV* vs = ks + kSubTile * kv_row_stride<KV>();
     float* xs = reinterpret_cast<float*>(smem + L.att);  // embedding row, before any attention
     uint8_t* ring = smem + L.ring;
     unsigned long long* xw = st.exchange;
@@ -939,6 +967,17 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         const Seg sg = mk_segment(a, g, cta, nctas);
         const float* sc_s = sc_base + (g & 1) * a.rows_cap;
         H4B_TRACE(8 + 3 * g);
+        if (g >= 8 && g < 12) H4B_TRACE_CTA(4 * (g - 8));
+#ifdef H4B_PHASE_TRACE
+        if (g >= 8 && g < 12 && threadIdx.x == 0) {
+            // one L2 round trip of a word that is already there (this CTA's own launch counter)
+            const uint64_t t0 = globaltimer_ns();
+            const unsigned long long w = ll_load(xw + a.x.gen + cta);
+            uint64_t t1;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1) : "l"(w));  // waits for w
+            H4B_TRACE_VAL(1650 + (g - 8), t1 - t0);
+        }
+#endif
         async_copy_wait_all();  // this segment's scales (and gamma), fetched a segment ago
 
         // ---- prologue ----
@@ -947,7 +986,8 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
             const bool o = kind == SEG_O;
             act = mk_prologue_quant(xw + (o ? a.x.att : a.x.act), xw + (o ? a.x.att_max : a.x.act_max),
                                     o ? m.kv_heads : nctas, tl + (o ? TAG_ATT : TAG_ACT),
-                                    o ? m.heads * m.head_dim : m.intermediate, xq, red, flags);
+                                    o ? m.heads * m.head_dim : m.intermediate, xq, red, flags,
+                                    g >= 8 && g < 12 ? 1600 + 2 * (g - 8) : -1);
         } else {
             // qkv reads x after the previous layer's down (layer 0: the
             // embedding in xs), gate/up after this layer's o, the head after
@@ -956,15 +996,17 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
             const unsigned long long* src = xw + (kind == SEG_GATE_UP ? a.x.x_o : a.x.x_down);
             const uint32_t tag = kind == SEG_GATE_UP ? tl + TAG_XO : tl - kTagsPerLayer + TAG_XDOWN;
             act = mk_prologue_rms(from_xs ? xs : nullptr, from_xs ? nullptr : src, tag, gamma_s, H, eps, xq, red,
-                                  flags);
+                                  flags, g >= 8 && g < 12 ? 1600 + 2 * (g - 8) : -1);
         }
-        mk_prefetch_next(a, g, cta, nctas, sc_base, gamma_s);
         H4B_TRACE(8 + 3 * g + 1);
+        if (g >= 8 && g < 12) H4B_TRACE_CTA(4 * (g - 8) + 1);
+        mk_prefetch_next(a, g, cta, nctas, sc_base, gamma_s);
 
         // ---- tiles ----
         mk_run_tiles(sg, seq, a.stages, a.slot_bytes, ring, full, empty, xq, acc_s, flags);
         seq += sg.ntiles;
         H4B_TRACE(8 + 3 * g + 2);
+        if (g >= 8 && g < 12) H4B_TRACE_CTA(4 * (g - 8) + 2);
         if (mk_stop(flags)) return;
 
         // ---- epilogue ----
@@ -997,6 +1039,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         } else {
             mk_finish_token(a, sg, sc_s, act, acc_s, xw, tl, pos, flags);
         }
+        if (g >= 8 && g < 12) H4B_TRACE_CTA(4 * (g - 8) + 3);
     }
 }
 
@@ -1018,7 +1061,9 @@ static int plan_persistent(const h4b_model* m, const h4b_state* s, MkPlan* p) {
     const int max_width = std::max(m->hidden, std::max(q_size, m->intermediate));
     if (max_width > kMkMaxWidth) return H4B_EUNSUPPORTED;
     const int nctas = sm_count();
-    if (nctas > kMkMaxCtas) return H4B_EUNSUPPORTED;
+    if (nctas > kMkConsumers || nctas > kMkMaxCtas) return H4B_EUNSUPPORTED;  // one act maximum per thread
+    if (std::max(q_size, m->intermediate) > kMkQuantGroups * 8 * kMkConsumers) return H4B_EUNSUPPORTED;
+    if (m->heads / m->kv_heads > kMkWarps) return H4B_EUNSUPPORTED;  // one consumer warp per q head of a group
     MkArgs& a = p->args;
     a = MkArgs{};
     a.m = *m;
@@ -1026,6 +1071,12 @@ static int plan_persistent(const h4b_model* m, const h4b_state* s, MkPlan* p) {
     a.x = x_layout(*m);
     a.attn_chunk = 32;
     a.max_splits = mk_splits_max(m);
+    {
+        const int groups = m->heads / m->kv_heads;
+        const int kvb = s->kv_dtype == 0 ? 4 : 2;
+        const int staging = 2 * kSubTile * (kHeadDim + 16 / kvb) * kvb;
+        a.stage_splits = staging / (groups * kPartialStride * 8);
+    }
     a.xq_bytes = max_width;
     // Rows one CTA owns in any segment, plus one partition unit of slack.
     const int biggest = std::max({m->vocab, 2 * m->intermediate, q_size + 2 * m->kv_heads * m->head_dim, m->hidden});
@@ -1078,6 +1129,12 @@ int decode_persistent(const h4b_model* m, const h4b_state* s, cudaStream_t strea
 extern "C" int h4b_phase_trace(unsigned long long* host) {
     H4B_CUDA_TRY(cudaDeviceSynchronize());
     H4B_CUDA_TRY(cudaMemcpyFromSymbol(host, h4b::g_phase_trace, sizeof(unsigned long long) * 3 * 2048));
+    return 0;
+}
+
+extern "C" int h4b_phase_trace_ctas(unsigned long long* host) {
+    H4B_CUDA_TRY(cudaDeviceSynchronize());
+    H4B_CUDA_TRY(cudaMemcpyFromSymbol(host, h4b::g_phase_all, sizeof(unsigned long long) * 1024 * 16));
     return 0;
 }
 #endif
