@@ -34,11 +34,11 @@ sys.path.insert(0, str(ROOT))
 METRIC = "batch-1 decode tok/s Qwen3-4B int4; body-GEMV HBM GB/s vs ~8 TB/s"
 PROMPT = 128
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic
-# byte, from the ncu captures summarised under profiles/: the persistent
-# decode kernel on a 4-layer Qwen3-4B-shaped model (weights + LM head +
-# KV), and the body GEMV kernel. Traffic grows in proportion to the bytes
-# streamed, so the ratio scales a launch of the full model.
-NCU_TRAFFIC_PER_BYTE = {"persistent": 1.0213, "gemv": None}
+# byte, from the ncu capture in profiles/decode_persistent_full_4layer.md: the
+# persistent decode kernel on a 4-layer Qwen3-4B-shaped model (weights + LM
+# head + KV). Traffic grows in proportion to the bytes streamed, so the ratio
+# scales a launch of the full model. (No capture of the chain-mode GEMV yet.)
+NCU_TRAFFIC_PER_BYTE = {"persistent": 1.0123, "gemv": None}
 
 
 def parse_args():

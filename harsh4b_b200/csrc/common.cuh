@@ -57,8 +57,8 @@ __device__ __forceinline__ int trace_slot() {
     do {                                             \
         if (threadIdx.x == 0) H4B_TRACE_ANY(ev);     \
     } while (0)
-// Per-CTA timestamps (all CTAs): g_phase_all[cta][ev], ev < 16.
-__device__ unsigned long long g_phase_all[1024][16];
+// Per-CTA timestamps (all CTAs): g_phase_all[cta][ev], ev < 32.
+__device__ unsigned long long g_phase_all[1024][32];
 #define H4B_TRACE_CTA(ev)                                                                    \
     do {                                                                                     \
         if (threadIdx.x == 0) ::h4b::g_phase_all[blockIdx.x][(ev)] = ::h4b::globaltimer_ns(); \
