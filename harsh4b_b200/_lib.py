@@ -63,8 +63,10 @@ _SIGNATURES = {
     "h4b_graph_launch": [_vp, _vp],
     "h4b_graph_destroy": [_vp],
     "h4b_persistent_exchange_words": [ctypes.POINTER(ModelDesc)],
+    "h4b_sample": [_vp, _i32, _vp, _i32, _f32, _i32, _f32, _f32, ctypes.c_double, _vp, _vp, _vp, _vp, _vp],
+    "h4b_sample_scratch_bytes": [_i32, _i32],
 }
-_RESTYPES = {"h4b_persistent_exchange_words": ctypes.c_longlong}
+_RESTYPES = {"h4b_persistent_exchange_words": ctypes.c_longlong, "h4b_sample_scratch_bytes": ctypes.c_longlong}
 
 
 def exported_symbols() -> list[str]:

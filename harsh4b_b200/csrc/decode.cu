@@ -233,10 +233,12 @@ int decode_step(const h4b_model* m, const h4b_state* s, cudaStream_t stream) {
 }
 
 int prepare_persistent();  // persistent.cu
+int prepare_sampling();    // sample.cu
 
 int prepare_other_kernels() {
     int r = 0;
     if ((r = prepare_persistent())) return r;
+    if ((r = prepare_sampling())) return r;
     if ((r = cudaFuncSetAttribute(gqa_split_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   subtile_smem_bytes<float>())))
         return r;

@@ -4,3 +4,4 @@
 #include "attention.cu"
 #include "decode.cu"
 #include "persistent.cu"
+#include "sample.cu"

@@ -120,3 +120,30 @@ def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
     check(lib().h4b_argmax(_dev(logits, torch.float32, "logits"), logits.numel(), _dev(out, torch.int32, "out"),
                            stream_handle()), "h4b_argmax")
     return out
+
+
+def sample(logits: torch.Tensor, generated: torch.Tensor | None, uniform: float, *, temperature: float = 0.7,
+           top_k: int = 50, top_p: float = 0.9, repetition_penalty: float = 1.15, out: torch.Tensor | None = None,
+           scratch: torch.Tensor | None = None, return_candidates: bool = False):
+    """h4b_sample: one token from fp32 logits (penalised IN PLACE) on the GPU.
+    `generated` holds distinct int32 ids (or None); `uniform` is a draw in
+    [0, 1) from the caller's generator. Returns the int32 token tensor[1]
+    (and the candidate ids / probabilities when asked)."""
+    vocab = logits.numel()
+    out = torch.empty(1, dtype=torch.int32, device=logits.device) if out is None else out
+    k = min(top_k if top_k > 0 else 50, vocab)
+    if scratch is None:
+        nbytes = int(lib().h4b_sample_scratch_bytes(vocab, top_k))
+        if nbytes < 0:
+            check(nbytes, "h4b_sample_scratch_bytes")
+        scratch = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=logits.device)
+    ids = torch.empty(k, dtype=torch.int32, device=logits.device) if return_candidates else None
+    probs = torch.empty(k, dtype=torch.float32, device=logits.device) if return_candidates else None
+    n_gen = 0 if generated is None else generated.numel()
+    check(lib().h4b_sample(_dev(logits, torch.float32, "logits"), vocab,
+                           _dev(generated, torch.int32, "generated") if n_gen else None, n_gen, float(temperature),
+                           int(top_k), float(top_p), float(repetition_penalty), float(uniform),
+                           _dev(out, torch.int32, "out"), ids.data_ptr() if ids is not None else None,
+                           probs.data_ptr() if probs is not None else None, scratch.data_ptr(), stream_handle()),
+          "h4b_sample")
+    return (out, ids, probs) if return_candidates else out

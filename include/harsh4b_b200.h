@@ -109,6 +109,21 @@ int h4b_embedding(const int32_t *token, const uint8_t *embedding, const float *s
  * of logits[n], written to *token_out (device int32). */
 int h4b_argmax(const float *logits, int n, int32_t *token_out, void *stream);
 
+/* Stochastic sampling of one token (inference_runtime.sample_numpy,
+ * inference_runtime.py:144-163; cpu_lightspark.sample_logits,
+ * cpu_lightspark.py:700-726): repetition penalty on the `n_generated`
+ * DISTINCT ids in `generated` (applied to `logits` in place), then greedy if
+ * temperature <= 0.01, else top-k (top_k <= 64; <= 0 means 50) of
+ * logits / temperature, softmax, top-p cut, and the token whose float64 CDF
+ * interval holds `uniform` (a draw in [0, 1) from the caller's generator --
+ * numpy's Generator.choice does the same search). Optional outputs: the k
+ * candidate ids (descending) and their final probabilities. `scratch` holds
+ * h4b_sample_scratch_bytes(vocab, top_k) bytes. */
+int h4b_sample(float *logits, int vocab, const int32_t *generated, int n_generated, float temperature, int top_k,
+               float top_p, float repetition_penalty, double uniform, int32_t *token_out, int32_t *topk_ids_out,
+               float *topk_probs_out, void *scratch, void *stream);
+long long h4b_sample_scratch_bytes(int vocab, int top_k);
+
 /* ---- model level ----------------------------------------------------------- */
 
 /* Device-resident Qwen3 model. Every weight kind is one buffer covering all

@@ -225,3 +225,43 @@ def sample_logits(logits: np.ndarray, generated: list[int], *, argmax: bool, tem
         probabilities /= probabilities.sum(dtype=np.float32)
     generator = generator or np.random.default_rng(0)
     return int(generator.choice(candidates, p=probabilities))
+
+
+def choice_uniform(ids: np.ndarray, probabilities: np.ndarray, uniform: float) -> int:
+    """numpy's Generator.choice(ids, p=probabilities) for a given draw
+    u = generator.random(): the first index whose normalised float64
+    cumulative probability exceeds u (searchsorted, side='right')."""
+    cdf = np.asarray(probabilities, dtype=np.float64).cumsum()
+    cdf /= cdf[-1]
+    return int(ids[int(np.searchsorted(cdf, uniform, side="right"))])
+
+
+def sample_runtime(logits: np.ndarray, generated: list[int], uniform: float, *, temperature: float = 0.7,
+                   top_p: float = 0.9, top_k: int = 50, repetition_penalty: float = 1.15,
+                   return_candidates: bool = False):
+    """Restates inference_runtime.sample_numpy (inference_runtime.py:144-163),
+    the CPU runtime's sampler, with the generator's draw passed in as
+    `uniform` (see choice_uniform). top_k <= 0 means 50 (the CUDA and MLX
+    samplers' rule, inference_runtime.py:243,180)."""
+    values = np.array(logits, dtype=np.float32, copy=True).reshape(-1)
+    if generated and repetition_penalty != 1.0:
+        ids = np.array(sorted(set(generated)), dtype=np.int64)
+        repeated = values[ids]
+        values[ids] = np.where(repeated > 0, repeated / np.float32(repetition_penalty),
+                               repeated * np.float32(repetition_penalty))
+    if temperature <= 0.01:
+        token = int(values.argmax())
+        return (token, None, None) if return_candidates else token
+    values /= np.float32(temperature)
+    count = min(top_k if top_k > 0 else 50, values.size)
+    ids = np.argpartition(-values, count - 1)[:count]
+    ids = ids[np.lexsort((ids, -values[ids]))]  # descending; equal values by index (the reference leaves ties open)
+    selected = values[ids]
+    selected -= selected.max()
+    probabilities = np.exp(selected, dtype=np.float32)
+    probabilities /= probabilities.sum(dtype=np.float32)
+    if top_p < 1.0:
+        probabilities[(np.cumsum(probabilities) - probabilities) >= top_p] = 0
+        probabilities /= probabilities.sum(dtype=np.float32)
+    token = choice_uniform(ids, probabilities, uniform)
+    return (token, ids, probabilities) if return_candidates else token

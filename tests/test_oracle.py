@@ -168,3 +168,30 @@ def test_kv_precision_sensitivity():
     sa, sb = a.new_state(16), b.new_state(16)
     drift = max(float(np.abs(a.forward_token(t, sa) - b.forward_token(t, sb)).max()) for t in prompt)
     assert drift > 1e-2
+
+
+def test_choice_uniform_is_numpy_choice():
+    """Generator.choice(ids, p) == the float64 CDF search at generator.random()."""
+    from oracle.model import choice_uniform
+
+    for seed in range(200):
+        rng = np.random.default_rng(seed)
+        n = int(rng.integers(1, 65))
+        p = rng.random(n).astype(np.float32)
+        p /= p.sum(dtype=np.float32)
+        ids = rng.permutation(5000)[:n]
+        a, b = np.random.default_rng(seed + 1), np.random.default_rng(seed + 1)
+        assert int(a.choice(ids, p=p)) == choice_uniform(ids, p, b.random())
+
+
+def test_sample_runtime_matches_reference_golden():
+    """Tokens the reference's sample_numpy drew (tests/golden/sample_cases.npz)."""
+    from oracle.model import sample_runtime
+
+    data = np.load(Path(__file__).resolve().parent / "golden" / "sample_cases.npz")
+    for i in range(len(data["tokens"])):
+        temperature, top_p, top_k, penalty = data["params"][i]
+        generated = [int(t) for t in data["generated"][i] if t >= 0]
+        token = sample_runtime(data["logits"][i], generated, float(data["uniform"][i]), temperature=temperature,
+                               top_p=top_p, top_k=int(top_k), repetition_penalty=penalty)
+        assert token == int(data["tokens"][i]), i
