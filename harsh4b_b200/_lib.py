@@ -65,6 +65,8 @@ _SIGNATURES = {
     "h4b_persistent_exchange_words": [ctypes.POINTER(ModelDesc)],
     "h4b_sample": [_vp, _i32, _vp, _i32, _f32, _i32, _f32, _f32, ctypes.c_double, _vp, _vp, _vp, _vp, _vp],
     "h4b_sample_scratch_bytes": [_i32, _i32],
+    "h4b_quantize_rows": [_vp, _vp, _vp, _vp, _i32, _i32, _vp],
+    "h4b_int4_gemm": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp],
 }
 _RESTYPES = {"h4b_persistent_exchange_words": ctypes.c_longlong, "h4b_sample_scratch_bytes": ctypes.c_longlong}
 

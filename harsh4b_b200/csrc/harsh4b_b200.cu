@@ -5,3 +5,4 @@
 #include "decode.cu"
 #include "persistent.cu"
 #include "sample.cu"
+#include "gemm.cu"

@@ -147,3 +147,33 @@ def sample(logits: torch.Tensor, generated: torch.Tensor | None, uniform: float,
                            probs.data_ptr() if probs is not None else None, scratch.data_ptr(), stream_handle()),
           "h4b_sample")
     return (out, ids, probs) if return_candidates else out
+
+
+def quantize_rows(values: torch.Tensor):
+    """Per-token int8 quantisation of fp32 [M, K]: returns (x8, scales[M], sums[M])."""
+    rows, width = values.shape
+    x8 = torch.empty(rows, width, dtype=torch.int8, device=values.device)
+    scales = torch.empty(rows, dtype=torch.float32, device=values.device)
+    sums = torch.empty(rows, dtype=torch.int32, device=values.device)
+    check(lib().h4b_quantize_rows(_dev(values, torch.float32, "values"), x8.data_ptr(), scales.data_ptr(),
+                                  sums.data_ptr(), rows, width, stream_handle()), "h4b_quantize_rows")
+    return x8, scales, sums
+
+
+def int4_gemm(x8: torch.Tensor, act_scales: torch.Tensor, act_sums: torch.Tensor, weights: torch.Tensor,
+              scales: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """h4b_int4_gemm: fp32 [M, N] from int8 activations [M, K] and int4 weights [N, K/2]."""
+    tokens, width = x8.shape
+    rows = weights.shape[0]
+    out = torch.empty(tokens, rows, dtype=torch.float32, device=x8.device) if out is None else out
+    check(lib().h4b_int4_gemm(_dev(x8, torch.int8, "x8"), _dev(act_scales, torch.float32, "act_scales"),
+                              _dev(act_sums, torch.int32, "act_sums"), _dev(weights, torch.uint8, "weights"),
+                              _dev(scales, torch.float32, "scales"), _dev(out, torch.float32, "out"), tokens, rows,
+                              width, stream_handle()), "h4b_int4_gemm")
+    return out
+
+
+def int4_gemm_rows(values: torch.Tensor, weights: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """fp32 [M, K] -> fp32 [M, N]: per-token quantisation, then the batched GEMM."""
+    x8, act_scales, sums = quantize_rows(values)
+    return int4_gemm(x8, act_scales, sums, weights, scales)

@@ -124,6 +124,21 @@ int h4b_sample(float *logits, int vocab, const int32_t *generated, int n_generat
                float *topk_probs_out, void *scratch, void *stream);
 long long h4b_sample_scratch_bytes(int vocab, int top_k);
 
+/* ---- batched (M > 1 tokens): batched decode and prefill ---------------------
+ * Per-token quantisation of `rows` activations of `width` floats (the
+ * quantize_activation contract applied to each row), also returning each
+ * row's int8 sum. */
+int h4b_quantize_rows(const float *values, int8_t *quantized, float *scales, int32_t *sums, int rows, int width,
+                      void *stream);
+
+/* out[m][n] = float(sum_k w[n][k] * x8[m][k]) * act_scales[m] * scales[n] for
+ * m < tokens, n < rows: litespark_int4_i8_gemv (litespark_int4.cpp:78-84)
+ * applied to `tokens` activations at once on the tensor cores; row m equals
+ * the single-token GEMV of token m bit for bit. act_sums[m] = sum_k x8[m][k]
+ * (from h4b_quantize_rows). rows % 128 == 0 and width % 64 == 0. */
+int h4b_int4_gemm(const int8_t *x8, const float *act_scales, const int32_t *act_sums, const uint8_t *weights,
+                  const float *scales, float *output, int tokens, int rows, int width, void *stream);
+
 /* ---- model level ----------------------------------------------------------- */
 
 /* Device-resident Qwen3 model. Every weight kind is one buffer covering all
