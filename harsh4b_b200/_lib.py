@@ -40,6 +40,15 @@ class StateDesc(ctypes.Structure):
                            "act", "logits", "absmax", "argmax_key", "attn_partials", "attn_counters", "exchange")]
 
 
+class BatchStateDesc(ctypes.Structure):
+    """Mirror of ``h4b_batch_state``."""
+
+    _fields_ = [("batch", _i32), ("capacity", _i32), ("kv_dtype", _i32), ("attn_splits", _i32)] + [
+        (n, _vp) for n in ("k_cache", "v_cache", "positions", "tokens", "next_tokens", "x", "x8", "act_scale",
+                           "act_sum", "qkv", "attended", "proj", "gate_up", "act", "logits", "attn_partials",
+                           "attn_counters")]
+
+
 _SIGNATURES = {
     "h4b_prepare": [],
     "h4b_get_status": [_vp],
@@ -67,6 +76,8 @@ _SIGNATURES = {
     "h4b_sample_scratch_bytes": [_i32, _i32],
     "h4b_quantize_rows": [_vp, _vp, _vp, _vp, _i32, _i32, _vp],
     "h4b_int4_gemm": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp],
+    "h4b_validate_batch": [ctypes.POINTER(ModelDesc), ctypes.POINTER(BatchStateDesc)],
+    "h4b_decode_batch": [ctypes.POINTER(ModelDesc), ctypes.POINTER(BatchStateDesc), _vp],
 }
 _RESTYPES = {"h4b_persistent_exchange_words": ctypes.c_longlong, "h4b_sample_scratch_bytes": ctypes.c_longlong}
 

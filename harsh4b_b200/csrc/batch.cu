@@ -1,0 +1,239 @@
+// Batched decode: B sequences advance one token each per call
+// (LiteSparkQwen.forward_token, cpu_lightspark.py:424-468, for a batch; the
+// reference has no batched path). The body projections run as tensor-core
+// GEMMs (gemm.cu) over the B activations; attention runs the split-K kernel
+// with its batch dimension (each sequence has its own position and KV
+// cache). Every row follows the single-token arithmetic exactly: RMSNorm in
+// the GEMV prologue's 256-lane order, per-token absmax quantisation, exact
+// int32 sums with the float(acc) * act_scale * w_scale epilogue, the same
+// attention kernel, residual adds and SwiGLU -- so each sequence's logits
+// equal what the one-token chain gives it.
+
+namespace h4b {
+
+// Embedding rows (cpu_lightspark.py:341-349): one CTA per sequence.
+__global__ void batch_embed_kernel(const int32_t* tokens, const uint8_t* table, const float* scales, int vocab, int H,
+                                   float* x) {
+    const int b = blockIdx.x;
+    const int token = tokens[b];
+    const bool ok = token >= 0 && token < vocab;
+    if (!ok && threadIdx.x == 0) report(kStatusBadToken);
+    const float scale = ok ? scales[token] : 0.f;
+    const uint8_t* row = table + static_cast<size_t>(ok ? token : 0) * (H >> 1);
+    float* out = x + static_cast<size_t>(b) * H;
+    for (int j = threadIdx.x; j < (H >> 1); j += blockDim.x) {
+        const int8_t byte = static_cast<int8_t>(row[j]);
+        out[2 * j] = ok ? __fmul_rn(static_cast<float>(static_cast<int8_t>(byte << 4) >> 4), scale) : 0.f;
+        out[2 * j + 1] = ok ? __fmul_rn(static_cast<float>(byte >> 4), scale) : 0.f;
+    }
+}
+
+// RMSNorm + per-token quantisation of one row per CTA (256 threads), in the
+// GEMV prologue's order: thread p sums groups p, p + 256, ... of 8 values
+// with fmaf, warps are butterfly-summed and added in order; x8 is written in
+// plain k order for the GEMM, with the row's int8 sum and dequant scale.
+__global__ void __launch_bounds__(256) batch_rmsnorm_quant_kernel(const float* x, const float* gamma, float eps, int H,
+                                                                  int8_t* x8, float* act_scale, int32_t* act_sum) {
+    __shared__ float red[32];
+    __shared__ int ired[8];
+    const int b = blockIdx.x, tid = threadIdx.x;
+    const float* row = x + static_cast<size_t>(b) * H;
+    const int groups = H >> 3;
+    float ss = 0.f;
+    for (int g = tid; g < groups; g += 256) {
+        float v[8];
+        load8(row + 8 * g, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = __fmaf_rn(v[e], v[e], ss);
+    }
+    ss = group_sum(ss, red, 8, 1);
+    const float mean = __fdiv_rn(ss, static_cast<float>(H));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    float local = 0.f;
+    for (int g = tid; g < groups; g += 256) {
+        float v[8], gm[8];
+        load8(row + 8 * g, v);
+        load8(gamma + 8 * g, gm);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) local = fmaxf(local, fabsf(__fmul_rn(__fmul_rn(v[e], inv), gm[e])));
+    }
+    const float m = group_max(local, red, 8, 1);
+    const float qs = quant_multiplier(m);
+    int8_t* out = x8 + static_cast<size_t>(b) * H;
+    int sum = 0;
+    for (int g = tid; g < groups; g += 256) {
+        float v[8], gm[8];
+        load8(row + 8 * g, v);
+        load8(gamma + 8 * g, gm);
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int q = quantize_one(__fmul_rn(__fmul_rn(v[e], inv), gm[e]), qs);
+            sum += q;
+            if (e < 4) lo |= static_cast<uint32_t>(q & 0xFF) << (8 * e);
+            else hi |= static_cast<uint32_t>(q & 0xFF) << (8 * (e - 4));
+        }
+        *reinterpret_cast<uint2*>(out + 8 * g) = make_uint2(lo, hi);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if ((tid & 31) == 0) ired[tid >> 5] = sum;
+    __syncthreads();
+    if (tid == 0) {
+        int t = 0;
+        for (int w = 0; w < 8; ++w) t += ired[w];
+        act_sum[b] = t;
+        act_scale[b] = dequant_scale(m);
+    }
+}
+
+// SwiGLU over rows laid out like the fused gate/up weight (blocks of 4 gate
+// rows then the 4 matching up rows): act = gate / (1 + exp(-gate)) * up.
+__global__ void batch_swiglu_kernel(const float* gate_up, int I, int B, float* act) {
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<long long>(B) * I) return;
+    const long long b = i / I;
+    const int p = static_cast<int>(i % I);
+    const int blk = p / kSwigluBlock, j = p % kSwigluBlock;
+    const float* row = gate_up + b * 2 * I;
+    const float g = row[2 * kSwigluBlock * blk + j], u = row[2 * kSwigluBlock * blk + kSwigluBlock + j];
+    act[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_cw(-g))), u);
+}
+
+// Greedy token per row (first maximum, numpy argmax semantics).
+__global__ void __launch_bounds__(1024) batch_argmax_kernel(const float* logits, int V, int32_t* out) {
+    __shared__ unsigned long long keys[32];
+    const float* row = logits + static_cast<size_t>(blockIdx.x) * V;
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const unsigned long long k = argmax_key(row[i], static_cast<uint32_t>(i));
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0) keys[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) best = keys[w] > best ? keys[w] : best;
+        out[blockIdx.x] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
+    }
+}
+
+__global__ void batch_advance_kernel(int32_t* positions, int B) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) positions[b] += 1;
+}
+
+int validate_batch(const h4b_model* m, const h4b_batch_state* s) {
+    if (!m || !s || s->batch < 1) return H4B_EINVAL;
+    if (m->head_dim != kHeadDim) return H4B_EUNSUPPORTED;
+    if (m->layers < 1 || m->kv_heads < 1 || m->heads % m->kv_heads) return H4B_EINVAL;
+    if (m->heads / m->kv_heads > kMaxGroups) return H4B_EUNSUPPORTED;
+    const int q_size = m->heads * m->head_dim, kv_size = m->kv_heads * m->head_dim;
+    // GEMM tiles: 128 output rows, 64-wide k steps; RMSNorm groups of 8
+    const int rows[] = {q_size + 2 * kv_size, m->hidden, 2 * m->intermediate, m->vocab};
+    for (int r : rows)
+        if (r % kGemmRows) return H4B_EUNSUPPORTED;
+    const int widths[] = {m->hidden, q_size, m->intermediate};
+    for (int w : widths)
+        if (w % kGemmK) return H4B_EUNSUPPORTED;
+    if (m->intermediate % kSwigluBlock) return H4B_EUNSUPPORTED;
+    if (s->capacity < 1 || s->capacity > m->max_pos) return H4B_EINVAL;
+    if (s->kv_dtype != 0 && s->kv_dtype != 1) return H4B_EINVAL;
+    if (s->attn_splits < 1 || s->attn_splits > 64) return H4B_EINVAL;
+    const void* required[] = {m->w_qkv, m->s_qkv, m->w_o, m->s_o, m->w_gate_up, m->s_gate_up, m->w_down, m->s_down,
+                              m->w_embed, m->s_embed, m->norm_in, m->norm_post, m->norm_q, m->norm_k, m->norm_final,
+                              m->rope_cos, m->rope_sin, s->k_cache, s->v_cache, s->positions, s->tokens,
+                              s->next_tokens, s->x, s->x8, s->act_scale, s->act_sum, s->qkv, s->attended, s->proj,
+                              s->gate_up, s->act, s->logits};
+    for (const void* p : required)
+        if (!p || (reinterpret_cast<uintptr_t>(p) & 15)) return H4B_EINVAL;
+    if (s->attn_splits > 1 && (!s->attn_partials || !s->attn_counters)) return H4B_EINVAL;
+    return 0;
+}
+
+int decode_batch(const h4b_model* m, const h4b_batch_state* s, cudaStream_t stream) {
+    int rc = validate_batch(m, s);
+    if (rc) return rc;
+    const int B = s->batch, H = m->hidden, I = m->intermediate, d = m->head_dim;
+    const int q_size = m->heads * d, kv_size = m->kv_heads * d, qkv_rows = q_size + 2 * kv_size;
+    const size_t kv_layer = static_cast<size_t>(m->kv_heads) * s->capacity * d;  // elements
+    auto gemm = [&](const uint8_t* w, const float* ws, float* out, int rows, int width) {
+        GemmArgs g{s->x8, s->act_scale, s->act_sum, w, ws, out, B, rows, width};
+        return launch_int4_gemm(g, stream);
+    };
+    auto norm_quant = [&](const float* gamma) {
+        batch_rmsnorm_quant_kernel<<<B, 256, 0, stream>>>(s->x, gamma, m->eps, H, s->x8, s->act_scale, s->act_sum);
+        return cudaGetLastError() == cudaSuccess ? 0 : H4B_EINVAL;
+    };
+    auto add_x = [&]() {
+        const int n = B * H;
+        add_kernel<<<(n + 255) / 256, 256, 0, stream>>>(s->x, s->proj, n);
+        return cudaGetLastError() == cudaSuccess ? 0 : H4B_EINVAL;
+    };
+    batch_embed_kernel<<<B, 256, 0, stream>>>(s->tokens, m->w_embed, m->s_embed, m->vocab, H, s->x);
+    H4B_CUDA_TRY(cudaGetLastError());
+    for (int l = 0; l < m->layers; ++l) {
+        if ((rc = norm_quant(m->norm_in + static_cast<size_t>(l) * H))) return rc;
+        if ((rc = gemm(m->w_qkv + static_cast<size_t>(l) * qkv_rows * (H / 2), m->s_qkv + static_cast<size_t>(l) * qkv_rows,
+                       s->qkv, qkv_rows, H)))
+            return rc;
+        AttnArgs a = {};
+        a.q = s->qkv; a.knew = s->qkv + q_size; a.vnew = s->qkv + q_size + kv_size;
+        a.q_batch_stride = qkv_rows;
+        a.q_norm = m->norm_q + static_cast<size_t>(l) * d;
+        a.k_norm = m->norm_k + static_cast<size_t>(l) * d;
+        a.rope_cos = m->rope_cos; a.rope_sin = m->rope_sin; a.eps = m->eps;
+        const size_t eb = s->kv_dtype == 0 ? 4 : 2;
+        a.kcache = static_cast<char*>(s->k_cache) + l * kv_layer * eb;
+        a.vcache = static_cast<char*>(s->v_cache) + l * kv_layer * eb;
+        a.head_stride = static_cast<long long>(s->capacity) * d;
+        a.time_stride = d;
+        a.batch_stride = static_cast<long long>(m->layers) * kv_layer;
+        a.position = s->positions; a.capacity = s->capacity;
+        a.groups = m->heads / m->kv_heads; a.kv_heads = m->kv_heads; a.splits = s->attn_splits;
+        a.partials = s->attn_partials; a.counters = s->attn_counters;
+        a.out = s->attended; a.out_batch_stride = q_size; a.absmax_out = nullptr;
+        if ((rc = launch_attention(a, s->kv_dtype, B, stream, false))) return rc;
+        quantize_rows_kernel<<<B, 256, 0, stream>>>(s->attended, q_size, s->x8, s->act_scale, s->act_sum);
+        H4B_CUDA_TRY(cudaGetLastError());
+        if ((rc = gemm(m->w_o + static_cast<size_t>(l) * H * (q_size / 2), m->s_o + static_cast<size_t>(l) * H, s->proj,
+                       H, q_size)))
+            return rc;
+        if ((rc = add_x())) return rc;
+        if ((rc = norm_quant(m->norm_post + static_cast<size_t>(l) * H))) return rc;
+        if ((rc = gemm(m->w_gate_up + static_cast<size_t>(l) * 2 * I * (H / 2),
+                       m->s_gate_up + static_cast<size_t>(l) * 2 * I, s->gate_up, 2 * I, H)))
+            return rc;
+        const long long n_act = static_cast<long long>(B) * I;
+        batch_swiglu_kernel<<<static_cast<int>((n_act + 255) / 256), 256, 0, stream>>>(s->gate_up, I, B, s->act);
+        H4B_CUDA_TRY(cudaGetLastError());
+        quantize_rows_kernel<<<B, 256, 0, stream>>>(s->act, I, s->x8, s->act_scale, s->act_sum);
+        H4B_CUDA_TRY(cudaGetLastError());
+        if ((rc = gemm(m->w_down + static_cast<size_t>(l) * H * (I / 2), m->s_down + static_cast<size_t>(l) * H, s->proj,
+                       H, I)))
+            return rc;
+        if ((rc = add_x())) return rc;
+    }
+    if ((rc = norm_quant(m->norm_final))) return rc;
+    if ((rc = gemm(m->w_embed, m->s_embed, s->logits, m->vocab, H))) return rc;
+    batch_argmax_kernel<<<B, 1024, 0, stream>>>(s->logits, m->vocab, s->next_tokens);
+    H4B_CUDA_TRY(cudaGetLastError());
+    H4B_CUDA_TRY(cudaMemcpyAsync(s->tokens, s->next_tokens, sizeof(int32_t) * B, cudaMemcpyDeviceToDevice, stream));
+    batch_advance_kernel<<<(B + 127) / 128, 128, 0, stream>>>(s->positions, B);
+    H4B_CUDA_TRY(cudaGetLastError());
+    return 0;
+}
+
+}  // namespace h4b
+
+extern "C" int h4b_validate_batch(const h4b_model* model, const h4b_batch_state* state) {
+    return h4b::validate_batch(model, state);
+}
+
+extern "C" int h4b_decode_batch(const h4b_model* model, const h4b_batch_state* state, void* stream) {
+    return h4b::decode_batch(model, state, static_cast<cudaStream_t>(stream));
+}

@@ -6,3 +6,4 @@
 #include "persistent.cu"
 #include "sample.cu"
 #include "gemm.cu"
+#include "batch.cu"

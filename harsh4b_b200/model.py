@@ -17,7 +17,7 @@ import time
 import numpy as np
 import torch
 
-from ._lib import ModelDesc, StateDesc, check, device_status, lib, STATUS_WAIT_TIMEOUT
+from ._lib import BatchStateDesc, ModelDesc, StateDesc, check, device_status, lib, STATUS_WAIT_TIMEOUT
 from .cache import Checkpoint, read_cache
 
 KV_DTYPES = {"float32": (0, torch.float32), "float16": (1, torch.float16)}
@@ -167,6 +167,48 @@ class CudaDecodeState:
         torch.cuda.synchronize(self.model.device)
 
 
+class CudaBatchState:
+    """B independent decode sessions advanced together (one token each per
+    step). KV cache [B][L][kv_heads][capacity][head_dim]; every sequence keeps
+    its own position. Scratch sized for the batch; nothing allocates per step."""
+
+    def __init__(self, model: "CudaQwen", batch: int, capacity: int, attn_splits: int = 16):
+        if batch < 1 or capacity < 1:
+            raise ValueError("batch and capacity must be positive")
+        if capacity > model.max_pos:
+            raise ValueError(f"capacity {capacity} exceeds the model's {model.max_pos} positions")
+        self.model, self.batch, self.capacity, self.splits = model, batch, capacity, int(attn_splits)
+        dev = model.device
+        code, kv_torch = KV_DTYPES[model.kv_dtype]
+        shape = (batch, model.n_layers, model.kv_heads, capacity, model.head_dim)
+        self.k_cache = torch.zeros(shape, dtype=kv_torch, device=dev)
+        self.v_cache = torch.zeros(shape, dtype=kv_torch, device=dev)
+        i32 = dict(dtype=torch.int32, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        H, I, Q, KV = model.hidden, model.intermediate, model.q_size, model.kv_size
+        self.positions = torch.zeros(batch, **i32)
+        self.tokens = torch.zeros(batch, **i32)
+        self.next_tokens = torch.zeros(batch, **i32)
+        self.x = torch.zeros(batch, H, **f32)
+        self.x8 = torch.zeros(batch, max(H, Q, I), dtype=torch.int8, device=dev)
+        self.act_scale = torch.zeros(batch, **f32)
+        self.act_sum = torch.zeros(batch, **i32)
+        self.qkv = torch.zeros(batch, Q + 2 * KV, **f32)
+        self.attended = torch.zeros(batch, Q, **f32)
+        self.proj = torch.zeros(batch, H, **f32)
+        self.gate_up = torch.zeros(batch, 2 * I, **f32)
+        self.act = torch.zeros(batch, I, **f32)
+        self.logits = torch.zeros(batch, model.vocab, **f32)
+        self.partials = torch.zeros(batch * model.kv_heads * self.splits * model.groups * (model.head_dim + 4), **f32)
+        self.counters = torch.zeros(batch * model.kv_heads, **i32)
+        self.desc = BatchStateDesc(batch, capacity, code, self.splits, *[t.data_ptr() for t in (
+            self.k_cache, self.v_cache, self.positions, self.tokens, self.next_tokens, self.x, self.x8,
+            self.act_scale, self.act_sum, self.qkv, self.attended, self.proj, self.gate_up, self.act, self.logits,
+            self.partials, self.counters)])
+        check(lib().h4b_validate_batch(ctypes.byref(model.desc), ctypes.byref(self.desc)), "h4b_validate_batch")
+        self.position = np.zeros(batch, dtype=np.int64)  # host copy of every sequence's position
+
+
 class CudaQwen:
     """Qwen3 decode on one B200 from the packed int4 cache layout."""
 
@@ -295,6 +337,37 @@ class CudaQwen:
         state.replay()
         current.wait_stream(state.stream)
         return state.logits
+
+    def new_batch_state(self, batch: int, capacity: int, attn_splits: int = 16) -> CudaBatchState:
+        return CudaBatchState(self, batch, capacity, attn_splits)
+
+    def forward_batch(self, token_ids, state: CudaBatchState) -> torch.Tensor:
+        """One token for each of the state's B sequences; returns the [B, V]
+        logits (a view, overwritten by the next call). Row b equals what
+        forward_token gives sequence b with the same attention splits."""
+        ids = [int(t) for t in token_ids]
+        if len(ids) != state.batch:
+            raise ValueError(f"expected {state.batch} token ids, got {len(ids)}")
+        if any(not 0 <= t < self.vocab for t in ids):
+            raise ValueError("token ID outside the vocabulary")
+        if int(state.position.max()) >= state.capacity:
+            raise ValueError("decode state capacity exhausted")
+        state.tokens.copy_(torch.tensor(ids, dtype=torch.int32), non_blocking=False)
+        check(lib().h4b_decode_batch(ctypes.byref(self.desc), ctypes.byref(state.desc),
+                                     torch.cuda.current_stream(self.device).cuda_stream), "h4b_decode_batch")
+        state.position += 1
+        return state.logits
+
+    def generate_batch(self, state: CudaBatchState, steps: int) -> None:
+        """`steps` greedy tokens for every sequence, each fed back on the device
+        (state.tokens holds the last tokens; call forward_batch first)."""
+        if int(state.position.max()) + steps > state.capacity:
+            raise ValueError("decode state capacity exhausted")
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        for _ in range(steps):
+            check(lib().h4b_decode_batch(ctypes.byref(self.desc), ctypes.byref(state.desc), stream),
+                  "h4b_decode_batch")
+        state.position += steps
 
     def generate_greedy(self, token_id: int, state: CudaDecodeState, steps: int) -> None:
         """Feed `token_id`, then `steps - 1` more greedy tokens, with no host

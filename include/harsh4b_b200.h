@@ -227,6 +227,38 @@ int h4b_graph_create_persistent(const h4b_model *model, const h4b_state *state, 
 int h4b_graph_launch(void *graph, void *stream);
 int h4b_graph_destroy(void *graph);
 
+/* ---- batched decode (B sequences, one token each per call) ----------------
+ * All buffers caller-allocated on the device, 16-byte aligned.
+ * k_cache/v_cache: [B][L][kv_heads][capacity][head_dim] in kv_dtype.
+ * positions/tokens/next_tokens: int32[B]; the step reads tokens and
+ * positions, writes next_tokens (greedy), copies them to tokens and advances
+ * every position by one. Scratch: x[B][H], x8 int8[B][max(H, q, I)],
+ * act_scale[B], act_sum[B], qkv[B][q + 2kv], attended[B][q], proj[B][H],
+ * gate_up[B][2I], act[B][I], logits[B][V]; attn_partials holds
+ * B * kv_heads * attn_splits * groups * (head_dim + 4) floats and
+ * attn_counters B * kv_heads ints, zero when the session is created. */
+typedef struct h4b_batch_state {
+    int batch, capacity, kv_dtype, attn_splits;
+    void *k_cache, *v_cache;
+    int32_t *positions, *tokens, *next_tokens;
+    float *x;
+    int8_t *x8;
+    float *act_scale;
+    int32_t *act_sum;
+    float *qkv, *attended, *proj, *gate_up, *act, *logits;
+    float *attn_partials;
+    int *attn_counters;
+} h4b_batch_state;
+
+int h4b_validate_batch(const h4b_model *model, const h4b_batch_state *state);
+
+/* One decode token for each of the B sequences (forward_token per sequence):
+ * tensor-core GEMMs over the batch for every projection and the LM head,
+ * batched split-K attention, per-row RMSNorm / quantisation / SwiGLU with the
+ * single-token arithmetic, so row b equals the one-token step of sequence b.
+ * Capturable in a CUDA graph. */
+int h4b_decode_batch(const h4b_model *model, const h4b_batch_state *state, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
