@@ -77,6 +77,8 @@ _SIGNATURES = {
     "h4b_quantize_rows": [_vp, _vp, _vp, _vp, _i32, _i32, _vp],
     "h4b_int4_gemm": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp],
     "h4b_validate_batch": [ctypes.POINTER(ModelDesc), ctypes.POINTER(BatchStateDesc)],
+    "h4b_int4_gemv_absmax": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp],
+    "h4b_residual_acc": [_vp, _vp, _vp, _vp, _i32, _vp],
     "h4b_decode_batch": [ctypes.POINTER(ModelDesc), ctypes.POINTER(BatchStateDesc), _vp],
 }
 _RESTYPES = {"h4b_persistent_exchange_words": ctypes.c_longlong, "h4b_sample_scratch_bytes": ctypes.c_longlong}

@@ -86,6 +86,15 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* v, int8_t* q
     if (threadIdx.x == 0) *scale_out = dequant_scale(m);
 }
 
+// x[r] += float(acc[r]) * dequant_scale(*absmax) * w_scale[r]: the residual
+// epilogue applied to int32 row sums reduced across a tensor-parallel group.
+__global__ void residual_acc_kernel(float* x, const int32_t* acc, const float* absmax, const float* w_scale, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float v = __fmul_rn(__fmul_rn(static_cast<float>(acc[i]), dequant_scale(*absmax)), w_scale[i]);
+    x[i] = __fadd_rn(x[i], v);
+}
+
 __global__ void add_kernel(float* x, const float* y, int n) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) x[i] = __fadd_rn(x[i], y[i]);
@@ -383,5 +392,14 @@ extern "C" int h4b_graph_destroy(void* graph) {
     if (h->exec) cudaGraphExecDestroy(h->exec);
     if (h->graph) cudaGraphDestroy(h->graph);
     delete h;
+    return 0;
+}
+
+extern "C" int h4b_residual_acc(float* x, const int32_t* acc, const float* absmax, const float* w_scales, int n,
+                                void* stream) {
+    if (!x || !acc || !absmax || !w_scales || n < 1) return H4B_EINVAL;
+    h4b::residual_acc_kernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, acc, absmax, w_scales,
+                                                                                           n);
+    H4B_CUDA_TRY(cudaGetLastError());
     return 0;
 }

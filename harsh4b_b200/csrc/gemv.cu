@@ -380,7 +380,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
         for (int i = tid; i < nrows; i += kGemvThreads) {
             const float v = value(i);
-            if constexpr (EPI == EPI_STORE) a.out[r0 + i] = v;
+            if constexpr (EPI == EPI_STORE) {
+                if (a.out) a.out[r0 + i] = v;
+            }
             else a.out[r0 + i] = __fadd_rn(a.out[r0 + i], v);
             if (a.acc_out) a.acc_out[r0 + i] = acc_s[i];
         }
@@ -526,6 +528,7 @@ int prepare_kernels() {
     int r = 0;
     if ((r = set_smem_limits<PRO_INT8, EPI_STORE>()) || (r = set_smem_limits<PRO_QUANT, EPI_STORE>()) ||
         (r = set_smem_limits<PRO_RMSNORM, EPI_STORE>()) || (r = set_smem_limits<PRO_QUANT_ABSMAX, EPI_RESIDUAL>()) ||
+        (r = set_smem_limits<PRO_QUANT_ABSMAX, EPI_STORE>()) ||
         (r = set_smem_limits<PRO_RMSNORM, EPI_SWIGLU>()) || (r = set_smem_limits<PRO_RMSNORM, EPI_ARGMAX>()))
         return r;
     if ((r = prepare_other_kernels())) return r;
@@ -587,6 +590,8 @@ int launch_gemv(int pro, int epi, GemvArgs a, cudaStream_t stream, bool pdl) {
     if (pro == PRO_RMSNORM && epi == EPI_STORE) return launch_slots<PRO_RMSNORM, EPI_STORE>(a, p, stream, pdl);
     if (pro == PRO_QUANT_ABSMAX && epi == EPI_RESIDUAL)
         return launch_slots<PRO_QUANT_ABSMAX, EPI_RESIDUAL>(a, p, stream, pdl);
+    if (pro == PRO_QUANT_ABSMAX && epi == EPI_STORE)
+        return launch_slots<PRO_QUANT_ABSMAX, EPI_STORE>(a, p, stream, pdl);
     if (pro == PRO_RMSNORM && epi == EPI_SWIGLU) return launch_slots<PRO_RMSNORM, EPI_SWIGLU>(a, p, stream, pdl);
     if (pro == PRO_RMSNORM && epi == EPI_ARGMAX) return launch_slots<PRO_RMSNORM, EPI_ARGMAX>(a, p, stream, pdl);
     return H4B_EUNSUPPORTED;
@@ -617,4 +622,18 @@ extern "C" int h4b_int4_gemv_fused_quant(const float* values, const uint8_t* wei
     a.w = weights; a.wscale = scales; a.rows = rows; a.width = width;
     a.xin = values; a.out = output; a.acc_out = acc; a.act_scale_out = act_scale_out;
     return h4b::launch_gemv(h4b::PRO_QUANT, h4b::EPI_STORE, a, static_cast<cudaStream_t>(stream), false);
+}
+
+// Quantisation with a given absmax (a device scalar, e.g. the max over the
+// ranks of a tensor-parallel group) fused with the GEMV; writes the int32
+// row sums (and the fp32 rows when `output` is not null).
+extern "C" int h4b_int4_gemv_absmax(const float* values, const float* absmax, const uint8_t* weights,
+                                    const float* scales, float* output, int32_t* acc, int rows, int width,
+                                    void* stream) {
+    if (!values || !absmax || !weights || !scales || !acc) return H4B_EINVAL;
+    if (reinterpret_cast<uintptr_t>(values) & 15) return H4B_EINVAL;
+    h4b::GemvArgs a = {};
+    a.w = weights; a.wscale = scales; a.rows = rows; a.width = width;
+    a.xin = values; a.absmax_in = absmax; a.out = output; a.acc_out = acc;
+    return h4b::launch_gemv(h4b::PRO_QUANT_ABSMAX, h4b::EPI_STORE, a, static_cast<cudaStream_t>(stream), false);
 }

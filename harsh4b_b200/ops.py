@@ -177,3 +177,23 @@ def int4_gemm_rows(values: torch.Tensor, weights: torch.Tensor, scales: torch.Te
     """fp32 [M, K] -> fp32 [M, N]: per-token quantisation, then the batched GEMM."""
     x8, act_scales, sums = quantize_rows(values)
     return int4_gemm(x8, act_scales, sums, weights, scales)
+
+
+def int4_gemv_absmax(values: torch.Tensor, absmax: torch.Tensor, weights: torch.Tensor, scales: torch.Tensor,
+                     acc: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Quantise with a given device absmax, GEMV, int32 row sums into `acc`."""
+    rows, packed = weights.shape
+    check(lib().h4b_int4_gemv_absmax(_dev(values, torch.float32, "values"), _dev(absmax, torch.float32, "absmax"),
+                                     _dev(weights, torch.uint8, "weights"), _dev(scales, torch.float32, "scales"),
+                                     _dev(out, torch.float32, "out") if out is not None else None,
+                                     _dev(acc, torch.int32, "acc"), rows, 2 * packed, stream_handle()),
+          "h4b_int4_gemv_absmax")
+    return acc
+
+
+def residual_acc(x: torch.Tensor, acc: torch.Tensor, absmax: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """x += float(acc) * dequant(absmax) * scales (in place)."""
+    check(lib().h4b_residual_acc(_dev(x, torch.float32, "x"), _dev(acc, torch.int32, "acc"),
+                                 _dev(absmax, torch.float32, "absmax"), _dev(scales, torch.float32, "scales"),
+                                 x.numel(), stream_handle()), "h4b_residual_acc")
+    return x

@@ -124,6 +124,16 @@ int h4b_sample(float *logits, int vocab, const int32_t *generated, int n_generat
                float *topk_probs_out, void *scratch, void *stream);
 long long h4b_sample_scratch_bytes(int vocab, int top_k);
 
+/* ---- tensor parallelism (o and down split along K across ranks) ------------
+ * Quantise `values` with the given device absmax (the max over the ranks),
+ * then litespark_int4_i8_gemv over the local K slice: int32 row sums into
+ * `acc` (to be summed across ranks), fp32 rows into `output` if not null. */
+int h4b_int4_gemv_absmax(const float *values, const float *absmax, const uint8_t *weights, const float *scales,
+                         float *output, int32_t *acc, int rows, int width, void *stream);
+/* x[r] += float(acc[r]) * (max(*absmax, 1e-5) / 127) * w_scales[r] -- the
+ * residual epilogue of the reduced sums. */
+int h4b_residual_acc(float *x, const int32_t *acc, const float *absmax, const float *w_scales, int n, void *stream);
+
 /* ---- batched (M > 1 tokens): batched decode and prefill ---------------------
  * Per-token quantisation of `rows` activations of `width` floats (the
  * quantize_activation contract applied to each row), also returning each
