@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* v, int 
     }
 }
 
-int launch_int4_gemm(const GemmArgs& g, cudaStream_t stream) {
+int launch_int4_gemm_mma(const GemmArgs& g, cudaStream_t stream) {
     if (g.M < 1 || g.N < 1 || g.K < 1) return H4B_EINVAL;
     if (g.N % kGemmRows || g.K % kGemmK) return H4B_EUNSUPPORTED;
     const dim3 grid(g.N / kGemmRows, (g.M + kGemmTok - 1) / kGemmTok);
@@ -181,19 +181,3 @@ int launch_int4_gemm(const GemmArgs& g, cudaStream_t stream) {
 }
 
 }  // namespace h4b
-
-extern "C" int h4b_quantize_rows(const float* values, int8_t* quantized, float* scales, int32_t* sums, int rows,
-                                 int width, void* stream) {
-    if (!values || !quantized || !scales || !sums || rows < 1 || width < 1) return H4B_EINVAL;
-    h4b::quantize_rows_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(values, width, quantized, scales,
-                                                                                 sums);
-    H4B_CUDA_TRY(cudaGetLastError());
-    return 0;
-}
-
-extern "C" int h4b_int4_gemm(const int8_t* x8, const float* act_scales, const int32_t* act_sums, const uint8_t* weights,
-                             const float* scales, float* output, int tokens, int rows, int width, void* stream) {
-    if (!x8 || !act_scales || !act_sums || !weights || !scales || !output) return H4B_EINVAL;
-    h4b::GemmArgs g{x8, act_scales, act_sums, weights, scales, output, tokens, rows, width};
-    return h4b::launch_int4_gemm(g, static_cast<cudaStream_t>(stream));
-}

@@ -1,0 +1,387 @@
+// Batched int4 x int8 GEMM on the 5th-generation tensor cores (tcgen05 with
+// the accumulator in tensor memory), fed by TMA:
+//   out[m][n] = float(sum_k w[n][k] * x[m][k]) * act_scale[m] * w_scale[n]
+// the same contract and result bits as gemm.cu (integer sums are exact).
+//
+// Tile: 128 weight rows (the MMA's M) x TOK tokens (its N: 64, 128 or 256),
+// K advancing 128 per pipeline stage. A CTA has six warps:
+//   warp 4  lane 0: TMA producer -- per stage, the packed weight tile
+//           (128 rows x 64 bytes, no swizzle) and the activation tile (TOK
+//           rows x 128 bytes, 128-byte swizzle) land on the stage's `full`
+//           mbarrier; warp 4 also allocates and frees the tensor memory;
+//   warps 0-3: unpack the packed tile into signed int8 codes in the
+//           K-major 128-byte-swizzled layout the MMA reads, then arrive on
+//           `aready`; after the last stage they are the epilogue, one TMEM
+//           lane quarter (32 rows) per warp;
+//   warp 5  lane 0: issues tcgen05.mma kind::i8 (A s8 weights, B s8
+//           activations, D s32 in TMEM), 4 per stage (K = 32 each), and
+//           tcgen05.commit to the stage's `empty` mbarrier, which frees the
+//           stage for the producer; a final commit signals the epilogue.
+// Every wait is bounded (mbar_wait). A role whose wait runs out reports
+// kStatusWaitTimeout, marks the CTA as failed and stops issuing; the
+// producer still waits for the copies it issued, the MMA thread still
+// commits (so the epilogue's wait ends once its MMAs are done), and the
+// tensor memory is freed on every path.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+namespace h4b {
+
+constexpr int kTcRows = 128;     // weight rows per CTA (MMA M)
+constexpr int kTcK = 128;        // k per stage: one 128-byte swizzle atom of int8
+constexpr int kTcThreads = 192;  // warps 0-3 unpack + epilogue, warp 4 TMA + TMEM, warp 5 MMA
+
+template <int TOK>
+struct TcCfg {
+    static constexpr int kABytes = kTcRows * kTcK;           // unpacked weights, int8
+    static constexpr int kBBytes = TOK * kTcK;               // activations, int8
+    static constexpr int kPackedBytes = kTcRows * kTcK / 2;  // packed weights
+    static constexpr int kBOff = kABytes;
+    static constexpr int kPackedOff = kABytes + kBBytes;
+    static constexpr int kStageBytes = kABytes + kBBytes + kPackedBytes;
+    static constexpr int kStages = TOK == 256 ? 3 : (TOK == 128 ? 5 : 6);
+    static constexpr int kBarrierBytes = 256;
+    static constexpr int kSmem = kStages * kStageBytes + kBarrierBytes + 1024;  // + alignment slack
+    static constexpr uint32_t kTmemCols = TOK;
+    static_assert(kStageBytes % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
+    static_assert(kSmem <= 232448, "shared memory per CTA");
+    static_assert(3 * kStages * 8 + 16 <= kBarrierBytes, "barrier area");
+};
+
+struct TcArgs {
+    const float* act_scale;  // [M]
+    const float* w_scale;    // [N]
+    float* out;              // [M][N]
+    int M, N, K;
+};
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major operand in the 128-byte
+// swizzle layout: 8-row groups of 1024 bytes (stride byte offset 1024), the
+// leading byte offset unused (encoded 16 bytes), descriptor version 1,
+// layout type 2 (SWIZZLE_128B). The tile base is 1024-byte aligned.
+__device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
+    return static_cast<uint64_t>((smem_addr(tile) >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+// Instruction descriptor: D s32 (bits 4-5 = 2), A s8 (bits 7-9 = 1), B s8
+// (bits 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+template <int TOK>
+__host__ __device__ constexpr uint32_t tc_idesc() {
+    return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(TOK >> 3) << 17) |
+           (static_cast<uint32_t>(kTcRows >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma_i8(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Two packed bytes of w (picked by the byte_perm selector: 0x1100 the low
+// pair, 0x3322 the high pair) -> signed int8 codes lo0 hi0 lo1 hi1: a nibble
+// n read as u = n ^ 8 is n + 8 in 0..15, and a bytewise u - 8 is n in two's
+// complement.
+__device__ __forceinline__ uint32_t nib_s8(uint32_t w, uint32_t selector) {
+    const uint32_t t = __byte_perm(w, 0, selector);
+    return __vsub4(((t & 0x000F000Fu) | ((t >> 4) & 0x0F000F00u)) ^ 0x08080808u, 0x08080808u);
+}
+
+template <int TOK>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    int4_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                        const TcArgs g) {
+    using C = TcCfg<TOK>;
+    extern __shared__ uint8_t tc_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+    uint64_t* aready = full + C::kStages;
+    uint64_t* empty = aready + C::kStages;
+    uint64_t* accfull = empty + C::kStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accfull + 1);
+    volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * kTcRows, m0 = blockIdx.y * TOK;
+    const int steps = g.K / kTcK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&aready[s], 4);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accfull, 1);
+        *failed = wait_failed_before() ? 1 : 0;
+        fence_mbar_init();
+    }
+    if (warp == 4) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_addr(tmem_slot)), "r"(C::kTmemCols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    auto stage = [&](int s) { return smem + s * C::kStageBytes; };
+
+    if (warp == 4) {
+        if (lane == 0) {  // TMA producer
+            int issued = 0;
+            if (!*failed) {
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+                asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+                for (int it = 0; it < steps; ++it) {
+                    const int s = it % C::kStages;
+                    const uint32_t round = it / C::kStages;
+                    if (*failed) break;
+                    if (it >= C::kStages && !mbar_wait(&empty[s], (round - 1) & 1)) {
+                        *failed = 1;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], C::kPackedBytes + C::kBBytes);
+                    tma_load_2d(stage(s) + C::kPackedOff, &wmap, it * (kTcK / 2), n0, &full[s]);
+                    tma_load_2d(stage(s) + C::kBOff, &xmap, it * kTcK, m0, &full[s]);
+                    issued = it + 1;
+                }
+            }
+            // the copies issued must land before the CTA may exit
+            for (int it = issued > C::kStages ? issued - C::kStages : 0; it < issued; ++it)
+                mbar_wait(&full[it % C::kStages], (it / C::kStages) & 1);
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = tc_idesc<TOK>();
+            for (int it = 0; it < steps && !*failed; ++it) {
+                const int s = it % C::kStages;
+                const uint32_t parity = (it / C::kStages) & 1;
+                if (!mbar_wait(&full[s], parity) || !mbar_wait(&aready[s], parity)) {
+                    *failed = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint64_t adesc = sw128_desc(stage(s)), bdesc = sw128_desc(stage(s) + C::kBOff);
+#pragma unroll
+                for (int kk = 0; kk < kTcK / 32; ++kk)  // +32 bytes along K = +2 in the start-address field
+                    tc_mma_i8(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (it | kk) != 0);
+                tc_commit(&empty[s]);
+            }
+            tc_commit(accfull);  // arrives once every MMA issued above has completed
+        }
+    } else {  // warps 0-3: unpack, then epilogue
+        const int t = threadIdx.x;
+        for (int it = 0; it < steps; ++it) {
+            const int s = it % C::kStages;
+            const bool ok = __all_sync(0xffffffffu, !*failed && mbar_wait(&full[s], (it / C::kStages) & 1));
+            if (!ok) {
+                if (lane == 0) *failed = 1;
+                break;
+            }
+            const uint8_t* packed = stage(s) + C::kPackedOff;
+            uint8_t* a = stage(s);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int c = i * 128 + t;  // 16-byte packed chunk: row c / 4, k bytes 32 * (c % 4) ..
+                const int row = c >> 2, piece = c & 3, sw = row & 7;
+                const uint4 w = *reinterpret_cast<const uint4*>(packed + c * 16);
+                const uint4 lo = make_uint4(nib_s8(w.x, 0x1100), nib_s8(w.x, 0x3322), nib_s8(w.y, 0x1100),
+                                            nib_s8(w.y, 0x3322));
+                const uint4 hi = make_uint4(nib_s8(w.z, 0x1100), nib_s8(w.z, 0x3322), nib_s8(w.w, 0x1100),
+                                            nib_s8(w.w, 0x3322));
+                uint8_t* rowp = a + (row >> 3) * 1024 + sw * 128;
+                *reinterpret_cast<uint4*>(rowp + (((2 * piece) ^ sw) << 4)) = lo;
+                *reinterpret_cast<uint4*>(rowp + (((2 * piece + 1) ^ sw) << 4)) = hi;
+            }
+            fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core's reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&aready[s]);
+        }
+        // epilogue: warp w reads TMEM lanes 32w..32w+31 = weight rows n0 + 32w + lane
+        const bool done = __all_sync(0xffffffffu, mbar_wait(accfull, 0) && !*failed);
+        tc_fence_after();
+        if (done) {
+            const int row = n0 + warp * 32 + lane;
+            const float ws = g.w_scale[row];
+            const uint32_t base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+#pragma unroll 1
+            for (int c0 = 0; c0 < TOK; c0 += 16) {
+                uint32_t v[16];
+                tmem_ld16(base + c0, v);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int m = m0 + c0 + j;
+                    if (m < g.M) {
+                        g.out[static_cast<size_t>(m) * g.N + row] =
+                            __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[j])), g.act_scale[m]), ws);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols)
+                     : "memory");
+    }
+}
+
+}  // namespace h4b
+
+#include <mutex>
+#include <unordered_map>
+
+namespace h4b {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda); encoded maps are cached per (address, shape, box).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+struct MapKey {
+    const void* base;
+    uint64_t inner, outer;
+    uint32_t box_inner, box_outer, swizzle;
+    bool operator==(const MapKey& o) const {
+        return base == o.base && inner == o.inner && outer == o.outer && box_inner == o.box_inner &&
+               box_outer == o.box_outer && swizzle == o.swizzle;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey& k) const {
+        size_t h = reinterpret_cast<uintptr_t>(k.base);
+        for (uint64_t v : {k.inner, k.outer, uint64_t(k.box_inner) << 32 | k.box_outer, uint64_t(k.swizzle)})
+            h = h * 1000003u ^ static_cast<size_t>(v);
+        return h;
+    }
+};
+
+// A row-major uint8 matrix [outer][inner] as a 2-D tensor map with box
+// [box_outer][box_inner]; rows past `outer` read as zeros.
+bool byte_matrix_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                     uint32_t box_outer, bool swizzle128) {
+    static std::mutex lock;
+    static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+    const MapKey key{base, inner, outer, box_inner, box_outer, swizzle128 ? 1u : 0u};
+    std::lock_guard<std::mutex> guard(lock);
+    auto hit = cache.find(key);
+    if (hit != cache.end()) {
+        *out = hit->second;
+        return true;
+    }
+    auto encode = tensor_map_encoder();
+    if (!encode) return false;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {inner};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t elem[2] = {1, 1};
+    if (encode(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE,
+               swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    if (cache.size() > 8192) cache.clear();
+    cache.emplace(key, *out);
+    return true;
+}
+
+bool tc_gemm_supported(const GemmArgs& g) {
+    return g.N % kTcRows == 0 && g.K % kTcK == 0 && (reinterpret_cast<uintptr_t>(g.w) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(g.x) & 15) == 0 && tensor_map_encoder() != nullptr;
+}
+
+template <int TOK>
+int launch_tc(const GemmArgs& g, cudaStream_t stream) {
+    using C = TcCfg<TOK>;
+    static std::once_flag once;
+    static cudaError_t attr = cudaSuccess;
+    std::call_once(once, [] {
+        attr = cudaFuncSetAttribute(int4_gemm_tc_kernel<TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    });
+    H4B_CUDA_TRY(attr);
+    CUtensorMap wmap, xmap;
+    if (!byte_matrix_map(&wmap, g.w, static_cast<uint64_t>(g.K) / 2, g.N, kTcK / 2, kTcRows, false) ||
+        !byte_matrix_map(&xmap, g.x, g.K, g.M, kTcK, TOK, true))
+        return H4B_EUNSUPPORTED;
+    const TcArgs a{g.act_scale, g.w_scale, g.out, g.M, g.N, g.K};
+    const dim3 grid(g.N / kTcRows, (g.M + TOK - 1) / TOK);
+    int4_gemm_tc_kernel<TOK><<<grid, kTcThreads, C::kSmem, stream>>>(wmap, xmap, a);
+    H4B_CUDA_TRY(cudaGetLastError());
+    return 0;
+}
+
+// kernel: 0 = tensor-core tcgen05 where the shape allows it (N % 128, K % 128),
+// else mma.sync; 1 = tcgen05 only; 2 = mma.sync only.
+int launch_int4_gemm(const GemmArgs& g, cudaStream_t stream, int kernel = 0) {
+    if (g.M < 1 || g.N < 1 || g.K < 1) return H4B_EINVAL;
+    if (kernel < 0 || kernel > 2) return H4B_EINVAL;
+    if (kernel == 2 || (kernel == 0 && !tc_gemm_supported(g))) return launch_int4_gemm_mma(g, stream);
+    if (!tc_gemm_supported(g)) return H4B_EUNSUPPORTED;
+    if (g.M <= 64) return launch_tc<64>(g, stream);
+    if (g.M <= 128) return launch_tc<128>(g, stream);
+    return launch_tc<256>(g, stream);
+}
+
+}  // namespace h4b
+
+extern "C" int h4b_quantize_rows(const float* values, int8_t* quantized, float* scales, int32_t* sums, int rows,
+                                 int width, void* stream) {
+    if (!values || !quantized || !scales || !sums || rows < 1 || width < 1) return H4B_EINVAL;
+    h4b::quantize_rows_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(values, width, quantized, scales,
+                                                                                 sums);
+    H4B_CUDA_TRY(cudaGetLastError());
+    return 0;
+}
+
+extern "C" int h4b_int4_gemm_ex(const int8_t* x8, const float* act_scales, const int32_t* act_sums,
+                                const uint8_t* weights, const float* scales, float* output, int tokens, int rows,
+                                int width, int kernel, void* stream) {
+    if (!x8 || !act_scales || !act_sums || !weights || !scales || !output) return H4B_EINVAL;
+    h4b::GemmArgs g{x8, act_scales, act_sums, weights, scales, output, tokens, rows, width};
+    return h4b::launch_int4_gemm(g, static_cast<cudaStream_t>(stream), kernel);
+}
+
+extern "C" int h4b_int4_gemm(const int8_t* x8, const float* act_scales, const int32_t* act_sums, const uint8_t* weights,
+                             const float* scales, float* output, int tokens, int rows, int width, void* stream) {
+    return h4b_int4_gemm_ex(x8, act_scales, act_sums, weights, scales, output, tokens, rows, width, 0, stream);
+}

@@ -6,4 +6,5 @@
 #include "persistent.cu"
 #include "sample.cu"
 #include "gemm.cu"
+#include "gemm_tc.cu"
 #include "batch.cu"

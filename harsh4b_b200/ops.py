@@ -160,23 +160,28 @@ def quantize_rows(values: torch.Tensor):
     return x8, scales, sums
 
 
+GEMM_KERNELS = {"auto": 0, "tcgen05": 1, "mma_sync": 2}
+
+
 def int4_gemm(x8: torch.Tensor, act_scales: torch.Tensor, act_sums: torch.Tensor, weights: torch.Tensor,
-              scales: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """h4b_int4_gemm: fp32 [M, N] from int8 activations [M, K] and int4 weights [N, K/2]."""
+              scales: torch.Tensor, out: torch.Tensor | None = None, kernel: str = "auto") -> torch.Tensor:
+    """h4b_int4_gemm_ex: fp32 [M, N] from int8 activations [M, K] and int4
+    weights [N, K/2]; `kernel` picks tcgen05, mma.sync or the automatic choice."""
     tokens, width = x8.shape
     rows = weights.shape[0]
     out = torch.empty(tokens, rows, dtype=torch.float32, device=x8.device) if out is None else out
-    check(lib().h4b_int4_gemm(_dev(x8, torch.int8, "x8"), _dev(act_scales, torch.float32, "act_scales"),
-                              _dev(act_sums, torch.int32, "act_sums"), _dev(weights, torch.uint8, "weights"),
-                              _dev(scales, torch.float32, "scales"), _dev(out, torch.float32, "out"), tokens, rows,
-                              width, stream_handle()), "h4b_int4_gemm")
+    check(lib().h4b_int4_gemm_ex(_dev(x8, torch.int8, "x8"), _dev(act_scales, torch.float32, "act_scales"),
+                                 _dev(act_sums, torch.int32, "act_sums"), _dev(weights, torch.uint8, "weights"),
+                                 _dev(scales, torch.float32, "scales"), _dev(out, torch.float32, "out"), tokens,
+                                 rows, width, GEMM_KERNELS[kernel], stream_handle()), "h4b_int4_gemm_ex")
     return out
 
 
-def int4_gemm_rows(values: torch.Tensor, weights: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+def int4_gemm_rows(values: torch.Tensor, weights: torch.Tensor, scales: torch.Tensor,
+                   kernel: str = "auto") -> torch.Tensor:
     """fp32 [M, K] -> fp32 [M, N]: per-token quantisation, then the batched GEMM."""
     x8, act_scales, sums = quantize_rows(values)
-    return int4_gemm(x8, act_scales, sums, weights, scales)
+    return int4_gemm(x8, act_scales, sums, weights, scales, kernel=kernel)
 
 
 def int4_gemv_absmax(values: torch.Tensor, absmax: torch.Tensor, weights: torch.Tensor, scales: torch.Tensor,

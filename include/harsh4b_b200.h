@@ -145,9 +145,17 @@ int h4b_quantize_rows(const float *values, int8_t *quantized, float *scales, int
  * m < tokens, n < rows: litespark_int4_i8_gemv (litespark_int4.cpp:78-84)
  * applied to `tokens` activations at once on the tensor cores; row m equals
  * the single-token GEMV of token m bit for bit. act_sums[m] = sum_k x8[m][k]
- * (from h4b_quantize_rows). rows % 128 == 0 and width % 64 == 0. */
+ * (from h4b_quantize_rows). rows % 128 == 0 and width % 64 == 0; with
+ * width % 128 == 0 the tcgen05 kernel (TMA-fed, accumulators in tensor
+ * memory) runs, otherwise the mma.sync kernel. */
 int h4b_int4_gemm(const int8_t *x8, const float *act_scales, const int32_t *act_sums, const uint8_t *weights,
                   const float *scales, float *output, int tokens, int rows, int width, void *stream);
+
+/* h4b_int4_gemm with an explicit kernel: 0 = as h4b_int4_gemm, 1 = tcgen05
+ * only (H4B_EUNSUPPORTED when the shape does not allow it), 2 = mma.sync
+ * only. Both give the same bits. */
+int h4b_int4_gemm_ex(const int8_t *x8, const float *act_scales, const int32_t *act_sums, const uint8_t *weights,
+                     const float *scales, float *output, int tokens, int rows, int width, int kernel, void *stream);
 
 /* ---- model level ----------------------------------------------------------- */
 

@@ -30,9 +30,15 @@ def _oracle_rows(weights, scales, values):
     return np.stack(outs), np.stack(x8s), np.array(act, dtype=np.float32), np.array(sums)
 
 
-@pytest.mark.parametrize("tokens,rows,width", [(2, 256, 2560), (17, 6144, 2560), (64, 2560, 9728),
-                                               (130, 2560, 4096), (5, 128, 64)])
-def test_gemm_rows_bit_exact(tokens, rows, width):
+SHAPES = [(2, 256, 2560), (17, 6144, 2560), (64, 2560, 9728), (100, 1024, 2560), (130, 2560, 4096),
+          (300, 384, 2560), (5, 128, 64)]
+
+
+@pytest.mark.parametrize("kernel", ["tcgen05", "mma_sync", "auto"])
+@pytest.mark.parametrize("tokens,rows,width", SHAPES)
+def test_gemm_rows_bit_exact(tokens, rows, width, kernel):
+    if kernel == "tcgen05" and width % 128:
+        pytest.skip("the tcgen05 kernel needs width % 128 == 0")
     rng = np.random.default_rng(tokens * 7 + rows)
     weights, scales, values = _problem(rng, tokens, rows, width)
     want, want_x8, want_scale, want_sum = _oracle_rows(weights, scales, values)
@@ -41,8 +47,39 @@ def test_gemm_rows_bit_exact(tokens, rows, width):
     np.testing.assert_array_equal(x8.cpu().numpy(), want_x8)
     np.testing.assert_array_equal(act.cpu().numpy(), want_scale)
     np.testing.assert_array_equal(sums.cpu().numpy(), want_sum)
-    out = ops.int4_gemm(x8, act, sums, torch.from_numpy(weights).cuda(), torch.from_numpy(scales).cuda())
+    out = ops.int4_gemm(x8, act, sums, torch.from_numpy(weights).cuda(), torch.from_numpy(scales).cuda(),
+                        kernel=kernel)
     np.testing.assert_array_equal(out.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("rows,width", [(2560, 2560), (9728, 2560), (2560, 9728)])
+def test_tcgen05_equals_mma_sync_at_prefill_size(rows, width):
+    """2048 tokens (a prefill): the two tensor-core kernels give the same bits
+    (each is pinned to the oracle above at smaller sizes)."""
+    g = torch.Generator(device="cuda").manual_seed(rows + width)
+    x8 = torch.randint(-127, 128, (2048, width), dtype=torch.int8, device="cuda", generator=g)
+    act = torch.rand(2048, device="cuda", generator=g) * 1e-2
+    sums = x8.to(torch.int32).sum(dim=1, dtype=torch.int32)
+    codes = torch.randint(-7, 8, (rows, width), dtype=torch.int16, device="cuda", generator=g)
+    w = ((codes[:, 0::2] & 0xF) | ((codes[:, 1::2] & 0xF) << 4)).to(torch.uint8)
+    scales = torch.rand(rows, device="cuda", generator=g) * 1e-2
+    a = ops.int4_gemm(x8, act, sums, w, scales, kernel="tcgen05")
+    b = ops.int4_gemm(x8, act, sums, w, scales, kernel="mma_sync")
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    dense = (codes.to(torch.float64) @ x8[:64].to(torch.float64).T).T  # exact integers in float64
+    want = (dense.to(torch.float32) * act[:64, None]) * scales[None, :]
+    assert torch.equal(a[:64], want[:64])
+
+
+def test_tcgen05_rejects_width_not_multiple_of_128():
+    x8 = torch.zeros(4, 64, dtype=torch.int8, device="cuda")
+    act = torch.ones(4, device="cuda")
+    sums = torch.zeros(4, dtype=torch.int32, device="cuda")
+    w = torch.zeros(128, 32, dtype=torch.uint8, device="cuda")
+    s = torch.ones(128, device="cuda")
+    with pytest.raises(ValueError):
+        ops.int4_gemm(x8, act, sums, w, s, kernel="tcgen05")
 
 
 def test_gemm_rejects_unsupported_shapes():
