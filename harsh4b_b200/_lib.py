@@ -49,6 +49,14 @@ class BatchStateDesc(ctypes.Structure):
                            "attn_counters")]
 
 
+class PrefillScratchDesc(ctypes.Structure):
+    """Mirror of ``h4b_prefill_scratch``."""
+
+    _fields_ = [("max_tokens", _i32), ("attn_queries", _i32)] + [
+        (n, _vp) for n in ("x", "x8", "act_scale", "act_sum", "qkv", "attended", "gate_up", "act", "proj", "tokens",
+                           "positions", "attn_partials", "attn_counters")]
+
+
 _SIGNATURES = {
     "h4b_prepare": [],
     "h4b_get_status": [_vp],
@@ -81,6 +89,8 @@ _SIGNATURES = {
     "h4b_int4_gemv_absmax": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp],
     "h4b_residual_acc": [_vp, _vp, _vp, _vp, _i32, _vp],
     "h4b_decode_batch": [ctypes.POINTER(ModelDesc), ctypes.POINTER(BatchStateDesc), _vp],
+    "h4b_prefill": [ctypes.POINTER(ModelDesc), ctypes.POINTER(StateDesc), ctypes.POINTER(PrefillScratchDesc), _i32,
+                    _vp],
 }
 _RESTYPES = {"h4b_persistent_exchange_words": ctypes.c_longlong, "h4b_sample_scratch_bytes": ctypes.c_longlong}
 

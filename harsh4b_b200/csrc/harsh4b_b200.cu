@@ -8,3 +8,4 @@
 #include "gemm.cu"
 #include "gemm_tc.cu"
 #include "batch.cu"
+#include "prefill.cu"

@@ -1,0 +1,179 @@
+// Prefill: `count` prompt tokens of one session in one call, through the
+// batched GEMMs (the reference feeds a prompt one forward_token at a time,
+// cpu_lightspark.py:809-810 and inference_runtime.py:177-181).
+//
+// Per layer the prompt rows go through the same operations as a decode
+// token, M rows at a time: RMSNorm + per-token quantisation, the tensor-core
+// int4 GEMM (gemm_tc.cu) for qkv / o / gate-up / down, residual adds and
+// SwiGLU. Attention runs in two launches so no query reads a key that
+// another CTA of the same launch is writing:
+//   1. prefill_rope_append_kernel: q/k RMSNorm and RoPE for every prompt
+//      token and head (the decode kernel's norm_rope), q written back in
+//      place, k and v appended to the session's cache at their positions;
+//   2. gqa_split_kernel with one batch entry per query, all on the one
+//      cache (batch stride 0), positions p0 + i, and no append.
+// The second launch reads back the cache values the first one stored, in
+// the cache precision, exactly as the decode kernel stages its own new key
+// and value, so every prompt row equals a chain decode step with the same
+// attention splits bit for bit. Only the last row goes through the LM head
+// (its logits and greedy token are what forward_token returns).
+
+namespace h4b {
+
+__global__ void prefill_setup_kernel(const int32_t* position, int count, int capacity, int32_t* positions,
+                                     unsigned long long* argmax_key) {
+    const int p0 = *position;
+    const bool fits = p0 >= 0 && p0 + count <= capacity;
+    if (!fits && blockIdx.x == 0 && threadIdx.x == 0) report(kStatusBadPosition);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x)
+        positions[i] = fits ? p0 + i : -1;  // -1: the attention kernels skip the row
+    if (blockIdx.x == 0 && threadIdx.x == 0) *argmax_key = 0ull;
+}
+
+// One warp per (prompt token, head): heads [0, q_heads) are queries,
+// [q_heads, q_heads + kv_heads) keys (+ the matching value row).
+template <typename KV>
+__global__ void __launch_bounds__(32) prefill_rope_append_kernel(float* qkv, int qkv_stride, int q_heads, int kv_heads,
+                                                                 const float* q_norm, const float* k_norm,
+                                                                 const float* rope_cos, const float* rope_sin,
+                                                                 float eps, const int32_t* positions, KV* kcache,
+                                                                 KV* vcache, long long head_stride,
+                                                                 long long time_stride) {
+    const int i = blockIdx.x, head = blockIdx.y, lane = threadIdx.x;
+    const int pos = positions[i];
+    if (pos < 0) return;
+    const float* cs = rope_cos + static_cast<long long>(pos) * (kHeadDim / 2);
+    const float* sn = rope_sin + static_cast<long long>(pos) * (kHeadDim / 2);
+    float* row = qkv + static_cast<long long>(i) * qkv_stride;
+    if (head < q_heads) {
+        float4* q = reinterpret_cast<float4*>(row + static_cast<long long>(head) * kHeadDim) + lane;
+        *q = norm_rope(*q, q_norm, cs, sn, eps, lane);
+        return;
+    }
+    const int kvh = head - q_heads;
+    const float* k = row + static_cast<long long>(q_heads + kvh) * kHeadDim;
+    const float* v = row + static_cast<long long>(q_heads + kv_heads + kvh) * kHeadDim;
+    const float4 kn = norm_rope(*(reinterpret_cast<const float4*>(k) + lane), k_norm, cs, sn, eps, lane);
+    const long long at = kvh * head_stride + static_cast<long long>(pos) * time_stride + 4 * lane;
+    store4<KV>(kcache + at, kn);
+    store4<KV>(vcache + at, *(reinterpret_cast<const float4*>(v) + lane));
+}
+
+__global__ void prefill_finish_kernel(const unsigned long long* argmax_key, int32_t* next_token, int32_t* token,
+                                      int32_t* position, int count) {
+    if (threadIdx.x == 0) {
+        const int32_t id = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(*argmax_key & 0xFFFFFFFFull));
+        *next_token = id;
+        if (token) *token = id;
+        *position += count;
+    }
+}
+
+int validate_prefill(const h4b_model* m, const h4b_state* s, const h4b_prefill_scratch* p, int count) {
+    int rc = validate(m, s);
+    if (rc) return rc;
+    if (!p || count < 1 || count > p->max_tokens || p->attn_queries < 1) return H4B_EINVAL;
+    const void* required[] = {p->x, p->x8, p->act_scale, p->act_sum, p->qkv, p->attended, p->gate_up, p->act,
+                              p->proj, p->tokens, p->positions};
+    for (const void* q : required)
+        if (!q || (reinterpret_cast<uintptr_t>(q) & 15)) return H4B_EINVAL;
+    if (s->attn_splits > 1 && (!p->attn_partials || !p->attn_counters)) return H4B_EINVAL;
+    return 0;
+}
+
+int prefill(const h4b_model* m, const h4b_state* s, const h4b_prefill_scratch* p, int count, cudaStream_t stream) {
+    int rc = validate_prefill(m, s, p, count);
+    if (rc) return rc;
+    const int H = m->hidden, I = m->intermediate, d = m->head_dim;
+    const int q_size = m->heads * d, kv_size = m->kv_heads * d, qkv_rows = q_size + 2 * kv_size;
+    const size_t kv_layer = static_cast<size_t>(m->kv_heads) * s->capacity * d;  // elements
+    const size_t eb = s->kv_dtype == 0 ? 4 : 2;
+    auto gemm = [&](const uint8_t* w, const float* ws, float* out, int rows, int width) {
+        GemmArgs g{p->x8, p->act_scale, p->act_sum, w, ws, out, count, rows, width};
+        return launch_int4_gemm(g, stream);
+    };
+    auto norm_quant = [&](const float* gamma) {
+        batch_rmsnorm_quant_kernel<<<count, 256, 0, stream>>>(p->x, gamma, m->eps, H, p->x8, p->act_scale, p->act_sum);
+        return cudaGetLastError() == cudaSuccess ? 0 : H4B_EINVAL;
+    };
+    auto add_x = [&]() {
+        const long long n = static_cast<long long>(count) * H;
+        add_kernel<<<static_cast<int>((n + 255) / 256), 256, 0, stream>>>(p->x, p->proj, static_cast<int>(n));
+        return cudaGetLastError() == cudaSuccess ? 0 : H4B_EINVAL;
+    };
+
+    prefill_setup_kernel<<<std::min((count + 255) / 256, 148), 256, 0, stream>>>(s->position, count, s->capacity,
+                                                                               p->positions, s->argmax_key);
+    batch_embed_kernel<<<count, 256, 0, stream>>>(p->tokens, m->w_embed, m->s_embed, m->vocab, H, p->x);
+    H4B_CUDA_TRY(cudaGetLastError());
+    for (int l = 0; l < m->layers; ++l) {
+        if ((rc = norm_quant(m->norm_in + static_cast<size_t>(l) * H))) return rc;
+        if ((rc = gemm(m->w_qkv + static_cast<size_t>(l) * qkv_rows * (H / 2), m->s_qkv + static_cast<size_t>(l) * qkv_rows,
+                       p->qkv, qkv_rows, H)))
+            return rc;
+        char* kc = static_cast<char*>(s->k_cache) + l * kv_layer * eb;
+        char* vc = static_cast<char*>(s->v_cache) + l * kv_layer * eb;
+        const dim3 heads_grid(count, m->heads + m->kv_heads);
+        const long long head_stride = static_cast<long long>(s->capacity) * d;
+        if (s->kv_dtype == 0)
+            prefill_rope_append_kernel<float><<<heads_grid, 32, 0, stream>>>(
+                p->qkv, qkv_rows, m->heads, m->kv_heads, m->norm_q + static_cast<size_t>(l) * d,
+                m->norm_k + static_cast<size_t>(l) * d, m->rope_cos, m->rope_sin, m->eps, p->positions,
+                reinterpret_cast<float*>(kc), reinterpret_cast<float*>(vc), head_stride, d);
+        else
+            prefill_rope_append_kernel<__half><<<heads_grid, 32, 0, stream>>>(
+                p->qkv, qkv_rows, m->heads, m->kv_heads, m->norm_q + static_cast<size_t>(l) * d,
+                m->norm_k + static_cast<size_t>(l) * d, m->rope_cos, m->rope_sin, m->eps, p->positions,
+                reinterpret_cast<__half*>(kc), reinterpret_cast<__half*>(vc), head_stride, d);
+        H4B_CUDA_TRY(cudaGetLastError());
+        for (int c0 = 0; c0 < count; c0 += p->attn_queries) {
+            const int n = std::min(p->attn_queries, count - c0);
+            AttnArgs a = {};
+            a.q = p->qkv + static_cast<size_t>(c0) * qkv_rows;
+            a.q_batch_stride = qkv_rows;
+            a.eps = m->eps;
+            a.kcache = kc; a.vcache = vc;
+            a.head_stride = head_stride;
+            a.time_stride = d;
+            a.batch_stride = 0;
+            a.position = p->positions + c0; a.capacity = s->capacity;
+            a.groups = m->heads / m->kv_heads; a.kv_heads = m->kv_heads; a.splits = s->attn_splits;
+            a.partials = p->attn_partials; a.counters = p->attn_counters;
+            a.out = p->attended + static_cast<size_t>(c0) * q_size; a.out_batch_stride = q_size;
+            if ((rc = launch_attention(a, s->kv_dtype, n, stream, false))) return rc;
+        }
+        quantize_rows_kernel<<<count, 256, 0, stream>>>(p->attended, q_size, p->x8, p->act_scale, p->act_sum);
+        H4B_CUDA_TRY(cudaGetLastError());
+        if ((rc = gemm(m->w_o + static_cast<size_t>(l) * H * (q_size / 2), m->s_o + static_cast<size_t>(l) * H, p->proj,
+                       H, q_size)))
+            return rc;
+        if ((rc = add_x())) return rc;
+        if ((rc = norm_quant(m->norm_post + static_cast<size_t>(l) * H))) return rc;
+        if ((rc = gemm(m->w_gate_up + static_cast<size_t>(l) * 2 * I * (H / 2),
+                       m->s_gate_up + static_cast<size_t>(l) * 2 * I, p->gate_up, 2 * I, H)))
+            return rc;
+        const long long n_act = static_cast<long long>(count) * I;
+        batch_swiglu_kernel<<<static_cast<int>((n_act + 255) / 256), 256, 0, stream>>>(p->gate_up, I, count, p->act);
+        H4B_CUDA_TRY(cudaGetLastError());
+        quantize_rows_kernel<<<count, 256, 0, stream>>>(p->act, I, p->x8, p->act_scale, p->act_sum);
+        H4B_CUDA_TRY(cudaGetLastError());
+        if ((rc = gemm(m->w_down + static_cast<size_t>(l) * H * (I / 2), m->s_down + static_cast<size_t>(l) * H, p->proj,
+                       H, I)))
+            return rc;
+        if ((rc = add_x())) return rc;
+    }
+    // the last prompt row: final RMSNorm, LM head, greedy token (the decode stages)
+    H4B_CUDA_TRY(cudaMemcpyAsync(s->x, p->x + static_cast<size_t>(count - 1) * H, sizeof(float) * H,
+                                 cudaMemcpyDeviceToDevice, stream));
+    if ((rc = launch_stage(m, s, STAGE_LM_HEAD, 0, stream, false))) return rc;
+    prefill_finish_kernel<<<1, 32, 0, stream>>>(s->argmax_key, s->next_token, s->token, s->position, count);
+    H4B_CUDA_TRY(cudaGetLastError());
+    return 0;
+}
+
+}  // namespace h4b
+
+extern "C" int h4b_prefill(const h4b_model* model, const h4b_state* state, const h4b_prefill_scratch* scratch,
+                           int count, void* stream) {
+    return h4b::prefill(model, state, scratch, count, static_cast<cudaStream_t>(stream));
+}

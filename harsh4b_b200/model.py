@@ -17,7 +17,8 @@ import time
 import numpy as np
 import torch
 
-from ._lib import BatchStateDesc, ModelDesc, StateDesc, check, device_status, lib, STATUS_WAIT_TIMEOUT
+from ._lib import (BatchStateDesc, ModelDesc, PrefillScratchDesc, StateDesc, check, device_status, lib,
+                   STATUS_WAIT_TIMEOUT)
 from .cache import Checkpoint, read_cache
 
 KV_DTYPES = {"float32": (0, torch.float32), "float16": (1, torch.float16)}
@@ -209,6 +210,37 @@ class CudaBatchState:
         self.position = np.zeros(batch, dtype=np.int64)  # host copy of every sequence's position
 
 
+class PrefillScratch:
+    """Device buffers for h4b_prefill: up to `max_tokens` prompt rows per call,
+    attention over `attn_queries` queries per launch with `splits` splits."""
+
+    def __init__(self, model: "CudaQwen", max_tokens: int, splits: int, attn_queries: int = 512):
+        dev = model.device
+        i32 = dict(dtype=torch.int32, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        H, I, Q, KV = model.hidden, model.intermediate, model.q_size, model.kv_size
+        self.max_tokens, self.splits = int(max_tokens), int(splits)
+        self.attn_queries = max(1, min(int(attn_queries), self.max_tokens))
+        M = self.max_tokens
+        self.x = torch.zeros(M, H, **f32)
+        self.x8 = torch.zeros(M, max(H, Q, I), dtype=torch.int8, device=dev)
+        self.act_scale = torch.zeros(M, **f32)
+        self.act_sum = torch.zeros(M, **i32)
+        self.qkv = torch.zeros(M, Q + 2 * KV, **f32)
+        self.attended = torch.zeros(M, Q, **f32)
+        self.gate_up = torch.zeros(M, 2 * I, **f32)
+        self.act = torch.zeros(M, I, **f32)
+        self.proj = torch.zeros(M, H, **f32)
+        self.tokens = torch.zeros(M, **i32)
+        self.positions = torch.zeros(M, **i32)
+        self.partials = torch.zeros(self.attn_queries * model.kv_heads * self.splits * model.groups *
+                                    (model.head_dim + 4), **f32)
+        self.counters = torch.zeros(self.attn_queries * model.kv_heads, **i32)
+        self.desc = PrefillScratchDesc(M, self.attn_queries, *[t.data_ptr() for t in (
+            self.x, self.x8, self.act_scale, self.act_sum, self.qkv, self.attended, self.gate_up, self.act,
+            self.proj, self.tokens, self.positions, self.partials, self.counters)])
+
+
 class CudaQwen:
     """Qwen3 decode on one B200 from the packed int4 cache layout."""
 
@@ -220,6 +252,7 @@ class CudaQwen:
             raise ValueError(f"mode must be one of {MODES}")
         lib()  # raises without a usable device or library
         self.mode = mode
+        self._prefill_scratch = None
         self.config = dict(config)
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.kv_dtype = kv_dtype
@@ -335,6 +368,37 @@ class CudaQwen:
         state.stream.wait_stream(current)
         state.set_token(token_id)
         state.replay()
+        current.wait_stream(state.stream)
+        return state.logits
+
+    def prefill(self, token_ids, state: CudaDecodeState, max_tokens: int = 2048) -> torch.Tensor:
+        """Feed a prompt in one pass per `max_tokens` rows (h4b_prefill): the
+        body projections run as tensor-core GEMMs over the prompt rows.
+        Returns the last token's logits; the state then stands where
+        forward_token over the same ids (with the state's attention splits)
+        leaves it, bit for bit."""
+        ids = np.asarray([int(t) for t in token_ids], dtype=np.int32)
+        if ids.size == 0:
+            raise ValueError("empty prompt")
+        if state.model is not self:
+            raise ValueError("decode state belongs to another model")
+        if state.position + ids.size > state.capacity:
+            raise ValueError("decode state capacity exhausted")
+        if ids.min() < 0 or ids.max() >= self.vocab:
+            raise ValueError("token ID outside the vocabulary")
+        rows = min(int(max_tokens), int(ids.size))
+        scratch = self._prefill_scratch
+        if scratch is None or scratch.max_tokens < rows or scratch.splits != state.splits:
+            scratch = self._prefill_scratch = PrefillScratch(self, rows, state.splits)
+        current = torch.cuda.current_stream(self.device)
+        state.stream.wait_stream(current)
+        with torch.cuda.stream(state.stream):
+            for start in range(0, ids.size, scratch.max_tokens):
+                part = ids[start:start + scratch.max_tokens]
+                scratch.tokens[:part.size].copy_(torch.from_numpy(part), non_blocking=False)
+                check(lib().h4b_prefill(ctypes.byref(self.desc), ctypes.byref(state.desc), ctypes.byref(scratch.desc),
+                                        int(part.size), state.stream.cuda_stream), "h4b_prefill")
+                state.position += int(part.size)
         current.wait_stream(state.stream)
         return state.logits
 

@@ -277,6 +277,40 @@ int h4b_validate_batch(const h4b_model *model, const h4b_batch_state *state);
  * Capturable in a CUDA graph. */
 int h4b_decode_batch(const h4b_model *model, const h4b_batch_state *state, void *stream);
 
+/* ---- prefill ----------------------------------------------------------------
+ * Scratch for h4b_prefill, owned by the caller: buffers for up to max_tokens
+ * prompt rows (16-byte aligned). attn_partials holds attn_queries * kv_heads
+ * * attn_splits * groups * (head_dim + 4) floats and attn_counters
+ * attn_queries * kv_heads ints (zero at creation; the kernels leave them
+ * zero), where attn_splits is the session's. */
+typedef struct h4b_prefill_scratch {
+    int max_tokens, attn_queries;
+    float *x;           /* [max_tokens][hidden] */
+    int8_t *x8;         /* [max_tokens][max(hidden, heads*head_dim, intermediate)] */
+    float *act_scale;   /* [max_tokens] */
+    int32_t *act_sum;   /* [max_tokens] */
+    float *qkv;         /* [max_tokens][(heads + 2 kv_heads) * head_dim] */
+    float *attended;    /* [max_tokens][heads * head_dim] */
+    float *gate_up;     /* [max_tokens][2 intermediate] */
+    float *act;         /* [max_tokens][intermediate] */
+    float *proj;        /* [max_tokens][hidden] */
+    int32_t *tokens;    /* [max_tokens] prompt token ids, filled by the caller */
+    int32_t *positions; /* [max_tokens] */
+    float *attn_partials;
+    int *attn_counters;
+} h4b_prefill_scratch;
+
+/* Feeds scratch->tokens[0, count) to the session at positions *position ..
+ * *position + count - 1 (LiteSparkQwen.forward_token called count times,
+ * cpu_lightspark.py:424-468, as the reference's prefill loop does,
+ * cpu_lightspark.py:809-810), with the body projections as tensor-core GEMMs
+ * over all prompt rows. Afterwards state->logits holds the last row's
+ * logits, next_token/token its greedy token and *position has advanced by
+ * count -- bit for bit what count h4b_decode_step calls with the session's
+ * attention splits leave. */
+int h4b_prefill(const h4b_model *model, const h4b_state *state, const h4b_prefill_scratch *scratch, int count,
+                void *stream);
+
 #ifdef __cplusplus
 }
 #endif
