@@ -50,13 +50,22 @@ def parse_args():
     parser.add_argument("--kv-dtype", choices=("float16", "float32"), default="float16")
     parser.add_argument("--seed", type=int, default=0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--workload", choices=("decode", "gemv"), default="decode",
-                        help="decode: config 0 (the headline); gemv: config 1 body-GEMV microbenchmark")
+    parser.add_argument("--workload", choices=("decode", "gemv", "batch", "prefill", "gemm", "attention", "tp"),
+                        default="decode",
+                        help="decode: config 0 (the headline); gemv: config 1 body GEMV; attention: config 2; "
+                             "batch: config 3 batched decode; prefill / tp: config 4; gemm: the a13 GEMM")
     parser.add_argument("--shapes", default="q,k,v,o,gate,up,down",
                         help="gemv workload: comma-separated projection names")
     parser.add_argument("--iters", type=int, default=200, help="gemv workload: timed launches per shape")
     parser.add_argument("--mode", choices=("persistent", "chain"), default="persistent",
                         help="decode step: one persistent kernel per token, or the PDL kernel chain")
+    parser.add_argument("--gemm-shapes", default="qkv,o,gate_up,down,lm_head", help="gemm workload: shapes")
+    parser.add_argument("--gemm-m", default="64,2048", help="gemm workload: token counts")
+    parser.add_argument("--attn-cases", default="1x512,1x4096,1x32768,32x512,32x4096,32x32768",
+                        help="attention workload: batch x context cases")
+    parser.add_argument("--batch", type=int, default=64, help="batch workload: sequences")
+    parser.add_argument("--prompt-len", type=int, default=2048, help="batch / prefill workloads: prompt tokens")
+    parser.add_argument("--context", type=int, default=4096, help="tp workload: context before decoding")
     parser.add_argument("--layers", type=int, default=None,
                         help="override the layer count (a smaller model for profiling captures; not the headline)")
     return parser.parse_args()
@@ -442,10 +451,380 @@ def run_gemv(args) -> int:
     return 0
 
 
+def _event_pair(torch):
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def run_batch(args) -> int:
+    """Config 3: batched greedy decode of B sequences (default 64) after a
+    prompt of --prompt-len random ids each, body projections on the tcgen05
+    GEMM. `value` = B x K tokens over K device-fed steps (generate_batch);
+    `e2e` = the same K steps through forward_batch with the B token ids
+    copied in and the B greedy ids read back every step. The prompts are fed
+    through forward_batch before timing (not timed)."""
+    import numpy as np
+    import torch
+
+    from harsh4b_b200.model import CudaQwen
+    from harsh4b_b200.synthetic import qwen3_4b_config, synthetic_checkpoint
+
+    peaks = measured_peaks()
+    B, P = args.batch, args.prompt_len
+    config = qwen3_4b_config(**({"num_hidden_layers": args.layers} if args.layers else {}))
+    model = CudaQwen.from_checkpoint(synthetic_checkpoint(config, seed=args.seed), kv_dtype=args.kv_dtype,
+                                     mode="chain")
+    rng = np.random.default_rng([args.seed, B, P])
+    prompts = rng.integers(0, model.vocab, size=(B, P))
+    capacity = P + 2 * (args.warmup + args.steps) + 2
+    state = model.new_batch_state(B, capacity)
+    t0 = time.perf_counter()
+    for i in range(P):
+        model.forward_batch(prompts[:, i], state)
+    torch.cuda.synchronize()
+    prompt_s = time.perf_counter() - t0
+    model.generate_batch(state, args.warmup)
+    start, end = _event_pair(torch)
+    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        start.record()
+        model.generate_batch(state, args.steps)
+        end.record()
+        torch.cuda.synchronize()
+    elapsed = start.elapsed_time(end) / 1000.0
+    ctx0 = P + args.warmup
+    # e2e: host ids in, host greedy ids out, every step
+    host_next = torch.empty(B, dtype=torch.int32).pin_memory()
+    tokens = state.next_tokens.cpu().numpy()
+    for _ in range(args.warmup):
+        model.forward_batch(tokens, state)
+        host_next.copy_(state.next_tokens)
+        tokens = host_next.numpy().copy()
+    e_start, e_end = _event_pair(torch)
+    torch.cuda.synchronize()
+    e_start.record()
+    for _ in range(args.steps):
+        model.forward_batch(tokens, state)
+        host_next.copy_(state.next_tokens)
+        tokens = host_next.numpy().copy()
+    e_end.record()
+    torch.cuda.synchronize()
+    e2e_elapsed = e_start.elapsed_time(e_end) / 1000.0
+    kv_bytes = 2 if args.kv_dtype == "float16" else 4
+    per_pos = model.n_layers * 2 * model.kv_size * kv_bytes
+    mean_ctx = ctx0 + (args.steps + 1) / 2
+    bytes_per_step = model.weight_bytes + B * per_pos * mean_ctx
+    achieved = bytes_per_step * args.steps / elapsed / 1e9
+    line = {
+        "metric": "batched decode tok/s Qwen3-4B int4 (config 3)", "value": round(B * args.steps / elapsed, 1),
+        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(elapsed / args.steps * 1000, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int4xint8", "data": "synthetic",
+        "config": {"workload": f"config3: batch {B}, {P}-token random prompts, greedy decode, tcgen05 GEMM body",
+                   "batch": B, "prompt": P, "kv_dtype": args.kv_dtype, "layers": model.n_layers,
+                   "context": [ctx0, ctx0 + args.steps], "l2": "inputs larger than L2",
+                   "prompt_feed_s": round(prompt_s, 2)},
+        "e2e": {"value": round(B * args.steps / e2e_elapsed, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+                "d2h_bytes_per_step": 4 * B},
+        "roofline": {"bound": "hbm", "kernel": "whole batched step (weights + every sequence's K/V)",
+                     "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "bytes_per_step": int(bytes_per_step),
+                     "peak_source": peaks["source"]},
+        "clocks": clocks.summary(), "device_status": model.status(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_prefill(args) -> int:
+    """Config 4's prefill: one --prompt-len-token prompt (default 2048) fed in
+    one CudaQwen.prefill call (tcgen05 GEMMs over all prompt rows). A step is
+    one whole prefill into a fresh session; `value` is prompt tok/s. The
+    roofline is the tensor pipe: 2 x body MACs per prompt row (int8 ops)."""
+    import numpy as np
+    import torch
+
+    from harsh4b_b200.model import CudaQwen
+    from harsh4b_b200.synthetic import qwen3_4b_config, synthetic_checkpoint
+
+    P = args.prompt_len
+    config = qwen3_4b_config(**({"num_hidden_layers": args.layers} if args.layers else {}))
+    model = CudaQwen.from_checkpoint(synthetic_checkpoint(config, seed=args.seed), kv_dtype=args.kv_dtype,
+                                     mode="chain")
+    ids = np.random.default_rng([args.seed, P]).integers(0, model.vocab, size=P)
+    state = model.new_state(P + 1)
+    for _ in range(args.warmup):
+        state.reset()
+        model.prefill(ids, state, max_tokens=P)
+    times = []
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        for _ in range(args.steps):
+            state.reset()
+            start, end = _event_pair(torch)
+            with torch.cuda.stream(state.stream):
+                start.record(state.stream)
+            model.prefill(ids, state, max_tokens=P)
+            with torch.cuda.stream(state.stream):
+                end.record(state.stream)
+            torch.cuda.synchronize()
+            times.append(start.elapsed_time(end) / 1000.0)
+    elapsed = sum(times)
+    H, I, Q, KV = model.hidden, model.intermediate, model.q_size, model.kv_size
+    body_macs = model.n_layers * (H * (Q + 2 * KV) + Q * H + H * 2 * I + I * H)
+    ops_per_prefill = 2 * body_macs * P + 2 * model.vocab * H
+    achieved = ops_per_prefill * args.steps / elapsed / 1e12
+    int8_peak = 2 * measured_bf16_tflops()
+    line = {
+        "metric": "prefill tok/s Qwen3-4B int4 (config 4 prefill)", "value": round(P * args.steps / elapsed, 1),
+        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(elapsed / args.steps * 1000, 3), "p50_ms": round(statistics.median(times) * 1000, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4xint8", "data": "synthetic",
+        "config": {"workload": f"config4 prefill: {P}-token random prompt, one h4b_prefill call",
+                   "prompt": P, "kv_dtype": args.kv_dtype, "layers": model.n_layers,
+                   "l2": "inputs larger than L2"},
+        "roofline": {"bound": "tensor", "kernel": "whole prefill (int8 ops of every GEMM)",
+                     "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOP/s",
+                     "frac": round(achieved / int8_peak, 4), "ops_per_step": int(ops_per_prefill),
+                     "peak_source": "2 x measured bf16 dense (int8 dense rate is twice bf16 on B200)"},
+        "clocks": clocks.summary(), "device_status": model.status(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def measured_bf16_tflops() -> float:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return float(json.loads(path.read_text())["bf16_tflops"])
+    return 1590.0
+
+
+def _graph_time(torch, fn, reps: int, warmup: int = 3) -> float:
+    """Seconds per call of `fn`, captured `reps` times in one CUDA graph."""
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(reps):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    start, end = _event_pair(torch)
+    start.record()
+    graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    del graph
+    return start.elapsed_time(end) / 1000.0 / reps
+
+
+GEMM_SHAPES = {"qkv": (6144, 2560), "o": (2560, 4096), "gate_up": (19456, 2560), "down": (2560, 9728),
+               "lm_head": (151936, 2560)}
+
+
+def run_gemm(args) -> int:
+    """a13: the batched int4 x int8 GEMM per body shape at M = 64 (batched
+    decode, HBM-bound) and M = 2048 (prefill, tensor-bound), tcgen05 kernel
+    and the mma.sync kernel, each launch captured in a CUDA graph. Weight
+    copies rotate so M = 64 reads come from HBM; outputs are checked equal
+    between the kernels."""
+    import torch
+
+    from harsh4b_b200 import ops
+
+    peaks = measured_peaks()
+    int8_peak = 2 * measured_bf16_tflops()
+    results = []
+    g = torch.Generator(device="cuda").manual_seed(args.seed)
+    for M in (int(m) for m in args.gemm_m.split(",")):
+        for name in args.gemm_shapes.split(","):
+            N, K = GEMM_SHAPES[name]
+            if name == "lm_head" and M > 64:
+                continue
+            copies = max(1, -(-300_000_000 // (N * K // 2)))
+            ws = [torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device="cuda", generator=g)
+                  for _ in range(copies)]
+            scales = torch.rand(N, device="cuda", generator=g)
+            x8 = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda", generator=g)
+            act = torch.rand(M, device="cuda", generator=g) * 1e-2
+            sums = x8.to(torch.int32).sum(1, dtype=torch.int32)
+            outs = {k: torch.empty(M, N, device="cuda") for k in ("tcgen05", "mma_sync")}
+            row = {"M": M, "shape": name, "N": N, "K": K}
+            for kern in ("tcgen05", "mma_sync"):
+                state = {"i": 0}
+
+                def launch(kern=kern, state=state):
+                    ops.int4_gemm(x8, act, sums, ws[state["i"] % copies], scales, out=outs[kern], kernel=kern)
+                    state["i"] += 1
+
+                sec = _graph_time(torch, launch, reps=max(copies, 8))
+                ops_ = 2 * M * N * K
+                row[kern] = {"us": round(sec * 1e6, 2), "tops": round(ops_ / sec / 1e12, 1),
+                             "gbs": round((N * K // 2 + 4 * N + M * K + 4 * M * N) / sec / 1e9, 1)}
+            row["equal"] = bool(torch.equal(outs["tcgen05"], outs["mma_sync"]))
+            tc = row["tcgen05"]
+            row["frac"] = (round(tc["gbs"] / peaks["hbm_gbs"], 4) if M <= 64 else round(tc["tops"] / int8_peak, 4))
+            results.append(row)
+            del ws
+    line = {"metric": "batched int4 x int8 GEMM (a13): tcgen05 vs mma.sync", "unit": "us",
+            "peaks": {"hbm_gbs": peaks["hbm_gbs"], "int8_tops": round(int8_peak, 1),
+                      "int8_source": "2 x measured bf16 dense"},
+            "config": {"workload": "a13 shapes at M = 64 (HBM-bound frac) and M = 2048 (tensor-bound frac)",
+                       "l2": "rotating weight copies > 300 MB at M = 64"},
+            "shapes": results}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_attention(args) -> int:
+    """Config 2: the decode attention kernel (qk-RMSNorm, RoPE, KV append,
+    split-K GQA over an fp16 cache) for 32 q / 8 kv heads at contexts 512,
+    4096, 32768 and batch 1 and 32; the cache is filled with N(0,1) values.
+    Batch 1 is the decode stage (h4b_decode_stage 2) of a session at the
+    given position, batch 32 the batched kernel (h4b_batch_attention)."""
+    import ctypes
+
+    import torch
+
+    from harsh4b_b200._lib import check, lib
+    from harsh4b_b200.model import CudaQwen
+    from harsh4b_b200.synthetic import qwen3_4b_config, synthetic_checkpoint
+
+    peaks = measured_peaks()
+    model = CudaQwen.from_checkpoint(synthetic_checkpoint(qwen3_4b_config(num_hidden_layers=1), seed=args.seed),
+                                     kv_dtype="float16", mode="chain")
+    results = []
+    for case in args.attn_cases.split(","):
+        batch, ctx = (int(v) for v in case.split("x"))
+        splits = max(1, min(64, 148 * 2 // (model.kv_heads * batch)))
+        splits = min(splits, max(1, ctx // 64))
+        if batch == 1:
+            st = model.new_state(ctx, attn_splits=splits)
+            st.k_cache.normal_(); st.v_cache.normal_(); st.qkv.normal_()
+            st.position_dev.fill_(ctx - 1)
+
+            def launch(st=st):
+                check(lib().h4b_decode_stage(ctypes.byref(model.desc), ctypes.byref(st.desc), 2, 0,
+                                             torch.cuda.current_stream().cuda_stream), "h4b_decode_stage")
+        else:
+            st = model.new_batch_state(batch, ctx, attn_splits=splits)
+            st.k_cache.normal_(); st.v_cache.normal_(); st.qkv.normal_()
+            st.positions.fill_(ctx - 1)
+
+            def launch(st=st):
+                check(lib().h4b_batch_attention(ctypes.byref(model.desc), ctypes.byref(st.desc), 0,
+                                                torch.cuda.current_stream().cuda_stream), "h4b_batch_attention")
+        sec = _graph_time(torch, launch, reps=20)
+        kv_bytes = batch * 2 * ctx * model.kv_size * 2
+        results.append({"batch": batch, "ctx": ctx, "splits": splits, "us": round(sec * 1e6, 2),
+                        "gbs": round(kv_bytes / sec / 1e9, 1), "frac": round(kv_bytes / sec / 1e9 / peaks["hbm_gbs"], 4),
+                        "kv_bytes": kv_bytes})
+        del st
+        torch.cuda.empty_cache()
+    line = {"metric": "GQA decode attention GB/s of K/V read (config 2)", "unit": "GB/s",
+            "peak": peaks["hbm_gbs"], "peak_source": peaks["source"],
+            "config": {"workload": "config2: 32 q / 8 kv heads, d 128, fp16 KV N(0,1), RoPE + qk-norm in kernel",
+                       "l2": "K/V of 1-32 sequences; 512-context batch-1 rows fit in L2 (graph replays reuse them)"},
+            "cases": results, "device_status": model.status()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_tp(args, rank, world, local_rank, dist) -> int:
+    """Config 4 decode: tensor-parallel batch-1 decode on `world` GPUs from a
+    context of --context tokens (the K/V cache is filled with N(0,1) values;
+    the prefill is not part of this line). A step is one token through
+    TensorParallelQwen.forward_token (all ranks, NCCL all-reduces of the o /
+    down int32 sums and their scales, all-gather of the greedy candidates).
+    Reports the p50 wall latency per token, the device time per token (max
+    over ranks) and the communication alone: the same collectives replayed
+    without the kernels (exposed, since this path does not overlap them)."""
+    import numpy as np
+    import torch
+
+    from harsh4b_b200.synthetic import qwen3_4b_config, synthetic_checkpoint
+    from harsh4b_b200.tp import TensorParallelQwen
+
+    device = torch.device("cuda", local_rank)
+    config = qwen3_4b_config(**({"num_hidden_layers": args.layers} if args.layers else {}))
+    model = TensorParallelQwen(synthetic_checkpoint(config, seed=args.seed), kv_dtype=args.kv_dtype, device=device)
+    C = args.context
+    state = model.new_state(C + args.warmup + args.steps + 1)
+    g = torch.Generator(device=device).manual_seed(args.seed + rank)
+    state.k_cache.normal_(generator=g)
+    state.v_cache.normal_(generator=g)
+    state.position_dev.fill_(C)
+    state.position = C
+    token = int(np.random.default_rng(args.seed).integers(0, model.vocab))
+    for _ in range(args.warmup):
+        token, _ = model.forward_token(token, state)
+    walls, device_ms = [], []
+    dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        for _ in range(args.steps):
+            start, end = _event_pair(torch)
+            t0 = time.perf_counter()
+            start.record()
+            token, _ = model.forward_token(token, state)
+            end.record()
+            torch.cuda.synchronize()
+            walls.append(time.perf_counter() - t0)
+            device_ms.append(start.elapsed_time(end))
+    # the collectives of one token alone
+    H, L = model.model.hidden, model.model.n_layers
+    amax = torch.zeros(1, device=device)
+    acc = torch.zeros(H, dtype=torch.int32, device=device)
+    pair = torch.zeros(2, dtype=torch.float64, device=device)
+    pairs = [torch.zeros(2, dtype=torch.float64, device=device) for _ in range(world)]
+
+    def comm_token():
+        for _ in range(2 * L):
+            dist.all_reduce(amax, op=dist.ReduceOp.MAX)
+            dist.all_reduce(acc, op=dist.ReduceOp.SUM)
+        dist.all_gather(pairs, pair)
+
+    for _ in range(3):
+        comm_token()
+    torch.cuda.synchronize()
+    c_start, c_end = _event_pair(torch)
+    c_start.record()
+    for _ in range(args.steps):
+        comm_token()
+    c_end.record()
+    torch.cuda.synchronize()
+    comm_ms = c_start.elapsed_time(c_end) / args.steps
+    stats = torch.tensor([statistics.median(walls) * 1000, statistics.median(device_ms), comm_ms],
+                         dtype=torch.float64, device=device)
+    dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    status = model.model.status()
+    if rank != 0:
+        return 0
+    p50, dev, comm = (float(v) for v in stats.cpu())
+    line = {
+        "metric": "tensor-parallel batch-1 decode latency Qwen3-4B int4 (config 4)", "value": round(1000.0 / p50, 2),
+        "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(p50, 4),
+        "p50_ms": round(p50, 4), "device_ms_p50": round(dev, 4), "comm_ms_per_token": round(comm, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int4xint8",
+        "data": "synthetic",
+        "config": {"workload": f"config4 TP: batch 1 from context {C} (K/V filled with N(0,1) values)",
+                   "context": C, "kv_dtype": args.kv_dtype, "layers": L, "parallelism": f"tp{world}",
+                   "collectives_per_token": 4 * L + 1},
+        "clocks": clocks.summary(), "device_status": status,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main() -> int:
     args = parse_args()
-    if args.workload == "gemv":
-        return run_gemv(args)
+    single = {"gemv": run_gemv, "batch": run_batch, "prefill": run_prefill, "gemm": run_gemm,
+              "attention": run_attention}
+    if args.workload in single:
+        return single[args.workload](args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -462,7 +841,21 @@ def main() -> int:
         torch_dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                       device_id=torch.device("cuda", local_rank))
         dist = torch_dist
+    if args.workload == "tp" and dist is None:  # one rank: a process group of one
+        import datetime
+
+        import torch
+        import torch.distributed as torch_dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29531")
+        torch.cuda.set_device(local_rank)
+        torch_dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=300),
+                                      device_id=torch.device("cuda", local_rank))
+        dist = torch_dist
     try:
+        if args.workload == "tp":
+            return run_tp(args, rank, world, local_rank, dist)
         return run_ours(args, rank, world, local_rank, dist)
     finally:
         if dist is not None:

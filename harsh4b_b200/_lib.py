@@ -89,6 +89,7 @@ _SIGNATURES = {
     "h4b_int4_gemv_absmax": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp],
     "h4b_residual_acc": [_vp, _vp, _vp, _vp, _i32, _vp],
     "h4b_decode_batch": [ctypes.POINTER(ModelDesc), ctypes.POINTER(BatchStateDesc), _vp],
+    "h4b_batch_attention": [ctypes.POINTER(ModelDesc), ctypes.POINTER(BatchStateDesc), _i32, _vp],
     "h4b_prefill": [ctypes.POINTER(ModelDesc), ctypes.POINTER(StateDesc), ctypes.POINTER(PrefillScratchDesc), _i32,
                     _vp],
 }

@@ -155,12 +155,35 @@ int validate_batch(const h4b_model* m, const h4b_batch_state* s) {
     return 0;
 }
 
+// Layer l's attention for every sequence of the batch: qk-RMSNorm, RoPE,
+// append at each sequence's position, split-K GQA over its own cache.
+int batch_attention(const h4b_model* m, const h4b_batch_state* s, int l, cudaStream_t stream) {
+    const int d = m->head_dim, q_size = m->heads * d, kv_size = m->kv_heads * d, qkv_rows = q_size + 2 * kv_size;
+    const size_t kv_layer = static_cast<size_t>(m->kv_heads) * s->capacity * d;  // elements
+    AttnArgs a = {};
+    a.q = s->qkv; a.knew = s->qkv + q_size; a.vnew = s->qkv + q_size + kv_size;
+    a.q_batch_stride = qkv_rows;
+    a.q_norm = m->norm_q + static_cast<size_t>(l) * d;
+    a.k_norm = m->norm_k + static_cast<size_t>(l) * d;
+    a.rope_cos = m->rope_cos; a.rope_sin = m->rope_sin; a.eps = m->eps;
+    const size_t eb = s->kv_dtype == 0 ? 4 : 2;
+    a.kcache = static_cast<char*>(s->k_cache) + l * kv_layer * eb;
+    a.vcache = static_cast<char*>(s->v_cache) + l * kv_layer * eb;
+    a.head_stride = static_cast<long long>(s->capacity) * d;
+    a.time_stride = d;
+    a.batch_stride = static_cast<long long>(m->layers) * kv_layer;
+    a.position = s->positions; a.capacity = s->capacity;
+    a.groups = m->heads / m->kv_heads; a.kv_heads = m->kv_heads; a.splits = s->attn_splits;
+    a.partials = s->attn_partials; a.counters = s->attn_counters;
+    a.out = s->attended; a.out_batch_stride = q_size; a.absmax_out = nullptr;
+    return launch_attention(a, s->kv_dtype, s->batch, stream, false);
+}
+
 int decode_batch(const h4b_model* m, const h4b_batch_state* s, cudaStream_t stream) {
     int rc = validate_batch(m, s);
     if (rc) return rc;
     const int B = s->batch, H = m->hidden, I = m->intermediate, d = m->head_dim;
     const int q_size = m->heads * d, kv_size = m->kv_heads * d, qkv_rows = q_size + 2 * kv_size;
-    const size_t kv_layer = static_cast<size_t>(m->kv_heads) * s->capacity * d;  // elements
     auto gemm = [&](const uint8_t* w, const float* ws, float* out, int rows, int width) {
         GemmArgs g{s->x8, s->act_scale, s->act_sum, w, ws, out, B, rows, width};
         return launch_int4_gemm(g, stream);
@@ -181,23 +204,7 @@ int decode_batch(const h4b_model* m, const h4b_batch_state* s, cudaStream_t stre
         if ((rc = gemm(m->w_qkv + static_cast<size_t>(l) * qkv_rows * (H / 2), m->s_qkv + static_cast<size_t>(l) * qkv_rows,
                        s->qkv, qkv_rows, H)))
             return rc;
-        AttnArgs a = {};
-        a.q = s->qkv; a.knew = s->qkv + q_size; a.vnew = s->qkv + q_size + kv_size;
-        a.q_batch_stride = qkv_rows;
-        a.q_norm = m->norm_q + static_cast<size_t>(l) * d;
-        a.k_norm = m->norm_k + static_cast<size_t>(l) * d;
-        a.rope_cos = m->rope_cos; a.rope_sin = m->rope_sin; a.eps = m->eps;
-        const size_t eb = s->kv_dtype == 0 ? 4 : 2;
-        a.kcache = static_cast<char*>(s->k_cache) + l * kv_layer * eb;
-        a.vcache = static_cast<char*>(s->v_cache) + l * kv_layer * eb;
-        a.head_stride = static_cast<long long>(s->capacity) * d;
-        a.time_stride = d;
-        a.batch_stride = static_cast<long long>(m->layers) * kv_layer;
-        a.position = s->positions; a.capacity = s->capacity;
-        a.groups = m->heads / m->kv_heads; a.kv_heads = m->kv_heads; a.splits = s->attn_splits;
-        a.partials = s->attn_partials; a.counters = s->attn_counters;
-        a.out = s->attended; a.out_batch_stride = q_size; a.absmax_out = nullptr;
-        if ((rc = launch_attention(a, s->kv_dtype, B, stream, false))) return rc;
+        if ((rc = batch_attention(m, s, l, stream))) return rc;
         quantize_rows_kernel<<<B, 256, 0, stream>>>(s->attended, q_size, s->x8, s->act_scale, s->act_sum);
         H4B_CUDA_TRY(cudaGetLastError());
         if ((rc = gemm(m->w_o + static_cast<size_t>(l) * H * (q_size / 2), m->s_o + static_cast<size_t>(l) * H, s->proj,
@@ -232,6 +239,13 @@ int decode_batch(const h4b_model* m, const h4b_batch_state* s, cudaStream_t stre
 
 extern "C" int h4b_validate_batch(const h4b_model* model, const h4b_batch_state* state) {
     return h4b::validate_batch(model, state);
+}
+
+extern "C" int h4b_batch_attention(const h4b_model* model, const h4b_batch_state* state, int layer, void* stream) {
+    int rc = h4b::validate_batch(model, state);
+    if (rc) return rc;
+    if (layer < 0 || layer >= model->layers) return H4B_EINVAL;
+    return h4b::batch_attention(model, state, layer, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int h4b_decode_batch(const h4b_model* model, const h4b_batch_state* state, void* stream) {

@@ -277,6 +277,11 @@ int h4b_validate_batch(const h4b_model *model, const h4b_batch_state *state);
  * Capturable in a CUDA graph. */
 int h4b_decode_batch(const h4b_model *model, const h4b_batch_state *state, void *stream);
 
+/* Layer `layer`'s attention step of h4b_decode_batch alone (reads state->qkv,
+ * appends each sequence's k/v at its position, writes state->attended), for
+ * per-kernel timing. */
+int h4b_batch_attention(const h4b_model *model, const h4b_batch_state *state, int layer, void *stream);
+
 /* ---- prefill ----------------------------------------------------------------
  * Scratch for h4b_prefill, owned by the caller: buffers for up to max_tokens
  * prompt rows (16-byte aligned). attn_partials holds attn_queries * kv_heads
