@@ -4,16 +4,20 @@
 // the same contract and result bits as gemm.cu (integer sums are exact).
 //
 // Tile: 128 weight rows (the MMA's M) x TOK tokens (its N: 64, 128 or 256),
-// K advancing 128 per pipeline stage. A CTA has six warps:
-//   warp 4  lane 0: TMA producer -- per stage, the packed weight tile
+// K advancing 128 per pipeline stage. A CTA has eighteen warps:
+//   warp 16 lane 0: TMA producer -- per stage, the packed weight tile
 //           (128 rows x 64 bytes, no swizzle) and the activation tile (TOK
 //           rows x 128 bytes, 128-byte swizzle) land on the stage's `full`
-//           mbarrier; warp 4 also allocates and frees the tensor memory;
-//   warps 0-3: unpack the packed tile into signed int8 codes in the
+//           mbarrier; warp 16 also allocates and frees the tensor memory;
+//   warps 0-15: unpack the packed tile into signed int8 codes in the
 //           K-major 128-byte-swizzled layout the MMA reads, then arrive on
-//           `aready`; after the last stage they are the epilogue, one TMEM
-//           lane quarter (32 rows) per warp;
-//   warp 5  lane 0: issues tcgen05.mma kind::i8 (A s8 weights, B s8
+//           `aready`. They work as four groups of four warps, group g taking
+//           stages g, g + 4, ...: four stages unpack at once and every
+//           scheduler holds four unpack warps, so the unpack (which paces
+//           the pipeline) is not one stage's dependent latency at a time.
+//           After the last stage they are the epilogue, warp w reading TMEM
+//           lane quarter w % 4 (32 rows) for column slice w / 4;
+//   warp 17 lane 0: issues tcgen05.mma kind::i8 (A s8 weights, B s8
 //           activations, D s32 in TMEM), 4 per stage (K = 32 each), and
 //           tcgen05.commit to the stage's `empty` mbarrier, which frees the
 //           stage for the producer; a final commit signals the epilogue.
@@ -29,23 +33,31 @@ namespace h4b {
 
 constexpr int kTcRows = 128;     // weight rows per CTA (MMA M)
 constexpr int kTcK = 128;        // k per stage: one 128-byte swizzle atom of int8
-constexpr int kTcThreads = 192;  // warps 0-3 unpack + epilogue, warp 4 TMA + TMEM, warp 5 MMA
+constexpr int kTcUnpackGroups = 4, kTcGroupWarps = 4;
+constexpr int kTcUnpackWarps = kTcUnpackGroups * kTcGroupWarps;
+constexpr int kTcThreads = 32 * (kTcUnpackWarps + 2);  // + producer warp + MMA warp
+constexpr int kTcProducerWarp = kTcUnpackWarps, kTcMmaWarp = kTcUnpackWarps + 1;
 
 template <int TOK>
 struct TcCfg {
-    static constexpr int kABytes = kTcRows * kTcK;           // unpacked weights, int8
+    static constexpr int kABytes = kTcRows * kTcK;           // one unpacked weight tile, int8
     static constexpr int kBBytes = TOK * kTcK;               // activations, int8
     static constexpr int kPackedBytes = kTcRows * kTcK / 2;  // packed weights
-    static constexpr int kBOff = kABytes;
-    static constexpr int kPackedOff = kABytes + kBBytes;
-    static constexpr int kStageBytes = kABytes + kBBytes + kPackedBytes;
-    static constexpr int kStages = TOK == 256 ? 3 : (TOK == 128 ? 5 : 6);
+    static constexpr int kBOff = 0, kPackedOff = kBBytes;    // inside a TMA stage
+    static constexpr int kStageBytes = kBBytes + kPackedBytes;
+    // A multiple of the unpack groups: group g then owns stages g, g + 4, ...
+    // and visits each in round order (see the kernel comment).
+    static constexpr int kStages = TOK == 64 ? 8 : 4;
+    static constexpr int kAOff = 0;                                  // kTcUnpackGroups unpacked tiles
+    static constexpr int kStageOff = kTcUnpackGroups * kABytes;      // then the TMA stages
+    static constexpr int kBarrierOff = kStageOff + kStages * kStageBytes;
     static constexpr int kBarrierBytes = 256;
-    static constexpr int kSmem = kStages * kStageBytes + kBarrierBytes + 1024;  // + alignment slack
+    static constexpr int kSmem = kBarrierOff + kBarrierBytes + 1024;  // + alignment slack
     static constexpr uint32_t kTmemCols = TOK;
-    static_assert(kStageBytes % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
+    static_assert(kStageBytes % 1024 == 0 && kABytes % 1024 == 0, "tiles keep the 1024-byte swizzle alignment");
+    static_assert(kStages % kTcUnpackGroups == 0, "each group must own whole stages");
     static_assert(kSmem <= 232448, "shared memory per CTA");
-    static_assert(3 * kStages * 8 + 16 <= kBarrierBytes, "barrier area");
+    static_assert(2 * kStages * 8 + 2 * kTcUnpackGroups * 8 + 16 <= kBarrierBytes, "barrier area");
 };
 
 struct TcArgs {
@@ -107,12 +119,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 }
 
 // Two packed bytes of w (picked by the byte_perm selector: 0x1100 the low
-// pair, 0x3322 the high pair) -> signed int8 codes lo0 hi0 lo1 hi1: a nibble
-// n read as u = n ^ 8 is n + 8 in 0..15, and a bytewise u - 8 is n in two's
-// complement.
+// pair, 0x3322 the high pair) -> signed int8 codes lo0 hi0 lo1 hi1. With one
+// 4-bit two's-complement code t per byte, t + (t & 8) * 0x1E sets the high
+// nibble of exactly the negative codes (8 * 0x1E = 0xF0, no carry between
+// bytes): the sign extension in one AND and one multiply-add.
 __device__ __forceinline__ uint32_t nib_s8(uint32_t w, uint32_t selector) {
-    const uint32_t t = __byte_perm(w, 0, selector);
-    return __vsub4(((t & 0x000F000Fu) | ((t >> 4) & 0x0F000F00u)) ^ 0x08080808u, 0x08080808u);
+    const uint32_t b = __byte_perm(w, 0, selector);
+    const uint32_t t = (b & 0x000F000Fu) | ((b >> 4) & 0x0F000F00u);
+    return t + (t & 0x08080808u) * 0x1Eu;
 }
 
 template <int TOK>
@@ -121,11 +135,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         const TcArgs g) {
     using C = TcCfg<TOK>;
     extern __shared__ uint8_t tc_smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
-    uint64_t* aready = full + C::kStages;
-    uint64_t* empty = aready + C::kStages;
-    uint64_t* accfull = empty + C::kStages;
+    // 1024-byte aligned base, by offsetting the shared array itself (an
+    // integer round trip would hide the address space and turn every tile
+    // access into a generic load or store)
+    uint8_t* smem = tc_smem_raw + ((1024u - (smem_addr(tc_smem_raw) & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarrierOff);  // TMA stage landed
+    uint64_t* empty = full + C::kStages;                                   // TMA stage consumed by the MMAs
+    uint64_t* aready = empty + C::kStages;                                 // unpacked tile g written
+    uint64_t* afree = aready + kTcUnpackGroups;                            // unpacked tile g read by the MMAs
+    uint64_t* accfull = afree + kTcUnpackGroups;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accfull + 1);
     volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -136,14 +154,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&aready[s], 4);
             mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < kTcUnpackGroups; ++a) {
+            mbar_init(&aready[a], kTcGroupWarps);
+            mbar_init(&afree[a], 1);
         }
         mbar_init(accfull, 1);
         *failed = wait_failed_before() ? 1 : 0;
         fence_mbar_init();
     }
-    if (warp == 4) {
+    if (warp == kTcProducerWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      ::"r"(smem_addr(tmem_slot)), "r"(C::kTmemCols) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -152,9 +173,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    auto stage = [&](int s) { return smem + s * C::kStageBytes; };
+    auto stage = [&](int s) { return smem + C::kStageOff + s * C::kStageBytes; };
+    auto atile = [&](int a) { return smem + C::kAOff + a * C::kABytes; };
 
-    if (warp == 4) {
+    // Every waiter below meets each barrier's phases in order (a parity wait
+    // cannot tell a phase from the one two rounds later): the producer and
+    // the MMA thread walk all iterations in order; unpack group g handles
+    // iterations g, g + 4, ..., whose TMA stages (it % kStages, a multiple
+    // of 4 apart) and unpacked tile (g) are its own.
+    if (warp == kTcProducerWarp) {
         if (lane == 0) {  // TMA producer
             int issued = 0;
             if (!*failed) {
@@ -178,39 +205,43 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int it = issued > C::kStages ? issued - C::kStages : 0; it < issued; ++it)
                 mbar_wait(&full[it % C::kStages], (it / C::kStages) & 1);
         }
-    } else if (warp == 5) {
+    } else if (warp == kTcMmaWarp) {
         if (lane == 0) {  // MMA issuer
             constexpr uint32_t idesc = tc_idesc<TOK>();
             for (int it = 0; it < steps && !*failed; ++it) {
-                const int s = it % C::kStages;
-                const uint32_t parity = (it / C::kStages) & 1;
-                if (!mbar_wait(&full[s], parity) || !mbar_wait(&aready[s], parity)) {
+                const int s = it % C::kStages, a = it % kTcUnpackGroups;
+                if (!mbar_wait(&full[s], (it / C::kStages) & 1) ||
+                    !mbar_wait(&aready[a], (it / kTcUnpackGroups) & 1)) {
                     *failed = 1;
                     break;
                 }
                 tc_fence_after();
-                const uint64_t adesc = sw128_desc(stage(s)), bdesc = sw128_desc(stage(s) + C::kBOff);
+                const uint64_t adesc = sw128_desc(atile(a)), bdesc = sw128_desc(stage(s) + C::kBOff);
 #pragma unroll
                 for (int kk = 0; kk < kTcK / 32; ++kk)  // +32 bytes along K = +2 in the start-address field
                     tc_mma_i8(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (it | kk) != 0);
                 tc_commit(&empty[s]);
+                tc_commit(&afree[a]);
             }
             tc_commit(accfull);  // arrives once every MMA issued above has completed
         }
-    } else {  // warps 0-3: unpack, then epilogue
-        const int t = threadIdx.x;
-        for (int it = 0; it < steps; ++it) {
+    } else {  // unpack groups, then the epilogue
+        const int group = warp / kTcGroupWarps;
+        const int t = threadIdx.x - group * 32 * kTcGroupWarps;  // thread within the group
+        for (int it = group; it < steps; it += kTcUnpackGroups) {
             const int s = it % C::kStages;
-            const bool ok = __all_sync(0xffffffffu, !*failed && mbar_wait(&full[s], (it / C::kStages) & 1));
+            const int use = it / kTcUnpackGroups;  // this group's tile use count
+            const bool ok = __all_sync(0xffffffffu, !*failed && (use == 0 || mbar_wait(&afree[group], (use - 1) & 1)) &&
+                                                        mbar_wait(&full[s], (it / C::kStages) & 1));
             if (!ok) {
                 if (lane == 0) *failed = 1;
                 break;
             }
             const uint8_t* packed = stage(s) + C::kPackedOff;
-            uint8_t* a = stage(s);
+            uint8_t* a = atile(group);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int c = i * 128 + t;  // 16-byte packed chunk: row c / 4, k bytes 32 * (c % 4) ..
+            for (int i = 0; i < kTcRows * kTcK / 2 / 16 / (32 * kTcGroupWarps); ++i) {
+                const int c = i * 32 * kTcGroupWarps + t;  // 16-byte packed chunk: row c / 4, k bytes 32 * (c % 4) ..
                 const int row = c >> 2, piece = c & 3, sw = row & 7;
                 const uint4 w = *reinterpret_cast<const uint4*>(packed + c * 16);
                 const uint4 lo = make_uint4(nib_s8(w.x, 0x1100), nib_s8(w.x, 0x3322), nib_s8(w.y, 0x1100),
@@ -223,17 +254,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core's reads
             __syncwarp();
-            if (lane == 0) mbar_arrive(&aready[s]);
+            if (lane == 0) mbar_arrive(&aready[group]);
         }
-        // epilogue: warp w reads TMEM lanes 32w..32w+31 = weight rows n0 + 32w + lane
+        // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = weight rows n0 + 32 (w % 4) + lane,
+        // columns (tokens) of slice w / 4
         const bool done = __all_sync(0xffffffffu, mbar_wait(accfull, 0) && !*failed);
         tc_fence_after();
         if (done) {
-            const int row = n0 + warp * 32 + lane;
+            constexpr int kSlices = kTcUnpackWarps / 4, kCols = TOK / kSlices;
+            static_assert(kCols % 16 == 0, "column slices of whole 16-column loads");
+            const int quarter = warp & 3, slice = warp >> 2;
+            const int row = n0 + quarter * 32 + lane;
             const float ws = g.w_scale[row];
-            const uint32_t base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+            const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll 1
-            for (int c0 = 0; c0 < TOK; c0 += 16) {
+            for (int c0 = slice * kCols; c0 < (slice + 1) * kCols; c0 += 16) {
                 uint32_t v[16];
                 tmem_ld16(base + c0, v);
 #pragma unroll
@@ -249,7 +284,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 4) {
+    if (warp == kTcProducerWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols)
                      : "memory");
