@@ -62,7 +62,7 @@ def parse_args():
     parser.add_argument("--gemm-shapes", default="qkv,o,gate_up,down,lm_head", help="gemm workload: shapes")
     parser.add_argument("--gemm-m", default="64,2048", help="gemm workload: token counts")
     parser.add_argument("--attn-cases", default="1x512,1x4096,1x32768,32x512,32x4096,32x32768",
-                        help="attention workload: batch x context cases")
+                        help="attention workload: batch x context [x splits] cases")
     parser.add_argument("--batch", type=int, default=64, help="batch workload: sequences")
     parser.add_argument("--prompt-len", type=int, default=2048, help="batch / prefill workloads: prompt tokens")
     parser.add_argument("--context", type=int, default=4096, help="tp workload: context before decoding")
@@ -392,7 +392,10 @@ def run_gemv(args) -> int:
     """Config 1: the fused quantise + int4 GEMV alone, per projection shape.
     Weight copies rotate so the bytes read per launch come from HBM (the
     copies together exceed the 126 MB L2); launches are queued behind a
-    sleep kernel and timed with CUDA events on their stream."""
+    sleep kernel and timed with CUDA events on their stream. `us`/`gbs`: each
+    launch waits for the previous one to finish; `pdl_chain`: the same launches
+    with programmatic dependent launch (as the decode chain runs them), so a
+    launch streams its weights while the previous one finishes."""
     import numpy as np
     import torch
 
@@ -422,22 +425,29 @@ def run_gemv(args) -> int:
         got_acc = acc.cpu().numpy()
         exact = bool(np.array_equal(got_acc, want_acc))
         mismatch = np.nonzero(got_acc != want_acc)[0]
-        for i in range(min(3, args.iters)):
-            ops.int4_gemv_fused_quant(xt, ws[i % copies], ss[i % copies], out=out)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        torch.cuda._sleep(20_000_000)
-        start.record(stream)
-        for i in range(args.iters):
-            ops.int4_gemv_fused_quant(xt, ws[i % copies], ss[i % copies], out=out)
-        end.record(stream)
-        torch.cuda.synchronize()
-        us = start.elapsed_time(end) * 1000.0 / args.iters
-        gbs = bytes_per_launch / us / 1e3
+        scale_slot = torch.empty(1, dtype=torch.float32, device="cuda")
+
+        def timed(pdl: bool) -> float:
+            for i in range(min(3, args.iters)):
+                ops.int4_gemv_fused_quant(xt, ws[i % copies], ss[i % copies], out=out, scale=scale_slot, pdl=pdl)
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            torch.cuda._sleep(20_000_000)
+            start.record(stream)
+            for i in range(args.iters):
+                ops.int4_gemv_fused_quant(xt, ws[i % copies], ss[i % copies], out=out, scale=scale_slot, pdl=pdl)
+            end.record(stream)
+            torch.cuda.synchronize()
+            return start.elapsed_time(end) * 1000.0 / args.iters
+
+        us, us_pdl = timed(False), timed(True)
+        gbs, gbs_pdl = bytes_per_launch / us / 1e3, bytes_per_launch / us_pdl / 1e3
         from harsh4b_b200._lib import device_status
         results[name] = {"rows": rows, "width": width, "us": round(us, 3), "gbs": round(gbs, 1),
-                         "frac": round(gbs / peaks["hbm_gbs"], 4), "int32_bit_exact": exact,
-                         "device_status": device_status()}
+                         "frac": round(gbs / peaks["hbm_gbs"], 4),
+                         "pdl_chain": {"us": round(us_pdl, 3), "gbs": round(gbs_pdl, 1),
+                                       "frac": round(gbs_pdl / peaks["hbm_gbs"], 4)},
+                         "int32_bit_exact": exact, "device_status": device_status()}
         if not exact:
             results[name]["mismatched_rows"] = int(mismatch.size)
             results[name]["first_mismatches"] = mismatch[:6].tolist()
@@ -698,9 +708,12 @@ def run_attention(args) -> int:
                                      kv_dtype="float16", mode="chain")
     results = []
     for case in args.attn_cases.split(","):
-        batch, ctx = (int(v) for v in case.split("x"))
-        splits = max(1, min(64, 148 * 2 // (model.kv_heads * batch)))
-        splits = min(splits, max(1, ctx // 64))
+        fields = [int(v) for v in case.split("x")]
+        batch, ctx = fields[0], fields[1]
+        if len(fields) > 2:  # batch x context x splits
+            splits = fields[2]
+        else:  # enough CTAs for five per SM, at least 64 tokens per split
+            splits = max(1, min(64, -(-5 * 148 // (model.kv_heads * batch)), ctx // 64))
         if batch == 1:
             st = model.new_state(ctx, attn_splits=splits)
             st.k_cache.normal_(); st.v_cache.normal_(); st.qkv.normal_()

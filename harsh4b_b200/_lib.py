@@ -63,6 +63,7 @@ _SIGNATURES = {
     "h4b_device_info": [_vp, _vp, _vp],
     "h4b_int4_i8_gemv": [_vp, _vp, _vp, _f32, _vp, _vp, _i32, _i32, _vp],
     "h4b_int4_gemv_fused_quant": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp],
+    "h4b_int4_gemv_fused_quant_ex": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp],
     "h4b_quantize_activation": [_vp, _vp, _vp, _i32, _vp],
     "h4b_rmsnorm": [_vp, _vp, _vp, _i32, _f32, _vp],
     "h4b_add_inplace": [_vp, _vp, _i32, _vp],

@@ -624,6 +624,18 @@ extern "C" int h4b_int4_gemv_fused_quant(const float* values, const uint8_t* wei
     return h4b::launch_gemv(h4b::PRO_QUANT, h4b::EPI_STORE, a, static_cast<cudaStream_t>(stream), false);
 }
 
+extern "C" int h4b_int4_gemv_fused_quant_ex(const float* values, const uint8_t* weights, const float* scales,
+                                            float* output, int32_t* acc, float* act_scale_out, int rows, int width,
+                                            int flags, void* stream) {
+    if (!values || !weights || !scales || !output || (flags & ~H4B_LAUNCH_PDL)) return H4B_EINVAL;
+    if (reinterpret_cast<uintptr_t>(values) & 15) return H4B_EINVAL;
+    h4b::GemvArgs a = {};
+    a.w = weights; a.wscale = scales; a.rows = rows; a.width = width;
+    a.xin = values; a.out = output; a.acc_out = acc; a.act_scale_out = act_scale_out;
+    return h4b::launch_gemv(h4b::PRO_QUANT, h4b::EPI_STORE, a, static_cast<cudaStream_t>(stream),
+                            (flags & H4B_LAUNCH_PDL) != 0);
+}
+
 // Quantisation with a given absmax (a device scalar, e.g. the max over the
 // ranks of a tensor-parallel group) fused with the GEMV; writes the int32
 // row sums (and the fp32 rows when `output` is not null).

@@ -35,17 +35,20 @@ def int4_i8_gemv(x8: torch.Tensor, weights: torch.Tensor, scales: torch.Tensor, 
 
 
 def int4_gemv_fused_quant(values: torch.Tensor, weights: torch.Tensor, scales: torch.Tensor,
-                          *, out: torch.Tensor | None = None, acc: torch.Tensor | None = None):
-    """quantize_activation + int4 GEMV in one kernel: returns (out, acc, act_scale tensor[1])."""
+                          *, out: torch.Tensor | None = None, acc: torch.Tensor | None = None,
+                          scale: torch.Tensor | None = None, pdl: bool = False):
+    """quantize_activation + int4 GEMV in one kernel: returns (out, acc, act_scale tensor[1]).
+    pdl=True launches with programmatic dependent launch (H4B_LAUNCH_PDL)."""
     rows, packed = weights.shape
     out = torch.empty(rows, dtype=torch.float32, device=weights.device) if out is None else out
-    scale = torch.empty(1, dtype=torch.float32, device=weights.device)
-    check(lib().h4b_int4_gemv_fused_quant(_dev(values, torch.float32, "values"),
-                                          _dev(weights, torch.uint8, "weights"),
-                                          _dev(scales, torch.float32, "scales"), _dev(out, torch.float32, "out"),
-                                          _dev(acc, torch.int32, "acc") if acc is not None else None,
-                                          scale.data_ptr(), rows, 2 * packed, stream_handle()),
-          "h4b_int4_gemv_fused_quant")
+    scale = torch.empty(1, dtype=torch.float32, device=weights.device) if scale is None else scale
+    check(lib().h4b_int4_gemv_fused_quant_ex(_dev(values, torch.float32, "values"),
+                                             _dev(weights, torch.uint8, "weights"),
+                                             _dev(scales, torch.float32, "scales"), _dev(out, torch.float32, "out"),
+                                             _dev(acc, torch.int32, "acc") if acc is not None else None,
+                                             _dev(scale, torch.float32, "scale"), rows, 2 * packed,
+                                             1 if pdl else 0, stream_handle()),
+          "h4b_int4_gemv_fused_quant_ex")
     return out, acc, scale
 
 

@@ -60,6 +60,17 @@ int h4b_int4_gemv_fused_quant(const float *values, const uint8_t *weights, const
                               float *output, int32_t *acc, float *act_scale_out,
                               int rows, int width, void *stream);
 
+/* Launch flag: programmatic dependent launch. The kernel may start while
+ * the previous kernel on the stream is still running; it streams its weights
+ * into shared memory at once and waits for the previous kernel's writes
+ * (griddepcontrol.wait) before it reads activations or writes anything. */
+#define H4B_LAUNCH_PDL 1
+
+/* h4b_int4_gemv_fused_quant with launch flags (H4B_LAUNCH_PDL). */
+int h4b_int4_gemv_fused_quant_ex(const float *values, const uint8_t *weights, const float *scales,
+                                 float *output, int32_t *acc, float *act_scale_out,
+                                 int rows, int width, int flags, void *stream);
+
 /* Replaces kernel.quantize_activation (third-party, called at
  * cpu_lightspark.py:433): q = clamp(rint(v * 127/m), -127, 127) with
  * m = max(absmax(v), 1e-5); *scale_out = m / 127. */
