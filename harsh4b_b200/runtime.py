@@ -8,8 +8,9 @@ The reference picks its backend in ``create_runtime`` (inference_runtime.py:
 INTEGRATION.md). Methods keep the reference's names and meaning:
 
 * ``prefill(ids, max_tokens) -> (logits, session)``: a fresh decode state
-  sized for the prompt plus the output, the prompt fed one token at a time
-  (the reference's CPU runtime does the same, :124-128);
+  sized for the prompt plus the output, the prompt fed in one pass through
+  the batched GEMMs (the reference's CPU runtime loops over the tokens,
+  :124-128; the resulting state and logits are the same);
 * ``decode(token, session) -> logits``;
 * ``sample(logits, generated, temperature) -> int``: sample_numpy's policy
   (:144-163; top-p 0.9, top-k 50, repetition penalty 1.15) on the device,
@@ -113,10 +114,12 @@ class CudaRuntime(Runtime):
         self._scratch = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=model.device)
 
     def prefill(self, ids, max_tokens):
+        """A fresh session with the prompt fed in one CudaQwen.prefill pass (the
+        reference's CPU runtime feeds it token by token, :124-128; the state
+        ends the same, with the prompt's attention split count fixed per
+        session)."""
         state = self.model.new_state(len(ids) + max_tokens)
-        logits = None
-        for token in ids:
-            logits = self.model.forward_token(int(token), state)
+        logits = self.model.prefill([int(t) for t in ids], state)
         return logits, state
 
     def decode(self, token, session):

@@ -70,12 +70,16 @@ def test_cuda_runtime_matches_oracle_greedy_and_sampled():
     from harsh4b_b200.runtime import CudaRuntime
     from harsh4b_b200.synthetic import synthetic_checkpoint, synthetic_prompt, tiny_config
     from oracle.model import sample_runtime
-    from _models import oracle_for
+    from _models import oracle_model
 
     checkpoint = synthetic_checkpoint(tiny_config(), seed=3)
     prompt = synthetic_prompt(checkpoint.config, 10, seed=3)
     model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float32")
-    reference = oracle_for(checkpoint, model)
+    # the prompt goes through one prefill pass (the session's fixed split
+    # count), later tokens through the persistent step (its per-context rule)
+    decode_rule, n = model.attention_split_rule(), len(prompt)
+    reference = oracle_model(checkpoint, kv_dtype=np.float32,
+                             attn_splits=lambda ctx: model.attn_splits if ctx <= n else decode_rule(ctx))
     for temperature in (0.0, 0.7):
         rt = CudaRuntime(model=model, tokenizer=_Tokenizer(model.vocab), seed=11)
         draws = np.random.default_rng(11)
