@@ -752,9 +752,11 @@ def run_tp(args, rank, world, local_rank, dist) -> int:
     the prefill is not part of this line). A step is one token through
     TensorParallelQwen.forward_token (all ranks, NCCL all-reduces of the o /
     down int32 sums and their scales, all-gather of the greedy candidates).
-    Reports the p50 wall latency per token, the device time per token (max
-    over ranks) and the communication alone: the same collectives replayed
-    without the kernels (exposed, since this path does not overlap them)."""
+    Reports the p50 wall latency per token with the token captured in one
+    CUDA graph (and, under "eager", dispatched call by call), the device time
+    per token (max over ranks) and the communication alone: the same
+    collectives issued without the kernels (exposed, since this path does not
+    overlap them)."""
     import numpy as np
     import torch
 
@@ -765,28 +767,40 @@ def run_tp(args, rank, world, local_rank, dist) -> int:
     config = qwen3_4b_config(**({"num_hidden_layers": args.layers} if args.layers else {}))
     model = TensorParallelQwen(synthetic_checkpoint(config, seed=args.seed), kv_dtype=args.kv_dtype, device=device)
     C = args.context
-    state = model.new_state(C + args.warmup + args.steps + 1)
+    state = model.new_state(C + 3 * (args.warmup + args.steps) + 1)  # three timed rounds
     g = torch.Generator(device=device).manual_seed(args.seed + rank)
     state.k_cache.normal_(generator=g)
     state.v_cache.normal_(generator=g)
     state.position_dev.fill_(C)
     state.position = C
     token = int(np.random.default_rng(args.seed).integers(0, model.vocab))
-    for _ in range(args.warmup):
-        token, _ = model.forward_token(token, state)
-    walls, device_ms = [], []
-    dist.barrier(device_ids=[local_rank])
-    torch.cuda.synchronize()
-    with ClockSampler(local_rank) as clocks:
+
+    def run(graph: bool):
+        nonlocal token
+        for _ in range(args.warmup):
+            token, _ = model.forward_token(token, state, graph=graph)
+        walls, device_ms = [], []
+        dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
         for _ in range(args.steps):
             start, end = _event_pair(torch)
             t0 = time.perf_counter()
             start.record()
-            token, _ = model.forward_token(token, state)
+            token, _ = model.forward_token(token, state, graph=graph)
             end.record()
             torch.cuda.synchronize()
             walls.append(time.perf_counter() - t0)
             device_ms.append(start.elapsed_time(end))
+        return statistics.median(walls) * 1000, statistics.median(device_ms)
+
+    eager_wall, eager_dev = run(graph=False)
+    model.comm = "nccl"  # the same token with NCCL collectives, for comparison
+    nccl_wall, nccl_dev = run(graph=True)
+    model.release_graphs()
+    model.comm = "p2p"
+    with ClockSampler(local_rank) as clocks:
+        graph_wall, graph_dev = run(graph=True)
+    model.release_graphs()
     # the collectives of one token alone
     H, L = model.model.hidden, model.model.n_layers
     amax = torch.zeros(1, device=device)
@@ -810,17 +824,22 @@ def run_tp(args, rank, world, local_rank, dist) -> int:
     c_end.record()
     torch.cuda.synchronize()
     comm_ms = c_start.elapsed_time(c_end) / args.steps
-    stats = torch.tensor([statistics.median(walls) * 1000, statistics.median(device_ms), comm_ms],
+    stats = torch.tensor([graph_wall, graph_dev, comm_ms, eager_wall, eager_dev, nccl_wall, nccl_dev],
                          dtype=torch.float64, device=device)
     dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     status = model.model.status()
+    model.close()
     if rank != 0:
         return 0
-    p50, dev, comm = (float(v) for v in stats.cpu())
+    p50, dev, comm, eager_p50, eager_dev_p50, nccl_p50, nccl_dev_p50 = (float(v) for v in stats.cpu())
     line = {
         "metric": "tensor-parallel batch-1 decode latency Qwen3-4B int4 (config 4)", "value": round(1000.0 / p50, 2),
         "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(p50, 4),
-        "p50_ms": round(p50, 4), "device_ms_p50": round(dev, 4), "comm_ms_per_token": round(comm, 4),
+        "p50_ms": round(p50, 4), "device_ms_p50": round(dev, 4),
+        "exchange": "one-shot P2P kernels over NVLink peer memory, token captured in a CUDA graph",
+        "eager": {"p50_ms": round(eager_p50, 4), "device_ms_p50": round(eager_dev_p50, 4)},
+        "nccl_graph": {"p50_ms": round(nccl_p50, 4), "device_ms_p50": round(nccl_dev_p50, 4),
+                       "collectives_alone_ms": round(comm, 4)},
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int4xint8",
         "data": "synthetic",
         "config": {"workload": f"config4 TP: batch 1 from context {C} (K/V filled with N(0,1) values)",

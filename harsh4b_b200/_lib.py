@@ -57,6 +57,12 @@ class PrefillScratchDesc(ctypes.Structure):
                            "positions", "attn_partials", "attn_counters")]
 
 
+class TpGroupDesc(ctypes.Structure):
+    """Mirror of ``h4b_tp_group``."""
+
+    _fields_ = [("world", _i32), ("rank", _i32), ("capacity", _i32), ("buffers", _vp * 8), ("generation", _vp)]
+
+
 _SIGNATURES = {
     "h4b_prepare": [],
     "h4b_get_status": [_vp],
@@ -91,10 +97,19 @@ _SIGNATURES = {
     "h4b_residual_acc": [_vp, _vp, _vp, _vp, _i32, _vp],
     "h4b_decode_batch": [ctypes.POINTER(ModelDesc), ctypes.POINTER(BatchStateDesc), _vp],
     "h4b_batch_attention": [ctypes.POINTER(ModelDesc), ctypes.POINTER(BatchStateDesc), _i32, _vp],
+    "h4b_tp_buffer_bytes": [_i32, _i32],
+    "h4b_ipc_alloc": [ctypes.c_longlong, ctypes.POINTER(_vp), _vp],
+    "h4b_ipc_open": [_vp, ctypes.POINTER(_vp)],
+    "h4b_ipc_close": [_vp],
+    "h4b_ipc_free": [_vp],
+    "h4b_tp_allreduce_max": [ctypes.POINTER(TpGroupDesc), _vp, _vp],
+    "h4b_tp_allreduce_sum_residual": [ctypes.POINTER(TpGroupDesc), _vp, _vp, _vp, _vp, _i32, _vp],
+    "h4b_tp_gather_best": [ctypes.POINTER(TpGroupDesc), _vp, _vp, _i32, _vp, _vp],
     "h4b_prefill": [ctypes.POINTER(ModelDesc), ctypes.POINTER(StateDesc), ctypes.POINTER(PrefillScratchDesc), _i32,
                     _vp],
 }
-_RESTYPES = {"h4b_persistent_exchange_words": ctypes.c_longlong, "h4b_sample_scratch_bytes": ctypes.c_longlong}
+_RESTYPES = {"h4b_persistent_exchange_words": ctypes.c_longlong, "h4b_sample_scratch_bytes": ctypes.c_longlong,
+             "h4b_tp_buffer_bytes": ctypes.c_longlong}
 
 
 def exported_symbols() -> list[str]:

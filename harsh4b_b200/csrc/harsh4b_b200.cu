@@ -9,3 +9,4 @@
 #include "gemm_tc.cu"
 #include "batch.cu"
 #include "prefill.cu"
+#include "tp.cu"

@@ -16,6 +16,11 @@ Partitioning (g ranks; g divides the q heads, the kv heads, the MLP width /
   token is the best (value, global index) over the ranks (all-gather);
 * embedding, RMSNorm, residual stream: replicated.
 
+The exchanges run either as single-kernel one-shot transfers over NVLink
+peer memory (comm="p2p", csrc/tp.cu: the absmax MAX, the int32 SUM fused
+with the residual epilogue, the greedy candidates) or as NCCL collectives
+(comm="nccl"); both give the same bits.
+
 Each rank's slice is itself a valid smaller model (hq heads, hk kv heads,
 I/g MLP width, a V/g-row LM head), built by :func:`shard_checkpoint`, so the
 single-GPU kernels run it unchanged; only the o/down epilogues move behind
@@ -91,7 +96,7 @@ class TensorParallelQwen:
     nccl backend, one process per GPU."""
 
     def __init__(self, checkpoint: Checkpoint, group=None, *, kv_dtype: str = "float16", device=None,
-                 attn_splits: int = 16):
+                 attn_splits: int = 16, comm: str = "p2p"):
         import torch
         import torch.distributed as dist
 
@@ -109,7 +114,60 @@ class TensorParallelQwen:
         self.vocab_offset = self.rank * self.model.vocab
         self.acc = torch.zeros(self.model.hidden, dtype=torch.int32, device=self.device)
         self._best = torch.zeros(2, dtype=torch.float64, device=self.device)
-        self._gather = [torch.zeros(2, dtype=torch.float64, device=self.device) for _ in range(self.world)]
+        self._gathered = torch.zeros(2 * self.world, dtype=torch.float64, device=self.device)
+        self._token_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self._graphs = {}
+        if comm not in ("p2p", "nccl"):
+            raise ValueError("comm must be 'p2p' or 'nccl'")
+        self.comm, self._own, self._peers, self.group_desc = comm, None, [], None
+        if comm == "p2p":
+            self._open_peer_buffers()
+
+    def _open_peer_buffers(self) -> None:
+        """Allocates this rank's receive buffer, exchanges IPC handles over the
+        process group and maps every peer's buffer (h4b_tp_group)."""
+        import ctypes
+
+        from ._lib import TpGroupDesc, check, lib
+
+        torch, dist = self.torch, self.dist
+        capacity = max(self.model.hidden, 2)
+        nbytes = int(lib().h4b_tp_buffer_bytes(self.world, capacity))
+        check(nbytes if nbytes < 0 else 0, "h4b_tp_buffer_bytes")
+        own, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+        with torch.cuda.device(self.device):
+            check(lib().h4b_ipc_alloc(nbytes, ctypes.byref(own), handle), "h4b_ipc_alloc")
+            self._own = own.value
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=self.group)
+            buffers = (ctypes.c_void_p * 8)()
+            for r in range(self.world):
+                if r == self.rank:
+                    buffers[r] = self._own
+                    continue
+                peer = ctypes.c_void_p()
+                check(lib().h4b_ipc_open(ctypes.create_string_buffer(handles[r], 64), ctypes.byref(peer)),
+                      "h4b_ipc_open")
+                self._peers.append(peer.value)
+                buffers[r] = peer.value
+        self._generation = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.group_desc = TpGroupDesc(self.world, self.rank, capacity, buffers, self._generation.data_ptr())
+
+    def close(self) -> None:
+        """Releases the graphs and the peer mappings (before the process group
+        is destroyed; every rank calls it)."""
+        from ._lib import lib
+
+        self.release_graphs()
+        self.torch.cuda.synchronize(self.device)
+        with self.torch.cuda.device(self.device):
+            for peer in self._peers:
+                lib().h4b_ipc_close(peer)
+            self._peers = []
+            if self._own is not None:
+                self.dist.barrier(group=self.group)  # no peer writes into it any more
+                lib().h4b_ipc_free(self._own)
+                self._own = None
 
     def new_state(self, capacity: int):
         return self.model.new_state(capacity)
@@ -122,41 +180,99 @@ class TensorParallelQwen:
         check(lib().h4b_decode_stage(ctypes.byref(self.model.desc), ctypes.byref(state.desc), stage, layer,
                                      self.torch.cuda.current_stream(self.device).cuda_stream), "h4b_decode_stage")
 
-    def forward_token(self, token_id: int, state):
-        """One token on every rank; returns (greedy token, local logits slice)."""
-        from . import ops
-
-        torch, dist, m = self.torch, self.dist, self.model
+    def forward_token(self, token_id: int, state, graph: bool = False):
+        """One token on every rank; returns (greedy token, local logits slice).
+        graph=True replays the whole token (kernels and collectives) as one
+        CUDA graph per state, captured on first use; the host then only
+        copies the token id in and the ranks' candidates out."""
         if state.position >= state.capacity:
             raise ValueError("decode state capacity exhausted")
         if not 0 <= int(token_id) < self.vocab:
             raise ValueError(f"token ID {token_id} is outside the vocabulary")
+        self._token_host[0] = int(token_id)
+        state.token_dev.copy_(self._token_host, non_blocking=True)
+        if graph:
+            cuda_graph = self._graphs.get(id(state))
+            if cuda_graph is None:
+                cuda_graph = self._capture(state)
+            cuda_graph.replay()
+        else:
+            self._token_body(state)
+        state.position += 1
+        pairs = self._gathered.cpu().numpy().reshape(self.world, 2)  # waits for the token
+        token = global_argmax(pairs[:, 0], pairs[:, 1].astype(np.int64))
+        return token, state.logits
+
+    def _capture(self, state):
+        """Captures _token_body for `state` (the token id is read from
+        state.token_dev, the position from the device, so replays advance)."""
+        torch, dist = self.torch, self.dist
+        if self.comm == "nccl":  # the communicators must exist before a capture
+            probe = torch.zeros(2, dtype=torch.float64, device=self.device)
+            dist.all_reduce(probe[:1], op=dist.ReduceOp.MAX, group=self.group)
+            dist.all_reduce(self.acc.new_zeros(1), op=dist.ReduceOp.SUM, group=self.group)
+            dist.all_gather_into_tensor(self._gathered.clone(), probe, group=self.group)
+        torch.cuda.synchronize(self.device)
+        side = torch.cuda.Stream(device=self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            self._token_body(state)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        self._graphs[id(state)] = graph
+        return graph
+
+    def release_graphs(self) -> None:
+        """Drops the captured graphs (they hold NCCL work: release them before
+        the process group is destroyed)."""
+        self._graphs.clear()
+
+    def _token_body(self, state) -> None:
+        """Every kernel and exchange of one token, on the current stream."""
+        from . import ops
+
+        torch, dist, m = self.torch, self.dist, self.model
         state.absmax.zero_()
         state.argmax_key.zero_()
-        state.token_dev.fill_(int(token_id))
         ops.embedding(state.token_dev, self.table, self.table_scales, out=state.x)
-        H, I = m.hidden, m.intermediate
         for l in range(m.n_layers):
             self._stage(state, 1, l)  # qkv rows of the local heads (RMSNorm + quantise fused)
             self._stage(state, 2, l)  # local attention; absmax[2l] = local max of attended
-            amax = state.absmax[2 * l:2 * l + 1]
-            dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
-            ops.int4_gemv_absmax(state.attended, amax, m.w_o[l], m.s_o[l], self.acc)
-            dist.all_reduce(self.acc, op=dist.ReduceOp.SUM, group=self.group)
-            ops.residual_acc(state.x, self.acc, amax, m.s_o[l])
+            self._k_split(state, state.attended, state.absmax[2 * l:2 * l + 1], m.w_o[l], m.s_o[l])
             self._stage(state, 4, l)  # local gate/up + SwiGLU; absmax[2l+1] = local max of act
-            amax = state.absmax[2 * l + 1:2 * l + 2]
-            dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
-            ops.int4_gemv_absmax(state.act, amax, m.w_down[l], m.s_down[l], self.acc)
-            dist.all_reduce(self.acc, op=dist.ReduceOp.SUM, group=self.group)
-            ops.residual_acc(state.x, self.acc, amax, m.s_down[l])
+            self._k_split(state, state.act, state.absmax[2 * l + 1:2 * l + 2], m.w_down[l], m.s_down[l])
         self._stage(state, 6)  # local LM head rows + local argmax key
         self._stage(state, 7)  # next_token (local index) and position += 1
-        state.position += 1
-        local = int(state.next_token_dev.item())
-        self._best[0] = state.logits[local].to(torch.float64)
-        self._best[1] = float(local + self.vocab_offset)
-        dist.all_gather(self._gather, self._best, group=self.group)
-        pairs = torch.stack(self._gather).cpu().numpy()
-        token = global_argmax(pairs[:, 0], pairs[:, 1].astype(np.int64))
-        return token, state.logits
+        if self.comm == "p2p":
+            self._p2p("h4b_tp_gather_best", state.logits.data_ptr(), state.next_token_dev.data_ptr(),
+                      self.vocab_offset, self._gathered.data_ptr())
+            return
+        local = state.next_token_dev.to(torch.int64)
+        self._best[0:1].copy_(state.logits.index_select(0, local))
+        self._best[1:2].copy_(local + self.vocab_offset)
+        dist.all_gather_into_tensor(self._gathered, self._best, group=self.group)
+
+    def _p2p(self, name: str, *args) -> None:
+        import ctypes
+
+        from ._lib import check, lib
+
+        stream = self.torch.cuda.current_stream(self.device).cuda_stream
+        check(getattr(lib(), name)(ctypes.byref(self.group_desc), *args, stream), name)
+
+    def _k_split(self, state, values, amax, weights, scales) -> None:
+        """A K-split projection (o or down): the global quantisation scale, this
+        rank's int32 row sums, their exact sum over the ranks, the residual."""
+        from . import ops
+
+        dist, H = self.dist, self.model.hidden
+        if self.comm == "p2p":
+            self._p2p("h4b_tp_allreduce_max", amax.data_ptr())
+            ops.int4_gemv_absmax(values, amax, weights, scales, self.acc)
+            self._p2p("h4b_tp_allreduce_sum_residual", self.acc.data_ptr(), state.x.data_ptr(), amax.data_ptr(),
+                      scales.data_ptr(), H)
+            return
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
+        ops.int4_gemv_absmax(values, amax, weights, scales, self.acc)
+        dist.all_reduce(self.acc, op=dist.ReduceOp.SUM, group=self.group)
+        ops.residual_acc(state.x, self.acc, amax, scales)

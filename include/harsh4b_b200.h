@@ -293,6 +293,40 @@ int h4b_decode_batch(const h4b_model *model, const h4b_batch_state *state, void 
  * per-kernel timing. */
 int h4b_batch_attention(const h4b_model *model, const h4b_batch_state *state, int layer, void *stream);
 
+/* ---- tensor-parallel exchanges over NVLink peer memory ------------------------
+ * One receive buffer per rank, mapped by every rank (CUDA IPC); values travel
+ * as {tag, payload} words stored into the peers' buffers and polled in one's
+ * own (bounded polls: a timeout sets status bit 1). generation is a device
+ * counter, zero at creation, advanced by every exchange; all ranks must run
+ * the same exchanges in the same order. */
+#define H4B_TP_MAX_RANKS 8
+typedef struct h4b_tp_group {
+    int world, rank, capacity;                        /* capacity: words per source slot */
+    unsigned long long *buffers[H4B_TP_MAX_RANKS];    /* rank r's receive buffer, as mapped here */
+    unsigned int *generation;
+} h4b_tp_group;
+
+/* Bytes of one receive buffer (two parities x world slots x capacity words). */
+long long h4b_tp_buffer_bytes(int world, int capacity);
+/* Zeroed device allocation shareable with other processes; handle receives
+ * the 64-byte cudaIpcMemHandle_t. */
+int h4b_ipc_alloc(long long bytes, void **ptr, void *handle);
+int h4b_ipc_open(const void *handle, void **ptr);
+int h4b_ipc_close(void *ptr);
+int h4b_ipc_free(void *ptr);
+/* value[0] <- max over ranks (the o / down quantisation absmax;
+ * replaces an all-reduce MAX). */
+int h4b_tp_allreduce_max(const h4b_tp_group *group, float *value, void *stream);
+/* x[i] += float(sum over ranks acc[i]) * dequant(absmax) * w_scales[i], i < n:
+ * the exact int32 all-reduce of a K-split projection fused with its residual
+ * epilogue (replaces all-reduce SUM + h4b_residual_acc). */
+int h4b_tp_allreduce_sum_residual(const h4b_tp_group *group, const int32_t *acc, float *x, const float *absmax,
+                                  const float *w_scales, int n, void *stream);
+/* pairs[2r] = rank r's logits[local_index], pairs[2r+1] = its local_index +
+ * vocab_offset (as doubles): the greedy candidates of every rank. */
+int h4b_tp_gather_best(const h4b_tp_group *group, const float *logits, const int32_t *local_index,
+                       int vocab_offset, double *pairs, void *stream);
+
 /* ---- prefill ----------------------------------------------------------------
  * Scratch for h4b_prefill, owned by the caller: buffers for up to max_tokens
  * prompt rows (16-byte aligned). attn_partials holds attn_queries * kv_heads

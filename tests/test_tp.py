@@ -126,7 +126,7 @@ def test_two_rank_sharded_oracle_equals_unsharded():
     np.testing.assert_array_equal(got, want)
 
 
-def _tp_gpu_rank(rank, world, port, config_name, results):
+def _tp_gpu_rank(rank, world, port, config_name, results, graph=False, comm="p2p"):
     import datetime
 
     from harsh4b_b200.synthetic import qwen3_4b_config
@@ -138,13 +138,13 @@ def _tp_gpu_rank(rank, world, port, config_name, results):
     try:
         config = tiny_config() if config_name == "tiny" else qwen3_4b_config(num_hidden_layers=2)
         ck = synthetic_checkpoint(config, seed=SEED)
-        model = TensorParallelQwen(ck, kv_dtype="float16", attn_splits=16)
+        model = TensorParallelQwen(ck, kv_dtype="float16", attn_splits=16, comm=comm)
         prompt = synthetic_prompt(config, STEPS, seed=SEED)
         state = model.new_state(2 * STEPS)
         rows, greedy = [], []
         fed = list(prompt)
         for i in range(2 * STEPS):
-            token, local = model.forward_token(int(fed[i]), state)
+            token, local = model.forward_token(int(fed[i]), state, graph=graph)
             parts = [torch.empty_like(local) for _ in range(world)]
             dist.all_gather(parts, local)
             rows.append(torch.cat(parts).cpu().numpy())
@@ -153,6 +153,7 @@ def _tp_gpu_rank(rank, world, port, config_name, results):
                 if i + 1 < 2 * STEPS:
                     fed.append(token)
         torch.cuda.synchronize()
+        model.close()
         if rank == 0:
             results.put((np.stack(rows), greedy, int(model.model.status())))
     finally:
@@ -160,8 +161,10 @@ def _tp_gpu_rank(rank, world, port, config_name, results):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("config_name", ["tiny", "qwen3_4b_2layer"])
-def test_two_gpu_tensor_parallel_matches_oracle(config_name):
+@pytest.mark.parametrize("config_name,graph,comm", [("tiny", False, "nccl"), ("qwen3_4b_2layer", True, "nccl"),
+                                                    ("tiny", False, "p2p"), ("tiny", True, "p2p"),
+                                                    ("qwen3_4b_2layer", False, "p2p"), ("qwen3_4b_2layer", True, "p2p")])
+def test_two_gpu_tensor_parallel_matches_oracle(config_name, graph, comm):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from harsh4b_b200.synthetic import qwen3_4b_config
@@ -169,7 +172,8 @@ def test_two_gpu_tensor_parallel_matches_oracle(config_name):
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_tp_gpu_rank, args=(r, 2, port, config_name, results)) for r in range(2)]
+    procs = [ctx.Process(target=_tp_gpu_rank, args=(r, 2, port, config_name, results, graph, comm))
+             for r in range(2)]
     for p in procs:
         p.start()
     try:
