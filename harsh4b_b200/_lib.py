@@ -52,7 +52,7 @@ class BatchStateDesc(ctypes.Structure):
 class PrefillScratchDesc(ctypes.Structure):
     """Mirror of ``h4b_prefill_scratch``."""
 
-    _fields_ = [("max_tokens", _i32), ("attn_queries", _i32)] + [
+    _fields_ = [("max_tokens", _i32), ("attn_queries", _i32), ("attn_splits", _i32)] + [
         (n, _vp) for n in ("x", "x8", "act_scale", "act_sum", "qkv", "attended", "gate_up", "act", "proj", "tokens",
                            "positions", "attn_partials", "attn_counters")]
 

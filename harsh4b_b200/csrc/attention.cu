@@ -466,6 +466,10 @@ __global__ void __launch_bounds__(256) gqa_merge_kernel(const AttnArgs a) {
 
 int launch_attention(const AttnArgs& a, int kv_dtype, int batch, cudaStream_t stream, bool pdl) {
     if (a.groups < 1 || a.groups > kMaxGroups || a.splits < 1 || a.kv_heads < 1 || batch < 1) return H4B_EINVAL;
+    if (!g_prepared) {  // the shared-memory opt-in of gqa_split_kernel<float>
+        const int rc = prepare_kernels();
+        if (rc) return rc;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.splits, a.kv_heads, batch);
     cfg.blockDim = dim3(32 * a.groups);

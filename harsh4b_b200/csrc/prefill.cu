@@ -15,8 +15,11 @@
 // The second launch reads back the cache values the first one stored, in
 // the cache precision, exactly as the decode kernel stages its own new key
 // and value, so every prompt row equals a chain decode step with the same
-// attention splits bit for bit. Only the last row goes through the LM head
-// (its logits and greedy token are what forward_token returns).
+// attention splits bit for bit. The split count is the scratch's own: one
+// split (the default) lets each query's CTA walk its whole context, which
+// stays in L2 for the layer, with no partials and no merge. Only the last
+// row goes through the LM head (its logits and greedy token are what
+// forward_token returns).
 
 namespace h4b {
 
@@ -73,11 +76,12 @@ int validate_prefill(const h4b_model* m, const h4b_state* s, const h4b_prefill_s
     int rc = validate(m, s);
     if (rc) return rc;
     if (!p || count < 1 || count > p->max_tokens || p->attn_queries < 1) return H4B_EINVAL;
+    if (p->attn_splits < 1 || p->attn_splits > 64) return H4B_EINVAL;
     const void* required[] = {p->x, p->x8, p->act_scale, p->act_sum, p->qkv, p->attended, p->gate_up, p->act,
                               p->proj, p->tokens, p->positions};
     for (const void* q : required)
         if (!q || (reinterpret_cast<uintptr_t>(q) & 15)) return H4B_EINVAL;
-    if (s->attn_splits > 1 && (!p->attn_partials || !p->attn_counters)) return H4B_EINVAL;
+    if (p->attn_splits > 1 && (!p->attn_partials || !p->attn_counters)) return H4B_EINVAL;
     return 0;
 }
 
@@ -137,7 +141,7 @@ int prefill(const h4b_model* m, const h4b_state* s, const h4b_prefill_scratch* p
             a.time_stride = d;
             a.batch_stride = 0;
             a.position = p->positions + c0; a.capacity = s->capacity;
-            a.groups = m->heads / m->kv_heads; a.kv_heads = m->kv_heads; a.splits = s->attn_splits;
+            a.groups = m->heads / m->kv_heads; a.kv_heads = m->kv_heads; a.splits = p->attn_splits;
             a.partials = p->attn_partials; a.counters = p->attn_counters;
             a.out = p->attended + static_cast<size_t>(c0) * q_size; a.out_batch_stride = q_size;
             if ((rc = launch_attention(a, s->kv_dtype, n, stream, false))) return rc;

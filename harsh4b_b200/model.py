@@ -233,10 +233,12 @@ class PrefillScratch:
         self.proj = torch.zeros(M, H, **f32)
         self.tokens = torch.zeros(M, **i32)
         self.positions = torch.zeros(M, **i32)
-        self.partials = torch.zeros(self.attn_queries * model.kv_heads * self.splits * model.groups *
-                                    (model.head_dim + 4), **f32)
-        self.counters = torch.zeros(self.attn_queries * model.kv_heads, **i32)
-        self.desc = PrefillScratchDesc(M, self.attn_queries, *[t.data_ptr() for t in (
+        if not 1 <= self.splits <= 64:
+            raise ValueError("prefill attention splits must be in 1..64")
+        parts = self.attn_queries * model.kv_heads * self.splits if self.splits > 1 else 1
+        self.partials = torch.zeros(parts * model.groups * (model.head_dim + 4), **f32)
+        self.counters = torch.zeros(max(1, self.attn_queries * model.kv_heads if self.splits > 1 else 1), **i32)
+        self.desc = PrefillScratchDesc(M, self.attn_queries, self.splits, *[t.data_ptr() for t in (
             self.x, self.x8, self.act_scale, self.act_sum, self.qkv, self.attended, self.gate_up, self.act,
             self.proj, self.tokens, self.positions, self.partials, self.counters)])
 
@@ -371,12 +373,13 @@ class CudaQwen:
         current.wait_stream(state.stream)
         return state.logits
 
-    def prefill(self, token_ids, state: CudaDecodeState, max_tokens: int = 2048) -> torch.Tensor:
+    def prefill(self, token_ids, state: CudaDecodeState, max_tokens: int = 2048,
+                attn_splits: int = 1) -> torch.Tensor:
         """Feed a prompt in one pass per `max_tokens` rows (h4b_prefill): the
-        body projections run as tensor-core GEMMs over the prompt rows.
-        Returns the last token's logits; the state then stands where
-        forward_token over the same ids (with the state's attention splits)
-        leaves it, bit for bit."""
+        body projections run as tensor-core GEMMs over the prompt rows, each
+        prompt query's attention in `attn_splits` context splits. Returns the
+        last token's logits; the state then stands where forward_token over
+        the same ids with that split count leaves it, bit for bit."""
         ids = np.asarray([int(t) for t in token_ids], dtype=np.int32)
         if ids.size == 0:
             raise ValueError("empty prompt")
@@ -388,8 +391,8 @@ class CudaQwen:
             raise ValueError("token ID outside the vocabulary")
         rows = min(int(max_tokens), int(ids.size))
         scratch = self._prefill_scratch
-        if scratch is None or scratch.max_tokens < rows or scratch.splits != state.splits:
-            scratch = self._prefill_scratch = PrefillScratch(self, rows, state.splits)
+        if scratch is None or scratch.max_tokens < rows or scratch.splits != int(attn_splits):
+            scratch = self._prefill_scratch = PrefillScratch(self, rows, int(attn_splits))
         current = torch.cuda.current_stream(self.device)
         state.stream.wait_stream(current)
         with torch.cuda.stream(state.stream):

@@ -329,12 +329,14 @@ int h4b_tp_gather_best(const h4b_tp_group *group, const float *logits, const int
 
 /* ---- prefill ----------------------------------------------------------------
  * Scratch for h4b_prefill, owned by the caller: buffers for up to max_tokens
- * prompt rows (16-byte aligned). attn_partials holds attn_queries * kv_heads
- * * attn_splits * groups * (head_dim + 4) floats and attn_counters
- * attn_queries * kv_heads ints (zero at creation; the kernels leave them
- * zero), where attn_splits is the session's. */
+ * prompt rows (16-byte aligned). attn_splits is the number of context splits
+ * of every prompt query's attention (1..64; 1 = each query walks its whole
+ * context in one CTA, no merge). With attn_splits > 1, attn_partials holds
+ * attn_queries * kv_heads * attn_splits * groups * (head_dim + 4) floats and
+ * attn_counters attn_queries * kv_heads ints (zero at creation; the kernels
+ * leave them zero). */
 typedef struct h4b_prefill_scratch {
-    int max_tokens, attn_queries;
+    int max_tokens, attn_queries, attn_splits;
     float *x;           /* [max_tokens][hidden] */
     int8_t *x8;         /* [max_tokens][max(hidden, heads*head_dim, intermediate)] */
     float *act_scale;   /* [max_tokens] */
@@ -356,8 +358,8 @@ typedef struct h4b_prefill_scratch {
  * cpu_lightspark.py:809-810), with the body projections as tensor-core GEMMs
  * over all prompt rows. Afterwards state->logits holds the last row's
  * logits, next_token/token its greedy token and *position has advanced by
- * count -- bit for bit what count h4b_decode_step calls with the session's
- * attention splits leave. */
+ * count -- bit for bit what count h4b_decode_step calls leave when the
+ * session's attention splits equal scratch->attn_splits. */
 int h4b_prefill(const h4b_model *model, const h4b_state *state, const h4b_prefill_scratch *scratch, int count,
                 void *stream);
 

@@ -25,9 +25,10 @@ def _oracle_run(reference, prompt, steps):
     return last, greedy, np.stack(after) if after else None
 
 
-def _cuda_run(model, prompt, steps, splits, max_tokens=2048):
+def _cuda_run(model, prompt, steps, splits, max_tokens=2048, prefill_splits=None):
     state = model.new_state(len(prompt) + steps, attn_splits=splits)
-    last = model.prefill(prompt, state, max_tokens=max_tokens).cpu().numpy().copy()
+    last = model.prefill(prompt, state, max_tokens=max_tokens,
+                         attn_splits=splits if prefill_splits is None else prefill_splits).cpu().numpy().copy()
     assert state.position == len(prompt)
     greedy, after = [], []
     logits = last
@@ -75,13 +76,29 @@ def test_prefill_then_persistent_decode():
     model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float16", mode="persistent")
     persistent = model.attention_split_rule()
     n = len(prompt)
-    reference = oracle_model(checkpoint, kv_dtype=np.float16, attn_splits=lambda ctx: 16 if ctx <= n else persistent(ctx))
+    reference = oracle_model(checkpoint, kv_dtype=np.float16, attn_splits=lambda ctx: 1 if ctx <= n else persistent(ctx))
     want_last, want_greedy, want_after = _oracle_run(reference, prompt, 8)
-    got_last, got_greedy, got_after = _cuda_run(model, prompt, 8, 16)
+    got_last, got_greedy, got_after = _cuda_run(model, prompt, 8, 16, prefill_splits=1)
     np.testing.assert_array_equal(got_last, want_last)
     assert got_greedy == want_greedy
     np.testing.assert_array_equal(got_after, want_after)
     assert model.status() == 0
+
+
+@pytest.mark.parametrize("prefill_splits", [1, 2])
+def test_prefill_split_count_independent_of_the_session(prefill_splits):
+    """The prompt's queries use the prefill's split count, later tokens the
+    session's: the oracle is told each."""
+    checkpoint = synthetic_checkpoint(tiny_config(), seed=37)
+    prompt = synthetic_prompt(checkpoint.config, 90, seed=8)
+    model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float16", mode="chain")
+    n = len(prompt)
+    reference = oracle_model(checkpoint, kv_dtype=np.float16, attn_splits=lambda ctx: prefill_splits if ctx <= n else 5)
+    want_last, want_greedy, want_after = _oracle_run(reference, prompt, 4)
+    got_last, got_greedy, got_after = _cuda_run(model, prompt, 4, 5, prefill_splits=prefill_splits)
+    np.testing.assert_array_equal(got_last, want_last)
+    assert got_greedy == want_greedy
+    np.testing.assert_array_equal(got_after, want_after)
 
 
 def test_qwen_shaped_prefill_matches_oracle():

@@ -75,11 +75,11 @@ def test_cuda_runtime_matches_oracle_greedy_and_sampled():
     checkpoint = synthetic_checkpoint(tiny_config(), seed=3)
     prompt = synthetic_prompt(checkpoint.config, 10, seed=3)
     model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float32")
-    # the prompt goes through one prefill pass (the session's fixed split
-    # count), later tokens through the persistent step (its per-context rule)
+    # the prompt goes through one prefill pass (one split per query), later
+    # tokens through the persistent step (its per-context rule)
     decode_rule, n = model.attention_split_rule(), len(prompt)
     reference = oracle_model(checkpoint, kv_dtype=np.float32,
-                             attn_splits=lambda ctx: model.attn_splits if ctx <= n else decode_rule(ctx))
+                             attn_splits=lambda ctx: 1 if ctx <= n else decode_rule(ctx))
     for temperature in (0.0, 0.7):
         rt = CudaRuntime(model=model, tokenizer=_Tokenizer(model.vocab), seed=11)
         draws = np.random.default_rng(11)
