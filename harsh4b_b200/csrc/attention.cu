@@ -246,14 +246,16 @@ __device__ __forceinline__ float transpose_reduce32(float v[32], int lane) {
 template <typename KV>
 __device__ __forceinline__ void stage_subtile(const KV* kc, const KV* vc, long long time_stride, int base, int n,
                                               int skip, KV* ks, KV* vs, int tid, int threads) {
-    constexpr int kRowVecs = kHeadDim * sizeof(KV) / 16;
-    for (int i = tid; i < 2 * n * kRowVecs; i += threads) {
-        const int which = i / (n * kRowVecs), rest = i % (n * kRowVecs);
-        const int r = rest / kRowVecs, piece = rest % kRowVecs;
+    constexpr int kRowVecs = kHeadDim * sizeof(KV) / 16;  // a power of two: no runtime division
+#pragma unroll 1
+    for (int i = tid; i < n * kRowVecs; i += threads) {
+        const int r = i / kRowVecs, piece = i % kRowVecs;
         if (base + r == skip) continue;
-        const KV* src = (which ? vc : kc) + static_cast<long long>(base + r) * time_stride;
-        async_copy16(reinterpret_cast<uint4*>((which ? vs : ks) + r * kv_row_stride<KV>()) + piece,
-                     reinterpret_cast<const uint4*>(src) + piece);
+        const long long src = static_cast<long long>(base + r) * time_stride;
+        async_copy16(reinterpret_cast<uint4*>(ks + r * kv_row_stride<KV>()) + piece,
+                     reinterpret_cast<const uint4*>(kc + src) + piece);
+        async_copy16(reinterpret_cast<uint4*>(vs + r * kv_row_stride<KV>()) + piece,
+                     reinterpret_cast<const uint4*>(vc + src) + piece);
     }
 }
 
@@ -275,21 +277,21 @@ __device__ __forceinline__ void stage_subtile(const KV* kc, const KV* vc, long l
 template <typename KV>
 __device__ __forceinline__ void attend_subtile(const float* qs, const KV* ks, const KV* vs, int n, float scale,
                                                int lane, float& m, float& l, float4& o) {
+    // The loops over rounds, token steps and V tokens stay rolled: this code
+    // runs once per layer in the persistent kernel, where every instruction
+    // is fetched cold, so a short body executed many times beats a long
+    // unrolled one. The arithmetic and its order are the unrolled form's.
     constexpr int S = kv_row_stride<KV>();
     const int qi = lane >> 3, tl = lane & 7;
+    const int rounds = n > 32 ? 2 : 1;
     float4 qv[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) qv[j] = *reinterpret_cast<const float4*>(qs + 4 * (qi + 4 * j));
-    float p_round[2];
-    float mt = -INFINITY;
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        if (32 * r >= n) {  // uniform: the sub-tile has no second round
-            p_round[r] = -INFINITY;
-            continue;
-        }
+    float p0 = -INFINITY, p1 = -INFINITY;
+#pragma unroll 1
+    for (int r = 0; r < rounds; ++r) {
         float mine = 0.f;
-#pragma unroll
+#pragma unroll 1
         for (int st = 0; st < 4; ++st) {
             const KV* krow = ks + min(32 * r + 8 * st + tl, n - 1) * S + 4 * qi;
             float p[8];
@@ -298,26 +300,27 @@ __device__ __forceinline__ void attend_subtile(const float* qs, const KV* ks, co
             const float s3 = ((p[0] + p[4]) + (p[2] + p[6])) + ((p[1] + p[5]) + (p[3] + p[7]));
             const float s4 = s3 + __shfl_xor_sync(0xffffffffu, s3, 16);
             const float s5 = s4 + __shfl_xor_sync(0xffffffffu, s4, 8);
-            if (st == qi) mine = s5;
+            mine = st == qi ? s5 : mine;
         }
-        const float sc = __fmul_rn(mine, scale);
-        p_round[r] = (32 * r + lane < n) ? sc : -INFINITY;
-        mt = fmaxf(mt, p_round[r]);
+        const float sc = (32 * r + lane < n) ? __fmul_rn(mine, scale) : -INFINITY;
+        if (r == 0) p0 = sc;
+        else p1 = sc;
     }
     H4B_TRACE_ATTN(1510);
-    mt = warp_max(mt);
-#pragma unroll
-    for (int r = 0; r < 2; ++r) p_round[r] = (32 * r + lane < n) ? exp_cw(p_round[r] - mt) : 0.f;
-    const float lt = warp_sum(p_round[0] + p_round[1]);
+    const float mt = warp_max(fmaxf(p0, p1));
+    p0 = lane < n ? exp_cw(p0 - mt) : 0.f;
+    p1 = 32 + lane < n ? exp_cw(p1 - mt) : 0.f;
+    const float lt = warp_sum(p0 + p1);
     H4B_TRACE_ATTN(1511);
     float4 ot = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        if (32 * r >= n) break;
-#pragma unroll
+#pragma unroll 1
+    for (int r = 0; r < rounds; ++r) {
+        const float pr = r == 0 ? p0 : p1;
+        const KV* vrow = vs + 4 * lane;
+#pragma unroll 4
         for (int t = 0; t < 32; ++t) {
-            const float p = __shfl_sync(0xffffffffu, p_round[r], t);
-            const float4 v = load4<KV>(vs + min(32 * r + t, n - 1) * S + 4 * lane);
+            const float p = __shfl_sync(0xffffffffu, pr, t);
+            const float4 v = load4<KV>(vrow + min(32 * r + t, n - 1) * S);
             ot.x = __fmaf_rn(p, v.x, ot.x);
             ot.y = __fmaf_rn(p, v.y, ot.y);
             ot.z = __fmaf_rn(p, v.z, ot.z);

@@ -95,48 +95,83 @@ struct Seg {
     int width, kb, r0, nrows, tile_rows, ntiles;
 };
 
-// Rows of GEMV segment g (4 per layer, then the LM head) that CTA `cta` owns.
-__device__ __forceinline__ Seg mk_segment(const MkArgs& a, int g, int cta, int nctas) {
+// Where one CTA's rows of each kind of GEMV segment lie: per kind (qkv, o,
+// gate/up, down, LM head) the first row, the row count, rows per ring tile
+// and the tile count. Computed once per launch by mk_geometry, so the
+// per-segment code holds no divisions.
+struct SegGeo {
+    int r0, nrows, tile_rows, ntiles;
+};
+constexpr int kSegKinds = 5;
+static_assert(kSegKinds * sizeof(SegGeo) <= 128, "geometry table region");
+
+__device__ __noinline__ void mk_geometry(const MkArgs& a, int cta, int nctas, SegGeo* geo) {
+    const h4b_model& m = a.m;
+    const int Q = m.heads * m.head_dim, KV = m.kv_heads * m.head_dim;
+    const int rows[kSegKinds] = {Q + 2 * KV, m.hidden, 2 * m.intermediate, m.hidden, m.vocab};
+    const int kb[kSegKinds] = {m.hidden / 2, Q / 2, m.hidden / 2, m.intermediate / 2, m.hidden / 2};
+    for (int k = 0; k < kSegKinds; ++k) {
+        const int align = k == SEG_GATE_UP ? 2 * kSwigluBlock : 1;
+        const uint32_t units = static_cast<uint32_t>(rows[k] / align);
+        // units * (cta + 1) < 2^32: the host checks vocab * CTAs
+        const int u0 = static_cast<int>(units * static_cast<uint32_t>(cta) / static_cast<uint32_t>(nctas));
+        const int u1 = static_cast<int>(units * static_cast<uint32_t>(cta + 1) / static_cast<uint32_t>(nctas));
+        SegGeo gk;
+        gk.r0 = u0 * align;
+        gk.nrows = (u1 - u0) * align;
+        // Fewest rounds of kMkWarps tiles that fit a ring slot, then rows
+        // spread evenly over those tiles, so no warp has a short last round
+        // while the others idle.
+        const int max_rows = max(1, a.slot_bytes / kb[k]);
+        const int rounds = ((gk.nrows + max_rows - 1) / max_rows + kMkWarps - 1) / kMkWarps;
+        const int tiles = max(1, min(rounds * kMkWarps, gk.nrows));
+        gk.tile_rows = max(1, (gk.nrows + tiles - 1) / tiles);
+        gk.ntiles = (gk.nrows + gk.tile_rows - 1) / gk.tile_rows;
+        geo[k] = gk;
+    }
+}
+
+// Rows of GEMV segment g (4 per layer, then the LM head) that this CTA owns.
+__device__ __forceinline__ Seg mk_segment(const MkArgs& a, const SegGeo* geo, int g) {
     const h4b_model& m = a.m;
     const int H = m.hidden, I = m.intermediate;
     const int Q = m.heads * m.head_dim, KV = m.kv_heads * m.head_dim;
+    const int kind = g == 4 * m.layers ? 4 : (g & 3);
+    const size_t l = static_cast<size_t>(g >> 2);
     Seg s;
-    int rows, align = 1;
-    if (g == 4 * m.layers) {
-        s.w = m.w_embed; s.ws = m.s_embed; rows = m.vocab; s.width = H;
-    } else {
-        const int l = g >> 2;
-        switch (g & 3) {
-            case SEG_QKV:
-                rows = Q + 2 * KV; s.width = H;
-                s.w = m.w_qkv + static_cast<size_t>(l) * rows * (H / 2);
-                s.ws = m.s_qkv + static_cast<size_t>(l) * rows;
-                break;
-            case SEG_O:
-                rows = H; s.width = Q;
-                s.w = m.w_o + static_cast<size_t>(l) * H * (Q / 2);
-                s.ws = m.s_o + static_cast<size_t>(l) * H;
-                break;
-            case SEG_GATE_UP:
-                rows = 2 * I; s.width = H; align = 2 * kSwigluBlock;
-                s.w = m.w_gate_up + static_cast<size_t>(l) * 2 * I * (H / 2);
-                s.ws = m.s_gate_up + static_cast<size_t>(l) * 2 * I;
-                break;
-            default:
-                rows = H; s.width = I;
-                s.w = m.w_down + static_cast<size_t>(l) * H * (I / 2);
-                s.ws = m.s_down + static_cast<size_t>(l) * H;
-                break;
-        }
+    switch (kind) {
+        case SEG_QKV:
+            s.width = H;
+            s.w = m.w_qkv + l * (Q + 2 * KV) * (H / 2);
+            s.ws = m.s_qkv + l * (Q + 2 * KV);
+            break;
+        case SEG_O:
+            s.width = Q;
+            s.w = m.w_o + l * H * (Q / 2);
+            s.ws = m.s_o + l * H;
+            break;
+        case SEG_GATE_UP:
+            s.width = H;
+            s.w = m.w_gate_up + l * 2 * I * (H / 2);
+            s.ws = m.s_gate_up + l * 2 * I;
+            break;
+        case SEG_DOWN:
+            s.width = I;
+            s.w = m.w_down + l * H * (I / 2);
+            s.ws = m.s_down + l * H;
+            break;
+        default:
+            s.width = H;
+            s.w = m.w_embed;
+            s.ws = m.s_embed;
+            break;
     }
     s.kb = s.width >> 1;
-    const int units = rows / align;
-    const int u0 = static_cast<int>(static_cast<long long>(cta) * units / nctas);
-    const int u1 = static_cast<int>(static_cast<long long>(cta + 1) * units / nctas);
-    s.r0 = u0 * align;
-    s.nrows = (u1 - u0) * align;
-    s.tile_rows = max(1, min((s.nrows + kMkWarps - 1) / kMkWarps, a.slot_bytes / s.kb));
-    s.ntiles = (s.nrows + s.tile_rows - 1) / s.tile_rows;
+    const SegGeo gk = geo[kind];
+    s.r0 = gk.r0;
+    s.nrows = gk.nrows;
+    s.tile_rows = gk.tile_rows;
+    s.ntiles = gk.ntiles;
     return s;
 }
 
@@ -206,6 +241,7 @@ __device__ void mk_poll_lane(const unsigned long long* w, int lane_id, int group
 // returns the max of the payloads it saw (0 when it holds none).
 __device__ float mk_poll_max(const unsigned long long* w, int n, uint32_t tag, int* flags) {
     float mx = 0.f;
+    #pragma unroll 1
     for (int i = threadIdx.x; i < n; i += kMkConsumers) {
         PollClock clk;
         unsigned long long word = ll_load(w + i);
@@ -270,6 +306,7 @@ __device__ float mk_prologue_rms_g(const float* xs, const unsigned long long* xw
         red[warp] = w0;
         if (warp == 0) red[kRmsLanes / 32 - 1] = w1;
     }
+    async_copy_wait_all();  // gamma_s (and the segment's scales), issued before the poll
     named_sync(1, kMkConsumers);
     float total = 0.f;
     for (int w = 0; w < kRmsLanes / 32; ++w) total += red[w];
@@ -390,7 +427,7 @@ __device__ float mk_prologue_quant(const unsigned long long* vw, const unsigned 
 // This CTA's tiles of one GEMV segment: int32 row sums into acc_s.
 template <int SLOTS, int RB>
 __device__ void mk_tiles(const Seg& sg, uint32_t seq0, int stages, int slot_bytes, const uint8_t* ring, uint64_t* full,
-                         uint64_t* empty, const int8_t* xq, int32_t* acc_s, int* flags) {
+                         uint64_t* empty, const int8_t* xq, int32_t* acc_s, int* flags, int trace_ev) {
     constexpr bool kXReg = SLOTS <= kMaxRegSlots;
     constexpr int kXSlots = kXReg ? SLOTS : 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -416,6 +453,7 @@ __device__ void mk_tiles(const Seg& sg, uint32_t seq0, int stages, int slot_byte
         }
     }
     bias *= -8;
+    if (trace_ev >= 0 && threadIdx.x == 0) H4B_TRACE_ANY(trace_ev);
     for (int t = warp; t < sg.ntiles; t += kMkWarps) {
         const uint32_t gseq = seq0 + t;
         const int slot = gseq % stages;
@@ -440,46 +478,51 @@ __device__ void mk_tiles(const Seg& sg, uint32_t seq0, int stages, int slot_byte
         if (lane == 0) mbar_arrive(&empty[slot]);
         if (lane == 0 && gseq >= 40 && gseq < 140) H4B_TRACE_ANY(1300 + gseq - 40);
     }
-    named_sync(1, kMkConsumers);  // acc_s complete
+    async_copy_wait_all();        // the segment's row scales
+    named_sync(1, kMkConsumers);  // acc_s complete, scales visible
 }
 
 __device__ void mk_run_tiles(const Seg& sg, uint32_t seq0, int stages, int slot_bytes, const uint8_t* ring, uint64_t* full,
-                             uint64_t* empty, const int8_t* xq, int32_t* acc_s, int* flags) {
+                             uint64_t* empty, const int8_t* xq, int32_t* acc_s, int* flags, int trace_ev = -1) {
     const int need = ((sg.width >> 5) + 31) / 32;
-    if (need <= 1) mk_tiles<1, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 2) mk_tiles<2, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 3) mk_tiles<3, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 4) mk_tiles<4, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 6) mk_tiles<6, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 8) mk_tiles<8, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 10) mk_tiles<10, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
-    else if (need <= 12) mk_tiles<12, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
-    else mk_tiles<16, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags);
+    if (need <= 1) mk_tiles<1, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
+    else if (need <= 2) mk_tiles<2, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
+    else if (need <= 3) mk_tiles<3, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
+    else if (need <= 4) mk_tiles<4, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
+    else if (need <= 6) mk_tiles<6, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
+    else if (need <= 8) mk_tiles<8, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
+    else if (need <= 10) mk_tiles<10, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
+    else if (need <= 12) mk_tiles<12, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
+    else mk_tiles<16, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
 }
 
 // Starts the 4-byte async copies of a segment's row scales into sc_s.
 __device__ __forceinline__ void mk_fetch_scales(const Seg& sg, float* sc_s) {
+    #pragma unroll 1
     for (int i = threadIdx.x; i < sg.nrows; i += kMkConsumers) async_copy4(sc_s + i, sg.ws + sg.r0 + i);
 }
 
 // Starts the async copy of an RMSNorm weight (n floats, n % 4 == 0, 16-byte
 // aligned) into gamma_s.
 __device__ __forceinline__ void mk_fetch_gamma(const float* gamma, float* gamma_s, int n) {
+    #pragma unroll 1
     for (int i = threadIdx.x; i < (n >> 2); i += kMkConsumers) async_copy16(gamma_s + 4 * i, gamma + 4 * i);
 }
 
-// Starts fetching what GEMV segment g + 1 needs while segment g's tiles run:
-// its row scales (into scale buffer (g + 1) & 1) and, after an RMSNorm
-// prologue (qkv, gate/up), the norm weight of the next RMSNorm phase.
-__device__ __forceinline__ void mk_prefetch_next(const MkArgs& a, int g, int cta, int nctas, float* sc_base,
-                                                 float* gamma_s) {
+// Starts the async copies of what GEMV segment g itself needs: its row
+// scales (into scale buffer g & 1, which segment g - 2 last read) and, for an
+// RMSNorm prologue (qkv, gate/up, LM head), the norm weight. Issued before
+// the segment's input is polled, so the copies overlap the handoff wait; the
+// RMSNorm prologue and the tile loop wait for them before reading.
+__device__ __forceinline__ void mk_fetch_own(const MkArgs& a, int g, const SegGeo* geo, float* sc_base,
+                                             float* gamma_s) {
     const h4b_model& m = a.m;
-    const int H = m.hidden, l = g >> 2;
-    if (g < 4 * m.layers) mk_fetch_scales(mk_segment(a, g + 1, cta, nctas), sc_base + ((g + 1) & 1) * a.rows_cap);
-    if (g >= 4 * m.layers) return;
-    if ((g & 3) == SEG_QKV) mk_fetch_gamma(m.norm_post + static_cast<size_t>(l) * H, gamma_s, H);
-    if ((g & 3) == SEG_GATE_UP)
-        mk_fetch_gamma(l + 1 < m.layers ? m.norm_in + static_cast<size_t>(l + 1) * H : m.norm_final, gamma_s, H);
+    const int H = m.hidden;
+    const size_t l = static_cast<size_t>(g >> 2);
+    mk_fetch_scales(mk_segment(a, geo, g), sc_base + (g & 1) * a.rows_cap);
+    if (g == 4 * m.layers) mk_fetch_gamma(m.norm_final, gamma_s, H);
+    else if ((g & 3) == SEG_QKV) mk_fetch_gamma(m.norm_in + l * H, gamma_s, H);
+    else if ((g & 3) == SEG_GATE_UP) mk_fetch_gamma(m.norm_post + l * H, gamma_s, H);
 }
 
 __device__ __forceinline__ float mk_value(const int32_t* acc_s, const float* sc_s, int i, float act_scale) {
@@ -508,6 +551,7 @@ __device__ __forceinline__ bool mk_poll_head(const unsigned long long* w, int la
 __device__ float4 mk_merge_direct(const unsigned long long* base, int splits, long long stride, uint32_t tag,
                                   float m0, float l0, float4 o0, int lane, bool& ok) {
     float mmax = -INFINITY;
+    #pragma unroll 1
     for (int s = lane; s < splits; s += 32) {
         float mv = m0;
         if (s != 0) {
@@ -527,6 +571,7 @@ __device__ float4 mk_merge_direct(const unsigned long long* base, int splits, lo
     mmax = warp_max(mmax);
     float l = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    #pragma unroll 1
     for (int s = 0; s < splits; ++s) {
         float ms = m0, ls = l0;
         float4 ov = o0;
@@ -597,6 +642,7 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
                                    kMkConsumers);
     // q/k norm weights and this position's RoPE row into consts_s
     // ([0, d) q gamma, [d, 2d) k gamma, [2d, 2.5d) cos, [2.5d, 3d) sin).
+    #pragma unroll 1
     for (int i = threadIdx.x; i < 3 * d / 4; i += kMkConsumers) {
         const float* src = i < d / 4 ? m.norm_q + static_cast<size_t>(l) * d + 4 * i
                          : i < d / 2 ? m.norm_k + static_cast<size_t>(l) * d + 4 * (i - d / 4)
@@ -605,6 +651,7 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
         async_copy16(consts_s + 4 * i, src);
     }
     if (l == 1) H4B_TRACE(1500);
+    if (l == 2) H4B_TRACE_CTA(16);
 
     const unsigned long long* qkv = xw + a.x.qkv;
     bool ok = true;
@@ -619,6 +666,7 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
         return false;
     }
     if (l == 1) H4B_TRACE(1501);
+    if (l == 2) H4B_TRACE_CTA(17);
     async_copy_wait_all();
     named_sync(1, kMkConsumers);  // consts_s (and the first sub-tile) landed
     if (head_warp) {
@@ -637,6 +685,7 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(d)));
     float mrun = -INFINITY, l_run = 0.f;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    #pragma unroll 1
     for (int base = t0; base < t1; base += kSubTile) {
         const int n = min(kSubTile, t1 - base);
         if (base != t0) {
@@ -650,12 +699,14 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
         async_copy_wait_all();
         named_sync(1, kMkConsumers);
         if (l == 1) H4B_TRACE(1502);
+    if (l == 2) H4B_TRACE_CTA(18);
 #ifdef H4B_PHASE_TRACE
         if (threadIdx.x == 0) g_trace_attn = (l == 1);
 #endif
         if (head_warp) attend_subtile<KV>(consts_s + (3 + warp) * d, ks, vs, n, scale, lane, mrun, l_run, o);
     }
     if (l == 1) H4B_TRACE(1503);
+    if (l == 2) H4B_TRACE_CTA(19);
 
     float4 result = make_float4(0.f, 0.f, 0.f, 0.f);
     const long long pstride = kPartialStride;
@@ -667,6 +718,7 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
             ll_store2(mine + 4 * lane + 2, o.z, o.w, tag_part);
             if (lane == 0) ll_store2(mine + kHeadDim, mrun, l_run, tag_part);
         }
+        if (l == 2) H4B_TRACE_CTA(22);
         return true;
     }
     if (splits == 1) {
@@ -677,46 +729,52 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
     } else if (splits <= a.stage_splits) {
         // Merge in split order (merge_splits' arithmetic), split 0 from
         // registers. The other splits' partials are copied as raw exchange
-        // words into the K/V staging area (free once the math is done) and
-        // re-copied until every word carries tag_part: one L2 round trip per
-        // polling round, and the poll holds no registers.
+        // words into the K/V staging area (free once the math is done). Each
+        // thread re-copies its own pieces until every word carries tag_part,
+        // with no CTA barrier between polling rounds, so a round costs one
+        // L2 round trip; one barrier follows once every thread is done.
         constexpr int kPieces = kPartialStride / 2;  // 16-byte pieces per (split, head) partial
+        constexpr int kWordPieces = kHeadDim / 2 + 1;  // o and (m, l); the last piece holds 2 pad words
         unsigned long long* stage = reinterpret_cast<unsigned long long*>(ks);  // [split][groups][kPartialStride]
-        int* stale_s = reinterpret_cast<int*>(red + 16);
-        const int total = splits * groups * kPieces;
+        const int total = (splits - 1) * groups * kWordPieces;  // pieces of the splits other than 0
         named_sync(1, kMkConsumers);  // every head warp is done reading the K/V sub-tile
+        bool timed_out = false;
         PollClock clk;
+#pragma unroll 1
         for (bool first = true;; first = false) {
+#pragma unroll 1
             for (int i = threadIdx.x; i < total; i += kMkConsumers) {
-                const int piece = i % kPieces, sh = i / kPieces;  // sh = split * groups + head warp
-                if (sh < groups) continue;  // split 0 is this CTA
+                const int piece = i % kWordPieces, sh = groups + i / kWordPieces;  // sh = split * groups + head
                 unsigned long long* dst = stage + static_cast<long long>(sh) * pstride + 2 * piece;
                 if (!first && ll_tag(dst[0]) == tag_part && ll_tag(dst[1]) == tag_part) continue;
                 async_copy16(dst, part + static_cast<long long>(sh) * pstride + 2 * piece);
             }
             async_copy_wait_all();
-            if (threadIdx.x == 0) *stale_s = 0;
-            named_sync(1, kMkConsumers);
             bool stale = false;
+#pragma unroll 1
             for (int i = threadIdx.x; i < total; i += kMkConsumers) {
-                const int piece = i % kPieces, sh = i / kPieces;
-                if (sh < groups || piece == kPieces - 1) continue;  // the last piece holds 2 pad words
+                const int piece = i % kWordPieces, sh = groups + i / kWordPieces;
                 const unsigned long long* w = stage + static_cast<long long>(sh) * pstride + 2 * piece;
                 stale = stale || ll_tag(w[0]) != tag_part || ll_tag(w[1]) != tag_part;
             }
-            if (stale) *stale_s = 1;
-            named_sync(1, kMkConsumers);
-            if (!*stale_s) break;
-            if (mk_stop(flags, threadIdx.x == 0 && poll_expired(clk))) return false;
+            if (!stale) break;
+            if (poll_expired(clk)) {
+                timed_out = true;
+                break;
+            }
         }
+        static_assert(kWordPieces < kPieces, "pad piece");
+        if (mk_stop(flags, timed_out)) return false;  // its barrier also publishes every staged piece
         if (head_warp) {
             const unsigned long long* mine = stage + warp * pstride;
             float mm = -INFINITY;
+            #pragma unroll 1
             for (int s = lane; s < splits; s += 32)
                 mm = fmaxf(mm, s == 0 ? mrun : ll_value(mine[static_cast<long long>(s) * groups * pstride + kHeadDim]));
             mm = warp_max(mm);
             float lsum = 0.f;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            #pragma unroll 1
             for (int s = 0; s < splits; ++s) {
                 const unsigned long long* w = mine + static_cast<long long>(s) * groups * pstride;
                 const float ls = s == 0 ? l_run : ll_value(w[kHeadDim + 1]);
@@ -741,6 +799,7 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
     }
     if (mk_stop(flags, !ok)) return false;
     if (l == 1) H4B_TRACE(1504);
+    if (l == 2) H4B_TRACE_CTA(20);
     float mx = 0.f;
     if (head_warp) {
         unsigned long long* att = xw + a.x.att + static_cast<long long>(qh) * d + 4 * lane;
@@ -757,11 +816,12 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
     }
     named_sync(1, kMkConsumers);  // red is reused by the next phase
     if (l == 1) H4B_TRACE(1505);
+    if (l == 2) H4B_TRACE_CTA(21);
     return true;
 }
 
 struct MkSmem {
-    int bars, red, xq, gamma, consts, acc, scale, xo, att, ring, total;
+    int bars, red, geo, xq, gamma, consts, acc, scale, xo, att, ring, total;
 };
 
 __host__ __device__ inline MkSmem mk_smem_layout(int xq_bytes, int hidden, int rows_cap, int kv_bytes, int stages,
@@ -769,7 +829,8 @@ __host__ __device__ inline MkSmem mk_smem_layout(int xq_bytes, int hidden, int r
     MkSmem s;
     s.bars = 0;
     s.red = 2 * kMkMaxStages * 8;
-    s.xq = s.red + 64 * 4;
+    s.geo = s.red + 64 * 4;
+    s.xq = s.geo + 128;  // kSegKinds SegGeo entries
     s.gamma = s.xq + xq_region(xq_bytes);
     s.consts = s.gamma + ((hidden * 4 + 127) & ~127);  // attention's q/k norm weights + RoPE row
     s.acc = s.consts + (3 + kMaxGroups) * kHeadDim * 4;  // + one staged q head per warp
@@ -791,6 +852,7 @@ __device__ void mk_finish_token(const MkArgs& a, const Seg& sg, const float* sc_
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int cta = blockIdx.x, nctas = gridDim.x;
     unsigned long long best = 0ull;
+    #pragma unroll 1
     for (int i = tid; i < sg.nrows; i += kMkConsumers) {
         const float v = mk_value(acc_s, sc_s, i, act);
         __stcg(st.logits + sg.r0 + i, v);
@@ -815,6 +877,7 @@ __device__ void mk_finish_token(const MkArgs& a, const Seg& sg, const float* sc_
     named_sync(1, kMkConsumers);
     bool failed = false;
     best = 0ull;
+    #pragma unroll 1
     for (int c = tid; c < nctas; c += kMkConsumers) {
         const unsigned long long* p = xw + a.x.keys + 2 * c;
         PollClock clk;
@@ -856,6 +919,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
     uint64_t* empty = full + kMkMaxStages;
     float* red = reinterpret_cast<float*>(smem + L.red);
     int* flags = reinterpret_cast<int*>(red + 32);  // [0] stop request, [1] consumers' snapshot, [2] tag base
+    SegGeo* geo = reinterpret_cast<SegGeo*>(smem + L.geo);
     int8_t* xq = reinterpret_cast<int8_t*>(smem + L.xq);
     float* gamma_s = reinterpret_cast<float*>(smem + L.gamma);
     int32_t* acc_s = reinterpret_cast<int32_t*>(smem + L.acc);
@@ -894,6 +958,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         }
         fence_mbar_init();
     }
+    if (warp == 1 && lane == 0) mk_geometry(a, cta, nctas, geo);
     __syncthreads();
     if (flags[0]) return;  // before any bulk copy is issued
     const uint32_t tbase = static_cast<uint32_t>(flags[2]);
@@ -904,7 +969,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
             uint32_t seq = 0;
             bool stop = false;
             for (int g = 0; g <= 4 * L_layers && !stop; ++g) {
-                const Seg sg = mk_segment(a, g, cta, nctas);
+                const Seg sg = mk_segment(a, geo, g);
                 for (int t = 0; t < sg.ntiles; ++t, ++seq) {
                     const int slot = seq % a.stages;
                     if (seq >= static_cast<uint32_t>(a.stages)) {
@@ -917,6 +982,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
                     }
                     const int rows_t = min(sg.tile_rows, sg.nrows - t * sg.tile_rows);
                     const uint32_t bytes = static_cast<uint32_t>(rows_t) * sg.kb;
+                    if (seq >= 40 && seq < 140) H4B_TRACE_ANY(1400 + seq - 40);
                     mbar_arrive_expect_tx(&full[slot], bytes);
                     bulk_g2s(ring + static_cast<size_t>(slot) * a.slot_bytes,
                              sg.w + static_cast<size_t>(sg.r0 + t * sg.tile_rows) * sg.kb, bytes, &full[slot]);
@@ -939,19 +1005,19 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
     // Embedding (cpu_lightspark.py:341-349), computed by every CTA into xs;
     // the rows this CTA owns in the o/down partition start its copy of x.
     {
-        const Seg so = mk_segment(a, SEG_O, cta, nctas);
+        const Seg so = mk_segment(a, geo, SEG_O);
         const bool ok = token >= 0 && token < m.vocab;
         if (!ok && cta == 0 && tid == 0) report(kStatusBadToken);
         const float scale = ok ? m.s_embed[token] : 0.f;
         const uint8_t* row = m.w_embed + static_cast<size_t>(ok ? token : 0) * (H >> 1);
+        #pragma unroll 1
         for (int j = tid; j < (H >> 1); j += kMkConsumers) {
             const int8_t byte = static_cast<int8_t>(row[j]);
             xs[2 * j] = ok ? __fmul_rn(static_cast<float>(static_cast<int8_t>(byte << 4) >> 4), scale) : 0.f;
             xs[2 * j + 1] = ok ? __fmul_rn(static_cast<float>(byte >> 4), scale) : 0.f;
         }
-        mk_fetch_gamma(m.norm_in, gamma_s, H);
-        mk_fetch_scales(mk_segment(a, SEG_QKV, cta, nctas), sc_base);
         named_sync(1, kMkConsumers);
+        #pragma unroll 1
         for (int i = tid; i < so.nrows; i += kMkConsumers) xo[i] = xs[so.r0 + i];
     }
 
@@ -964,7 +1030,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         const int l = g >> 2;
         const int kind = g == last ? 4 : (g & 3);  // SEG_* or 4 = LM head
         const uint32_t tl = tbase + kTagsPerLayer * l;
-        const Seg sg = mk_segment(a, g, cta, nctas);
+        const Seg sg = mk_segment(a, geo, g);
         const float* sc_s = sc_base + (g & 1) * a.rows_cap;
         H4B_TRACE(8 + 3 * g);
         if (g >= 8 && g < 12) H4B_TRACE_CTA(4 * (g - 8));
@@ -978,7 +1044,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
             H4B_TRACE_VAL(1650 + (g - 8), t1 - t0);
         }
 #endif
-        async_copy_wait_all();  // this segment's scales (and gamma), fetched a segment ago
+        mk_fetch_own(a, g, geo, sc_base, gamma_s);
 
         // ---- prologue ----
         float act;
@@ -1000,10 +1066,11 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         }
         H4B_TRACE(8 + 3 * g + 1);
         if (g >= 8 && g < 12) H4B_TRACE_CTA(4 * (g - 8) + 1);
-        mk_prefetch_next(a, g, cta, nctas, sc_base, gamma_s);
+        if (g >= 8 && g < 12) H4B_TRACE(1700 + (g - 8));
 
         // ---- tiles ----
-        mk_run_tiles(sg, seq, a.stages, a.slot_bytes, ring, full, empty, xq, acc_s, flags);
+        mk_run_tiles(sg, seq, a.stages, a.slot_bytes, ring, full, empty, xq, acc_s, flags,
+                     g >= 8 && g < 12 ? 1710 + (g - 8) : -1);
         seq += sg.ntiles;
         H4B_TRACE(8 + 3 * g + 2);
         if (g >= 8 && g < 12) H4B_TRACE_CTA(4 * (g - 8) + 2);
@@ -1011,6 +1078,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
 
         // ---- epilogue ----
         if (kind == SEG_QKV) {
+            #pragma unroll 1
             for (int i = tid; i < sg.nrows; i += kMkConsumers)
                 ll_store(xw + a.x.qkv + sg.r0 + i, mk_value(acc_s, sc_s, i, act), tl + TAG_QKV);
             if (cta < items &&
@@ -1020,12 +1088,14 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         } else if (kind == SEG_O || kind == SEG_DOWN) {
             const long long dst = kind == SEG_O ? a.x.x_o : a.x.x_down;
             const uint32_t tag = tl + (kind == SEG_O ? TAG_XO : TAG_XDOWN);
+            #pragma unroll 1
             for (int i = tid; i < sg.nrows; i += kMkConsumers) {
                 xo[i] = __fadd_rn(xo[i], mk_value(acc_s, sc_s, i, act));
                 ll_store(xw + dst + sg.r0 + i, xo[i], tag);
             }
         } else if (kind == SEG_GATE_UP) {
             float local = 0.f;
+            #pragma unroll 1
             for (int p = tid; p < (sg.nrows >> 1); p += kMkConsumers) {
                 const int b = p / kSwigluBlock, j = p % kSwigluBlock;
                 const int gi = 2 * kSwigluBlock * b + j;
@@ -1062,6 +1132,8 @@ static int plan_persistent(const h4b_model* m, const h4b_state* s, MkPlan* p) {
     if (max_width > kMkMaxWidth) return H4B_EUNSUPPORTED;
     const int nctas = sm_count();
     if (nctas > kMkConsumers || nctas > kMkMaxCtas) return H4B_EUNSUPPORTED;  // one act maximum per thread
+    if (static_cast<long long>(std::max(m->vocab, 2 * m->intermediate)) * nctas >= (1ll << 32))
+        return H4B_EUNSUPPORTED;  // mk_geometry's 32-bit row partition
     if (std::max(q_size, m->intermediate) > kMkQuantGroups * 8 * kMkConsumers) return H4B_EUNSUPPORTED;
     if (m->heads / m->kv_heads > kMkWarps) return H4B_EUNSUPPORTED;  // one consumer warp per q head of a group
     MkArgs& a = p->args;
