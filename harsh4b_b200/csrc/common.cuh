@@ -157,6 +157,13 @@ __device__ __forceinline__ void async_copy4(void* dst, const void* src) {
 __device__ __forceinline__ void async_copy16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_addr(dst)), "l"(src) : "memory");
 }
+// Closes the async copies issued so far into one group.
+__device__ __forceinline__ void async_copy_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Waits until at most N of this thread's committed copy groups are pending.
+template <int N>
+__device__ __forceinline__ void async_copy_wait_prior() {
+    asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory");
+}
 __device__ __forceinline__ void async_copy_wait_all() {
     asm volatile("cp.async.wait_all;" ::: "memory");
 }

@@ -306,7 +306,7 @@ __device__ float mk_prologue_rms_g(const float* xs, const unsigned long long* xw
         red[warp] = w0;
         if (warp == 0) red[kRmsLanes / 32 - 1] = w1;
     }
-    async_copy_wait_all();  // gamma_s (and the segment's scales), issued before the poll
+    async_copy_wait_prior<1>();  // gamma_s and the segment's scales (the newer group is attention's K/V)
     named_sync(1, kMkConsumers);
     float total = 0.f;
     for (int w = 0; w < kRmsLanes / 32; ++w) total += red[w];
@@ -478,13 +478,20 @@ __device__ void mk_tiles(const Seg& sg, uint32_t seq0, int stages, int slot_byte
         if (lane == 0) mbar_arrive(&empty[slot]);
         if (lane == 0 && gseq >= 40 && gseq < 140) H4B_TRACE_ANY(1300 + gseq - 40);
     }
-    async_copy_wait_all();        // the segment's row scales
+    async_copy_wait_prior<1>();   // the segment's row scales (the newer group is attention's K/V)
     named_sync(1, kMkConsumers);  // acc_s complete, scales visible
 }
 
 __device__ void mk_run_tiles(const Seg& sg, uint32_t seq0, int stages, int slot_bytes, const uint8_t* ring, uint64_t* full,
                              uint64_t* empty, const int8_t* xq, int32_t* acc_s, int* flags, int trace_ev = -1) {
     const int need = ((sg.width >> 5) + 31) / 32;
+    // Three rows per batch where the tile height allows it (more independent
+    // work per pass over the activation), else two.
+    if (sg.tile_rows % 3 == 0 && need <= 4) {
+        if (need <= 3) mk_tiles<3, 3>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
+        else mk_tiles<4, 3>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
+        return;
+    }
     if (need <= 1) mk_tiles<1, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
     else if (need <= 2) mk_tiles<2, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
     else if (need <= 3) mk_tiles<3, 2>(sg, seq0, stages, slot_bytes, ring, full, empty, xq, acc_s, flags, trace_ev);
@@ -607,6 +614,39 @@ __device__ float4 mk_merge_direct(const unsigned long long* base, int splits, lo
     return make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
 }
 
+// Starts the async copies attention needs before the new token's q/k/v
+// exist: the split's first sub-tile of past K/V rows (the new token's row,
+// which arrives from registers, is left out) and the q/k norm weights plus
+// this position's RoPE row into consts_s ([0, d) q gamma, [d, 2d) k gamma,
+// [2d, 2.5d) cos, [2.5d, 3d) sin). From layer 1 on the kernel issues them at
+// the top of the qkv segment, so they land while the qkv input is polled.
+template <typename KV>
+__device__ __forceinline__ void mk_attention_fetch(const MkArgs& a, int l, int h, int split, int splits, int pos,
+                                                   KV* ks, KV* vs, float* consts_s) {
+    const h4b_model& m = a.m;
+    const h4b_state& st = a.s;
+    const int d = kHeadDim;
+    const int ctx = pos + 1;
+    const int chunk = (ctx + splits - 1) / splits;
+    const int t0 = min(ctx, split * chunk), t1 = min(ctx, t0 + chunk);
+    const float* cs = m.rope_cos + static_cast<long long>(pos) * (d / 2);
+    const float* sn = m.rope_sin + static_cast<long long>(pos) * (d / 2);
+    const size_t kv_layer = static_cast<size_t>(m.kv_heads) * st.capacity * d;
+    const KV* kc = static_cast<const KV*>(st.k_cache) + l * kv_layer + static_cast<size_t>(h) * st.capacity * d;
+    const KV* vc = static_cast<const KV*>(st.v_cache) + l * kv_layer + static_cast<size_t>(h) * st.capacity * d;
+    const bool owns_new = t0 <= pos && pos < t1;
+    if (t0 < t1) stage_subtile<KV>(kc, vc, d, t0, min(kSubTile, t1 - t0), owns_new ? pos : -1, ks, vs, threadIdx.x,
+                                   kMkConsumers);
+#pragma unroll 1
+    for (int i = threadIdx.x; i < 3 * d / 4; i += kMkConsumers) {
+        const float* src = i < d / 4 ? m.norm_q + static_cast<size_t>(l) * d + 4 * i
+                         : i < d / 2 ? m.norm_k + static_cast<size_t>(l) * d + 4 * (i - d / 4)
+                         : i < 5 * d / 8 ? cs + 4 * (i - d / 2)
+                                         : sn + 4 * (i - 5 * d / 8);
+        async_copy16(consts_s + 4 * i, src);
+    }
+}
+
 // One attention split (kv head h, split `split` of `splits`) for layer l,
 // in the order of gqa_split_kernel. The first sub-tile of past K/V rows and
 // the norm/RoPE constants are fetched before the new token's q/k/v are
@@ -616,7 +656,8 @@ __device__ float4 mk_merge_direct(const unsigned long long* base, int splits, lo
 // must stop.
 template <typename KV>
 __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t tbase, int l, int h, int split,
-                             int splits, int pos, KV* ks, KV* vs, float* consts_s, float* red, int* flags) {
+                             int splits, int pos, KV* ks, KV* vs, float* consts_s, float* red, int* flags,
+                             bool prefetched) {
     const h4b_model& m = a.m;
     const h4b_state& st = a.s;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -628,8 +669,6 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
     const int ctx = pos + 1;
     const int chunk = (ctx + splits - 1) / splits;
     const int t0 = min(ctx, split * chunk), t1 = min(ctx, t0 + chunk);
-    const float* cs = m.rope_cos + static_cast<long long>(pos) * (d / 2);
-    const float* sn = m.rope_sin + static_cast<long long>(pos) * (d / 2);
     const size_t kv_layer = static_cast<size_t>(m.kv_heads) * st.capacity * d;
     KV* kc = static_cast<KV*>(st.k_cache) + l * kv_layer + static_cast<size_t>(h) * st.capacity * d;
     KV* vc = static_cast<KV*>(st.v_cache) + l * kv_layer + static_cast<size_t>(h) * st.capacity * d;
@@ -638,18 +677,7 @@ __device__ bool mk_attention(const MkArgs& a, unsigned long long* xw, uint32_t t
     const uint32_t tag_part = tbase + kTagsPerLayer * l + TAG_PART;
     const uint32_t tag_att = tbase + kTagsPerLayer * l + TAG_ATT;
 
-    if (t0 < t1) stage_subtile<KV>(kc, vc, d, t0, min(kSubTile, t1 - t0), owns_new ? pos : -1, ks, vs, threadIdx.x,
-                                   kMkConsumers);
-    // q/k norm weights and this position's RoPE row into consts_s
-    // ([0, d) q gamma, [d, 2d) k gamma, [2d, 2.5d) cos, [2.5d, 3d) sin).
-    #pragma unroll 1
-    for (int i = threadIdx.x; i < 3 * d / 4; i += kMkConsumers) {
-        const float* src = i < d / 4 ? m.norm_q + static_cast<size_t>(l) * d + 4 * i
-                         : i < d / 2 ? m.norm_k + static_cast<size_t>(l) * d + 4 * (i - d / 4)
-                         : i < 5 * d / 8 ? cs + 4 * (i - d / 2)
-                                         : sn + 4 * (i - 5 * d / 8);
-        async_copy16(consts_s + 4 * i, src);
-    }
+    if (!prefetched) mk_attention_fetch<KV>(a, l, h, split, splits, pos, ks, vs, consts_s);
     if (l == 1) H4B_TRACE(1500);
     if (l == 2) H4B_TRACE_CTA(16);
 
@@ -1045,6 +1073,10 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         }
 #endif
         mk_fetch_own(a, g, geo, sc_base, gamma_s);
+        async_copy_commit();  // group: this segment's scales and norm weight
+        if (kind == SEG_QKV && l > 0 && cta < items)  // layer 0: xs still holds the embedding
+            mk_attention_fetch<KV>(a, l, cta / splits, cta % splits, splits, pos, ks, vs, consts_s);
+        async_copy_commit();  // group: attention's first K/V sub-tile (empty elsewhere)
 
         // ---- prologue ----
         float act;
@@ -1083,7 +1115,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
                 ll_store(xw + a.x.qkv + sg.r0 + i, mk_value(acc_s, sc_s, i, act), tl + TAG_QKV);
             if (cta < items &&
                 !mk_attention<KV>(a, xw, tbase, l, cta / splits, cta % splits, splits, pos, ks, vs, consts_s, red,
-                                  flags))
+                                  flags, l > 0))
                 return;
         } else if (kind == SEG_O || kind == SEG_DOWN) {
             const long long dst = kind == SEG_O ? a.x.x_o : a.x.x_down;
