@@ -152,6 +152,7 @@ __device__ __forceinline__ void tile_batch(const uint8_t* tile, int kb, int trow
 // slot loads of the shared-memory activation path read zeros.
 __device__ __forceinline__ void zero_xq_tail(int8_t* xq, int n, int tid, int nthreads) {
     const int end = xq_region(n);
+    #pragma unroll 1
     for (int i = n + 4 * tid; i < end; i += 4 * nthreads) *reinterpret_cast<uint32_t*>(xq + i) = 0u;
 }
 
@@ -177,6 +178,7 @@ __device__ float gemv_prologue(const GemvArgs& a, int8_t* xq, float* red, const 
     const int tid = threadIdx.x;
     const int groups = a.width >> 3;
     if constexpr (PRO == PRO_INT8) {
+        #pragma unroll 2
         for (int g = tid; g < groups; g += kConsumers) {
             const uint2 raw = *reinterpret_cast<const uint2*>(a.x8 + 8 * g);
             int q[8];
@@ -193,6 +195,7 @@ __device__ float gemv_prologue(const GemvArgs& a, int8_t* xq, float* red, const 
         float inv = 1.0f;
         if constexpr (PRO == PRO_RMSNORM) {
             float ss = 0.f;
+            #pragma unroll 2
             for (int g = tid; g < groups; g += kConsumers) {
                 float v[8];
                 load8(a.xin + 8 * g, v);
@@ -208,6 +211,7 @@ __device__ float gemv_prologue(const GemvArgs& a, int8_t* xq, float* red, const 
             m = *a.absmax_in;
         } else {
             float local = 0.f;
+            #pragma unroll 2
             for (int g = tid; g < groups; g += kConsumers) {
                 float v[8], gm[8];
                 load8(a.xin + 8 * g, v);
@@ -293,6 +297,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
         }
         // Row scales are weights too: fetch them asynchronously before any
         // dependency wait, so lane 0 goes straight on to refilling the ring.
+        #pragma unroll 1
         for (int i = lane; i < nrows; i += 32) async_copy4(sc_s + i, a.wscale + r0 + i);
         if (lane == 0) {
             for (int t = a.stages; t < ntiles; ++t) {
@@ -314,6 +319,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
         float* gamma_s = reinterpret_cast<float*>(smem + L.gamma);
         if constexpr (PRO == PRO_RMSNORM) {
             // The norm weight is static: stage it before the dependency wait.
+            #pragma unroll 1
             for (int i = tid; i < (a.width >> 2); i += kConsumers)
                 reinterpret_cast<float4*>(gamma_s)[i] = __ldg(reinterpret_cast<const float4*>(a.gamma) + i);
         }
@@ -378,6 +384,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
         return __fmul_rn(__fmul_rn(static_cast<float>(acc_s[i]), act_scale), sc_s[i]);
     };
     if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
+        #pragma unroll 1
         for (int i = tid; i < nrows; i += kGemvThreads) {
             const float v = value(i);
             if constexpr (EPI == EPI_STORE) {
@@ -390,6 +397,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     } else if constexpr (EPI == EPI_SWIGLU) {
         float local = 0.f;
         const int pairs = nrows >> 1;
+        #pragma unroll 1
         for (int p = tid; p < pairs; p += kGemvThreads) {
             const int b = p / kSwigluBlock, j = p % kSwigluBlock;
             const int gi = 2 * kSwigluBlock * b + j;
@@ -409,6 +417,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
         }
     } else {  // EPI_ARGMAX
         unsigned long long best = 0ull;
+        #pragma unroll 1
         for (int i = tid; i < nrows; i += kGemvThreads) {
             const float v = value(i);
             a.out[r0 + i] = v;
