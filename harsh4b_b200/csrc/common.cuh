@@ -204,8 +204,10 @@ __device__ __forceinline__ unsigned long long ll_load(const unsigned long long* 
 }
 
 // Bounded polling: a poll loop calls poll_expired() between rounds; it
-// backs off briefly and returns true (after reporting) once the wait limit
-// has passed or another wait has already failed.
+// returns true (after reporting) once the wait limit has passed or another
+// wait has already failed. Rounds follow each other without a sleep: a round
+// is already one L2 round trip, and a 96 ns back-off between rounds measured
+// 1 % slower on the persistent decode (later detection of each handoff).
 struct PollClock {
     uint64_t start = 0;
     uint32_t rounds = 0;
@@ -215,7 +217,6 @@ __device__ __forceinline__ bool poll_expired(PollClock& c) {
         c.start = globaltimer_ns();
         return false;
     }
-    __nanosleep(96);
     if ((c.rounds & 255) != 0) return false;
     if (wait_failed_before()) return true;
     if (globaltimer_ns() - c.start > kWaitLimitNs) {
