@@ -19,6 +19,8 @@
 // so the producer keeps loading the next phases' weights while consumers
 // wait on a dependency. Every wait is bounded; a CTA that gives up sets the
 // status word and every other CTA then stops at its next wait.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace h4b {
@@ -1154,6 +1156,18 @@ int mk_splits_max(const h4b_model* m) {
     return std::max(1, std::min(64, sm_count() / m->kv_heads));
 }
 
+// Tuning builds (-DH4B_TUNING) read overrides of the plan's knobs from the
+// environment; the normal build uses the defaults.
+static int tuning_env(const char* name, int fallback) {
+#ifdef H4B_TUNING
+    const char* e = std::getenv(name);  // read per plan: a captured graph keeps its value
+    if (e && *e) return std::max(1, std::atoi(e));
+#else
+    (void)name;
+#endif
+    return fallback;
+}
+
 static int plan_persistent(const h4b_model* m, const h4b_state* s, MkPlan* p) {
     int rc = validate(m, s);
     if (rc) return rc;
@@ -1173,7 +1187,7 @@ static int plan_persistent(const h4b_model* m, const h4b_state* s, MkPlan* p) {
     a.m = *m;
     a.s = *s;
     a.x = x_layout(*m);
-    a.attn_chunk = 32;
+    a.attn_chunk = tuning_env("H4B_ATTN_CHUNK", 32);
     a.max_splits = mk_splits_max(m);
     {
         const int groups = m->heads / m->kv_heads;
