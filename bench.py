@@ -38,7 +38,7 @@ PROMPT = 128
 # persistent decode kernel on a 4-layer Qwen3-4B-shaped model (weights + LM
 # head + KV). Traffic grows in proportion to the bytes streamed, so the ratio
 # scales a launch of the full model. (No capture of the chain-mode GEMV yet.)
-NCU_TRAFFIC_PER_BYTE = {"persistent": 1.0546, "gemv": None}
+NCU_TRAFFIC_PER_BYTE = {"persistent": 1.0550, "gemv": None}
 
 
 def parse_args():
