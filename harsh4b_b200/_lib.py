@@ -57,6 +57,16 @@ class PrefillScratchDesc(ctypes.Structure):
                            "positions", "attn_partials", "attn_counters")]
 
 
+class LatticeProjectionDesc(ctypes.Structure):
+    """Mirror of ``h4b_lattice_projection``."""
+
+    _fields_ = [("rows", _i32), ("width", _i32), ("blocksize", _i32), ("nblocks", _i32),
+                ("maskid", _vp), ("t0", _vp), ("t1c", _vp), ("n_t1", ctypes.c_longlong),
+                ("t1c_bytes", ctypes.c_longlong), ("mu", _vp), ("a0", _vp), ("a1", _vp),
+                ("param_dtype", _i32), ("n_o2", _i32), ("o2_idx", _i32 * 4), ("left", _vp), ("right", _vp),
+                ("dim_l", _i32), ("dim_r", _i32)]
+
+
 class TpGroupDesc(ctypes.Structure):
     """Mirror of ``h4b_tp_group``."""
 
@@ -107,9 +117,12 @@ _SIGNATURES = {
     "h4b_tp_gather_best": [ctypes.POINTER(TpGroupDesc), _vp, _vp, _i32, _vp, _vp],
     "h4b_prefill": [ctypes.POINTER(ModelDesc), ctypes.POINTER(StateDesc), ctypes.POINTER(PrefillScratchDesc), _i32,
                     _vp],
+    "h4b_lattice_scratch_bytes": [_i32],
+    "h4b_lattice_to_int4": [ctypes.POINTER(LatticeProjectionDesc), _vp, _vp, _vp, ctypes.POINTER(_i32), _vp],
+    "h4b_rows_to_int4": [_vp, _i32, _i32, _i32, _vp, _vp, _vp],
 }
 _RESTYPES = {"h4b_persistent_exchange_words": ctypes.c_longlong, "h4b_sample_scratch_bytes": ctypes.c_longlong,
-             "h4b_tp_buffer_bytes": ctypes.c_longlong}
+             "h4b_tp_buffer_bytes": ctypes.c_longlong, "h4b_lattice_scratch_bytes": ctypes.c_longlong}
 
 
 def exported_symbols() -> list[str]:

@@ -469,7 +469,7 @@ __global__ void __launch_bounds__(256) gqa_merge_kernel(const AttnArgs a) {
 
 int launch_attention(const AttnArgs& a, int kv_dtype, int batch, cudaStream_t stream, bool pdl) {
     if (a.groups < 1 || a.groups > kMaxGroups || a.splits < 1 || a.kv_heads < 1 || batch < 1) return H4B_EINVAL;
-    if (!g_prepared) {  // the shared-memory opt-in of gqa_split_kernel<float>
+    {  // the shared-memory opt-in of gqa_split_kernel<float> on this device
         const int rc = prepare_kernels();
         if (rc) return rc;
     }
@@ -533,22 +533,26 @@ namespace h4b {
 constexpr int kNoAllocScratchFloats = 256 * 1024;  // 1 MiB
 static __device__ __align__(256) float g_noalloc_partials[kNoAllocScratchFloats];
 
-constexpr int kMaxDevices = 64;
-static std::once_flag g_noalloc_once[kMaxDevices];
-static float* g_noalloc_ptr[kMaxDevices];
-static cudaError_t g_noalloc_err[kMaxDevices];
+static std::atomic<float*> g_noalloc_ptr[kMaxDevices];
 
+// The device address of the static array on the current device. Looked up
+// with cudaGetSymbolAddress on the first call per device and cached; a failed
+// lookup (e.g. a first call made inside a stream capture) is not cached, so
+// the next call tries again.
 static int noalloc_scratch(float** out) {
     int dev = 0;
     H4B_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kMaxDevices) return H4B_EUNSUPPORTED;
-    std::call_once(g_noalloc_once[dev], [dev] {
-        void* ptr = nullptr;
-        g_noalloc_err[dev] = cudaGetSymbolAddress(&ptr, g_noalloc_partials);
-        g_noalloc_ptr[dev] = static_cast<float*>(ptr);
-    });
-    if (g_noalloc_err[dev] != cudaSuccess) return static_cast<int>(g_noalloc_err[dev]);
-    *out = g_noalloc_ptr[dev];
+    float* ptr = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+    if (!ptr) {
+        void* addr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_partials);
+        if (e != cudaSuccess) return static_cast<int>(e);
+        if (!addr) return H4B_EUNSUPPORTED;
+        ptr = static_cast<float*>(addr);
+        g_noalloc_ptr[dev].store(ptr, std::memory_order_release);
+    }
+    *out = ptr;
     return 0;
 }
 

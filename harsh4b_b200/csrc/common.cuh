@@ -7,6 +7,9 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "../../include/harsh4b_b200.h"
 
 namespace h4b {
@@ -16,6 +19,8 @@ namespace h4b {
 // word; h4b_get_status() reads and clears it from the host. (The library is
 // one translation unit, harsh4b_b200.cu, so this is its only definition.)
 __device__ int g_status = 0;
+
+constexpr int kMaxDevices = 64;  // per-device host-side state is kept for device ordinals below this
 
 constexpr int kStatusWaitTimeout = 1;     // an mbarrier wait ran out of time
 constexpr int kStatusBadToken = 2;        // token id outside the vocabulary

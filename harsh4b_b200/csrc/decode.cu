@@ -347,7 +347,7 @@ static int capture_step(const h4b_model* model, const h4b_state* state, void* st
     if (!graph_out) return H4B_EINVAL;
     int rc = validate(model, state);
     if (rc) return rc;
-    if (!g_prepared && (rc = prepare_kernels())) return rc;
+    if ((rc = prepare_kernels())) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     GraphHandle* h = new (std::nothrow) GraphHandle();
     if (!h) return H4B_EINVAL;

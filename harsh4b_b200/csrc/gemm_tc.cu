@@ -368,12 +368,17 @@ bool tc_gemm_supported(const GemmArgs& g) {
 template <int TOK>
 int launch_tc(const GemmArgs& g, cudaStream_t stream) {
     using C = TcCfg<TOK>;
-    static std::once_flag once;
-    static cudaError_t attr = cudaSuccess;
-    std::call_once(once, [] {
-        attr = cudaFuncSetAttribute(int4_gemm_tc_kernel<TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    });
-    H4B_CUDA_TRY(attr);
+    // The shared-memory opt-in applies to the current device only: set it
+    // once per device, recording only a success.
+    static std::atomic<bool> opted_in[kMaxDevices];
+    int dev = 0;
+    H4B_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return H4B_EUNSUPPORTED;
+    if (!opted_in[dev].load(std::memory_order_acquire)) {
+        H4B_CUDA_TRY(cudaFuncSetAttribute(int4_gemm_tc_kernel<TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          C::kSmem));
+        opted_in[dev].store(true, std::memory_order_release);
+    }
     CUtensorMap wmap, xmap;
     if (!byte_matrix_map(&wmap, g.w, static_cast<uint64_t>(g.K) / 2, g.N, kTcK / 2, kTcRows, false) ||
         !byte_matrix_map(&xmap, g.x, g.K, g.M, kTcK, TOK, true))

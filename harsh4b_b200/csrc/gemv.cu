@@ -448,16 +448,32 @@ struct GemvPlan {
     int grid, slots, tile_rows, stages, rows_cap, smem;
 };
 
-static int g_sm_count = 0;
+// Per-device state: the SM count and whether this device's kernels have
+// their shared-memory opt-ins. cudaFuncSetAttribute applies to the current
+// device only, so a process that drives several GPUs prepares each one.
+// Only successes are recorded; a failed preparation is retried next call.
+struct DeviceSetup {
+    std::atomic<int> sms{0};
+    std::atomic<bool> prepared{false};
+};
+static DeviceSetup g_devices[kMaxDevices];
+static std::mutex g_prepare_mutex;
+
+static int current_device() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+    return dev;
+}
 
 int sm_count() {
-    if (g_sm_count == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
-        if (g_sm_count <= 0) g_sm_count = 148;
+    const int dev = current_device();
+    if (dev < 0) return 148;
+    int n = g_devices[dev].sms.load(std::memory_order_relaxed);
+    if (n == 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        g_devices[dev].sms.store(n, std::memory_order_relaxed);
     }
-    return g_sm_count;
+    return n;
 }
 
 // Slot counts that have kernel instantiations (a lane covers `slots` 16-byte
@@ -527,13 +543,18 @@ static int set_smem_limits() {
     return 0;
 }
 
-static bool g_prepared = false;
 int prepare_other_kernels();  // attention and the small kernels (defined after them)
 
-// Raises every GEMV instantiation's dynamic shared-memory limit. Runs once,
-// outside any stream capture.
+// Raises every kernel's dynamic shared-memory limit on the current device.
+// Runs once per device (outside any stream capture: the first launch of each
+// kind on a device should not be captured); later calls cost one
+// cudaGetDevice and an atomic load.
 int prepare_kernels() {
-    if (g_prepared) return 0;
+    const int dev = current_device();
+    if (dev < 0) return H4B_EUNSUPPORTED;
+    if (g_devices[dev].prepared.load(std::memory_order_acquire)) return 0;
+    std::lock_guard<std::mutex> lock(g_prepare_mutex);
+    if (g_devices[dev].prepared.load(std::memory_order_relaxed)) return 0;
     int r = 0;
     if ((r = set_smem_limits<PRO_INT8, EPI_STORE>()) || (r = set_smem_limits<PRO_QUANT, EPI_STORE>()) ||
         (r = set_smem_limits<PRO_RMSNORM, EPI_STORE>()) || (r = set_smem_limits<PRO_QUANT_ABSMAX, EPI_RESIDUAL>()) ||
@@ -542,7 +563,7 @@ int prepare_kernels() {
         return r;
     if ((r = prepare_other_kernels())) return r;
     sm_count();
-    g_prepared = true;
+    g_devices[dev].prepared.store(true, std::memory_order_release);
     return 0;
 }
 
@@ -581,7 +602,7 @@ static int launch_slots(const GemvArgs& a, const GemvPlan& p, cudaStream_t s, bo
 
 // The (prologue, epilogue) pairs the decode path and the C ABI use.
 int launch_gemv(int pro, int epi, GemvArgs a, cudaStream_t stream, bool pdl) {
-    if (!g_prepared) {
+    {
         const int prc = prepare_kernels();
         if (prc) return prc;
     }

@@ -10,3 +10,4 @@
 #include "batch.cu"
 #include "prefill.cu"
 #include "tp.cu"
+#include "lattice.cu"

@@ -6,14 +6,18 @@
 //
 //   * the producer warp of each CTA walks that SM's rows of every weight
 //     matrix of the token in phase order (per layer qkv, o, gate/up, down;
-//     then the LM head) and streams them through one shared-memory ring of
-//     8 KB slots with 1-D bulk copies, waiting only for free slots;
-//   * the eight consumer warps run the phases: wait for the phase's input
-//     (a release/acquire counter that every producing CTA bumps once),
-//     quantise the input (prologue), consume this phase's ring tiles, write
-//     the outputs (epilogue) and bump the phase counter;
-//   * attention runs on the first kv_heads * S CTAs (S chosen per token from
-//     the context length); the last CTA of each kv head merges the splits.
+//     then the LM head) and streams them through a 14-slot shared-memory
+//     ring (slots of up to 16 KB) with 1-D bulk copies, waiting only for
+//     free slots;
+//   * seven consumer warps run the phases: poll the phase's input, quantise
+//     it (prologue), consume this phase's ring tiles (each slot is owned by
+//     one warp), write the outputs (epilogue);
+//   * every value one CTA hands to another is a tagged 64-bit exchange word
+//     {tag, fp32}; readers poll the words themselves until the tag of this
+//     launch and handoff appears (no flags, no fences, no clearing);
+//   * attention runs on the first kv_heads * S CTAs (S splits per kv head,
+//     chosen per token from the context length); split 0 of each kv head
+//     merges the splits in split order.
 //
 // The ring covers a few microseconds of this SM's share of HBM bandwidth,
 // so the producer keeps loading the next phases' weights while consumers
@@ -89,6 +93,7 @@ struct MkArgs {
     int max_splits;        // splits per kv head at most
     int stage_splits;      // splits whose partials fit the K/V staging area
     int xq_bytes, rows_cap;
+    int inflight;          // bulk copies the producer keeps in flight at most
 };
 
 struct Seg {
@@ -1010,6 +1015,18 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
                             break;
                         }
                     }
+                    if (seq >= static_cast<uint32_t>(a.inflight)) {
+                        // At most `inflight` copies outstanding: wait until the
+                        // copy `inflight` tiles back has landed. Its full
+                        // barrier stays in that completed phase until this
+                        // warp re-arms the slot, `stages` tiles later.
+                        const uint32_t back = seq - a.inflight;
+                        if (!mbar_wait(&full[back % a.stages], (back / a.stages) & 1)) {
+                            atomicOr(&flags[0], 1);
+                            stop = true;
+                            break;
+                        }
+                    }
                     const int rows_t = min(sg.tile_rows, sg.nrows - t * sg.tile_rows);
                     const uint32_t bytes = static_cast<uint32_t>(rows_t) * sg.kb;
                     if (seq >= 40 && seq < 140) H4B_TRACE_ANY(1400 + seq - 40);
@@ -1203,6 +1220,7 @@ static int plan_persistent(const h4b_model* m, const h4b_state* s, MkPlan* p) {
     const MkSmem base = mk_smem_layout(a.xq_bytes, m->hidden, a.rows_cap, kv_bytes, 0, 0);
     const int budget = 227 * 1024 - base.total;
     a.stages = kMkStages;
+    a.inflight = std::min(a.stages, tuning_env("H4B_INFLIGHT", a.stages));
     a.slot_bytes = std::min(kMkMaxSlotBytes, budget / kMkStages / 1024 * 1024);
     if (a.slot_bytes < max_width / 2) return H4B_EUNSUPPORTED;  // one row must fit a slot
     p->smem = mk_smem_layout(a.xq_bytes, m->hidden, a.rows_cap, kv_bytes, a.stages, a.slot_bytes).total;
@@ -1218,7 +1236,7 @@ int prepare_persistent() {
 }
 
 int decode_persistent(const h4b_model* m, const h4b_state* s, cudaStream_t stream) {
-    if (!g_prepared) {
+    {
         const int prc = prepare_kernels();
         if (prc) return prc;
     }

@@ -1,123 +1,106 @@
-"""Runtime entry for the B200 backend: the ``Runtime`` contract of the
-reference's chat server (inference_runtime.py:71-122) and a ``CudaRuntime``
-that serves it from :class:`harsh4b_b200.model.CudaQwen`.
+"""The B200 backend of the reference chat server's runtime contract.
 
-The reference picks its backend in ``create_runtime`` (inference_runtime.py:
-349-356); ``select_runtime`` already answers "cuda" when torch sees a GPU
-(:16-32). A maintainer routes "cuda" to :class:`CudaRuntime` (see
-INTEGRATION.md). Methods keep the reference's names and meaning:
+The reference defines ``Runtime`` (inference_runtime.py:71-122: ``status``,
+``stream`` and the context budget) and one subclass per backend that
+supplies ``prefill``, ``decode``, ``sample``, ``memory_gib`` and the
+attributes ``device``, ``hardware``, ``description``, ``tokenizer`` (and
+``torch``, read by benchmarks/bench_energy.py:269-273). This module ships
+only that backend half, :class:`CudaBackend`; the reference side composes it
+with its own base class::
+
+    from harsh4b_b200.runtime import CudaBackend
+
+    class CudaRuntime(CudaBackend, Runtime):
+        pass
+
+and ``create_runtime`` (inference_runtime.py:349-356) picks ``CudaRuntime``
+for ``"cuda"``, as ``select_runtime`` (:16-32) already answers ``"cuda"``
+when torch sees a GPU. ``stream()`` is the reference's, unchanged.
+
+Methods keep the reference's names and meaning:
 
 * ``prefill(ids, max_tokens) -> (logits, session)``: a fresh decode state
   sized for the prompt plus the output, the prompt fed in one pass through
   the batched GEMMs (the reference's CPU runtime loops over the tokens,
-  :124-128; the resulting state and logits are the same);
+  inference_runtime.py:177-181; the resulting state and logits are the same);
 * ``decode(token, session) -> logits``;
 * ``sample(logits, generated, temperature) -> int``: sample_numpy's policy
-  (:144-163; top-p 0.9, top-k 50, repetition penalty 1.15) on the device,
-  with the draw taken from this runtime's numpy generator;
-* ``memory_gib()``, ``status()``, ``stream(...)`` and the attributes
-  ``device``, ``hardware``, ``description``, ``tokenizer``, ``torch``.
+  (inference_runtime.py:144-163; top-p 0.9, top-k 50, repetition penalty
+  1.15) on the device, the draw taken from this runtime's numpy generator;
+* ``memory_gib()``.
+
+``create_runtime(model_path, ...)`` hands the backend the LATTICE checkpoint
+path (``checkpoint_path``, inference_runtime.py:35-43); a directory holding a
+packed cache (``manifest.json``) with its norms is accepted as well.
 """
 from __future__ import annotations
 
-import time
 from pathlib import Path
 
 import numpy as np
 
-MODEL_ID = "Qwen/Qwen3-4B"
+
+def load_model(path, *, kv_dtype: str = "float16", mode: str = "persistent", cache_dir=None, verbose: bool = False):
+    """A :class:`CudaQwen` from a LATTICE checkpoint file (converted on the
+    GPU into the shared packed cache) or from a self-contained cache
+    directory."""
+    from .model import CudaQwen
+
+    path = Path(path)
+    if path.is_dir():
+        return CudaQwen.from_cache(path, kv_dtype=kv_dtype, mode=mode)
+    from .lattice import build_b200_model
+
+    return build_b200_model(path, cache_dir=cache_dir, verbose=verbose, kv_dtype=kv_dtype, mode=mode)
 
 
-class Runtime:
-    """Backend-independent part of a runtime (inference_runtime.py:71-122)."""
+class CudaBackend:
+    """prefill / decode / sample / memory_gib of the reference's runtime
+    contract on the B200 decode path (combine with the reference's
+    ``Runtime`` for ``status`` and ``stream``).
 
-    max_context = 2048
-
-    def status(self) -> dict:
-        return dict(model=MODEL_ID, device=self.device, runtime=self.device, hardware=self.hardware,
-                    quant=self.description, ready=True, vram_gb=round(self.memory_gib(), 2),
-                    max_context=self.max_context)
-
-    def memory_gib(self) -> float:
-        return 0.0
-
-    def stream(self, prompt_ids, max_tokens, temperature, stopped=lambda: False):
-        """One fresh session per request; no forward pass after the last token.
-        Yields {"token": text, "done": False} per decoded piece, then
-        {"done": True, "stats": {...}} (the reference's stream contract)."""
-        from tokenizers.decoders import DecodeStream
-
-        if not prompt_ids or len(prompt_ids) + max_tokens > self.max_context:
-            raise ValueError("Prompt and output exceed the runtime context budget")
-        generated: list[int] = []
-        decoder = DecodeStream(skip_special_tokens=True)
-        prefill_seconds = decode_seconds = 0.0
-        decode_steps = 0
-        if not stopped():
-            t0 = time.perf_counter()
-            logits, session = self.prefill(prompt_ids, max_tokens)
-            token = self.sample(logits, generated, temperature)
-            prefill_seconds = time.perf_counter() - t0
-            while not stopped() and token not in self.tokenizer.stop_ids:
-                generated.append(token)
-                text = decoder.step(self.tokenizer.backend, token)
-                if text:
-                    yield {"token": text, "done": False}
-                if len(generated) >= max_tokens or stopped():
-                    break
-                t0 = time.perf_counter()
-                logits = self.decode(token, session)
-                token = self.sample(logits, generated, temperature)
-                decode_seconds += time.perf_counter() - t0
-                decode_steps += 1
-        yield {"done": True, "stats": {
-            "tokens": len(generated), "time": round(prefill_seconds + decode_seconds, 3),
-            "prefill_time": round(prefill_seconds, 3), "decode_time": round(decode_seconds, 3),
-            "decode_steps": decode_steps,
-            "tok_per_sec": round(decode_steps / decode_seconds, 2) if decode_seconds else 0.0,
-            "vram_gb": round(self.memory_gib(), 2), "runtime": self.device,
-        }}
-
-
-class CudaRuntime(Runtime):
-    """The reference's runtime contract on the B200 decode path."""
+    ``model`` and ``sampler`` let a caller hand in its own model object
+    (``new_state`` / ``prefill`` / ``forward_token``) or sampling policy
+    ``sampler(logits, generated, temperature) -> int``; without them the
+    backend builds the CUDA model from ``path`` and samples on the device,
+    and raises when no GPU is visible (there is no CPU fallback)."""
 
     device = "cuda"
 
-    def __init__(self, path=None, tokenizer=None, *, model=None, kv_dtype: str = "float16", mode: str = "persistent",
-                 seed: int | None = None, top_p: float = 0.9, top_k: int = 50, repetition_penalty: float = 1.15,
-                 **_):
+    def __init__(self, path=None, tokenizer=None, *, model=None, sampler=None, kv_dtype: str = "float16",
+                 mode: str = "persistent", seed: int | None = None, top_p: float = 0.9, top_k: int = 50,
+                 repetition_penalty: float = 1.15, cache_dir=None, verbose: bool = False, **_):
         import torch
 
-        from .model import CudaQwen
-
-        if not torch.cuda.is_available():
-            raise RuntimeError("CUDA is unavailable; harsh4b_b200 has no CPU fallback")
-        self.torch, self.tokenizer = torch, tokenizer
         if model is None:
+            if not torch.cuda.is_available():
+                raise RuntimeError("CUDA is unavailable; harsh4b_b200 has no CPU fallback")
             if path is None:
-                raise ValueError("CudaRuntime needs a LiteSpark cache directory or a CudaQwen model")
-            model = CudaQwen.from_cache(Path(path), kv_dtype=kv_dtype, mode=mode)
-        self.model = model
-        self.hardware = torch.cuda.get_device_name(model.device)
-        self.description = f"CUDA · B200 packed int4 ({getattr(model, 'mode', mode)} decode, {model.kv_dtype} KV)"
+                raise ValueError("CudaBackend needs a LATTICE checkpoint, a packed cache directory or a model")
+            model = load_model(path, kv_dtype=kv_dtype, mode=mode, cache_dir=cache_dir, verbose=verbose)
+        self.torch, self.tokenizer, self.model = torch, tokenizer, model
+        on_gpu = torch.device(getattr(model, "device", "cpu")).type == "cuda"
+        self.hardware = torch.cuda.get_device_name(model.device) if on_gpu else str(getattr(model, "device", "cpu"))
+        self.description = (f"CUDA · B200 packed int4 ({getattr(model, 'mode', mode)} decode, "
+                            f"{getattr(model, 'kv_dtype', kv_dtype)} KV)")
         self.top_p, self.top_k, self.repetition_penalty = float(top_p), int(top_k), float(repetition_penalty)
         self.generator = np.random.default_rng(seed)
-        self._work = torch.empty(model.vocab, dtype=torch.float32, device=model.device)
-        self._token = torch.empty(1, dtype=torch.int32, device=model.device)
-        self._seen = torch.empty(self.max_context, dtype=torch.int32, device=model.device)
-        from ._lib import lib
+        self._sampler = sampler
+        if sampler is None:
+            from ._lib import lib
 
-        nbytes = int(lib().h4b_sample_scratch_bytes(model.vocab, self.top_k))
-        if nbytes < 0:
-            raise ValueError(f"top_k {self.top_k} is not supported by the device sampler")
-        self._scratch = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=model.device)
+            self._work = torch.empty(model.vocab, dtype=torch.float32, device=model.device)
+            self._token = torch.empty(1, dtype=torch.int32, device=model.device)
+            self._seen = torch.empty(2048, dtype=torch.int32, device=model.device)
+            nbytes = int(lib().h4b_sample_scratch_bytes(model.vocab, self.top_k))
+            if nbytes < 0:
+                raise ValueError(f"top_k {self.top_k} is not supported by the device sampler")
+            self._scratch = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=model.device)
 
     def prefill(self, ids, max_tokens):
-        """A fresh session with the prompt fed in one CudaQwen.prefill pass (the
-        reference's CPU runtime feeds it token by token, :124-128; the state
-        ends the same, with the prompt's attention split count fixed per
-        session)."""
+        """A fresh session with the prompt fed in one CudaQwen.prefill pass
+        (the state ends as after feeding the prompt token by token, with the
+        prompt's attention split count fixed per session)."""
         state = self.model.new_state(len(ids) + max_tokens)
         logits = self.model.prefill([int(t) for t in ids], state)
         return logits, state
@@ -127,6 +110,8 @@ class CudaRuntime(Runtime):
 
     def sample(self, logits, generated, temperature):
         """sample_numpy's policy on the device; the logits are not modified."""
+        if self._sampler is not None:
+            return int(self._sampler(logits, generated, temperature))
         from . import ops
 
         torch = self.torch
@@ -148,25 +133,6 @@ class CudaRuntime(Runtime):
             return int(self._token.item())
 
     def memory_gib(self) -> float:
+        if self.torch.device(getattr(self.model, "device", "cpu")).type != "cuda":
+            return 0.0
         return self.torch.cuda.memory_allocated(self.model.device) / 2**30
-
-
-def select_runtime(requested: str = "auto") -> str:
-    """inference_runtime.select_runtime restricted to this backend: "cuda"
-    when a GPU is visible (raises otherwise -- there is no CPU path here)."""
-    if requested not in ("auto", "cuda"):
-        raise ValueError(f"harsh4b_b200 serves only the cuda runtime, not {requested!r}")
-    import torch
-
-    if not torch.cuda.is_available():
-        raise RuntimeError("CUDA is unavailable; harsh4b_b200 has no CPU fallback")
-    return "cuda"
-
-
-def create_runtime(name: str = "auto", model_path=None, tokenizer=None, **options) -> CudaRuntime:
-    """create_runtime (inference_runtime.py:349-356) for the cuda runtime:
-    `model_path` is a LiteSpark cache directory (build_litespark_cpu layout),
-    `tokenizer` an object with `.stop_ids` and `.backend` (the reference's
-    ChatTokenizer)."""
-    select_runtime(name)
-    return CudaRuntime(model_path, tokenizer, **options)

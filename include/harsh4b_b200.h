@@ -363,6 +363,51 @@ typedef struct h4b_prefill_scratch {
 int h4b_prefill(const h4b_model *model, const h4b_state *state, const h4b_prefill_scratch *scratch, int count,
                 void *stream);
 
+/* ---- format producer: LATTICE checkpoint -> packed int4 cache ------------- */
+
+/* One LATTICE projection as stored in the checkpoint (all pointers are
+ * device pointers; the reference reads the same fields in
+ * cpu_lightspark._convert_projection, cpu_lightspark.py:149-201):
+ * maskid / t0: uint8[rows][ceil(width/4)], four 2-bit codes per byte (code j
+ * of a row in bits 2(j%4)..2(j%4)+1 of byte j/4); t1c: the compact T1 codes
+ * of every column whose mode id is 0 or 1, row-major over the whole matrix,
+ * n_t1 codes in t1c_bytes bytes (MLX/lattice_model.py:160-185 expands them);
+ * mu, a0: [4][rows][nblocks], a1: [n_o2][rows][nblocks], float32
+ * (param_dtype 0) or float16 (param_dtype 1); o2_idx: the mode id each a1
+ * plane applies to; left: float32[dim_l][dim_l], right: float32[dim_r][dim_r]
+ * with dim_l * dim_r == width. */
+typedef struct h4b_lattice_projection {
+    int rows, width, blocksize, nblocks;
+    const uint8_t *maskid, *t0, *t1c;
+    long long n_t1, t1c_bytes;
+    const void *mu, *a0, *a1;
+    int param_dtype, n_o2;
+    int o2_idx[4];
+    const float *left, *right;
+    int dim_l, dim_r;
+} h4b_lattice_projection;
+
+/* Bytes of caller scratch h4b_lattice_to_int4 needs for `rows` rows. */
+long long h4b_lattice_scratch_bytes(int rows);
+
+/* Replaces cpu_lightspark._convert_projection (cpu_lightspark.py:149-201)
+ * with expand_t1 (MLX/lattice_model.py:160-185): reconstructs the fp32
+ * weights, absorbs the rotation (W_r -> left^T W_r right^T per row, fp64
+ * accumulation rounded once to fp32), and writes the row-int4 cache form:
+ * packed uint8[rows][width/2] and float32 scales[rows] with
+ * scale = max(max|w|, 1e-8) / 7 and codes clip(rint(w / scale), -7, 7).
+ * Checks, as expand_t1 does, that the mode ids select exactly n_t1 codes
+ * (*host_error = 1 and H4B_EINVAL otherwise). Synchronises `stream`. */
+int h4b_lattice_to_int4(const h4b_lattice_projection *projection, uint8_t *packed, float *scales,
+                        void *scratch, int *host_error, void *stream);
+
+/* Replaces cpu_lightspark._convert_embedding (cpu_lightspark.py:204-229):
+ * per-row symmetric int4 of a dense matrix source[rows][width] (float32 when
+ * source_dtype is 0, float16 when 1), same scale and code rule as above;
+ * bit-exact with the reference. */
+int h4b_rows_to_int4(const void *source, int source_dtype, int rows, int width, uint8_t *packed,
+                     float *scales, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

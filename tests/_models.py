@@ -54,3 +54,49 @@ def cuda_decode(model, prompt, steps, teacher=None, attn_splits=None):
 def top2_margin(logits):
     part = np.partition(logits, -2, axis=-1)
     return part[..., -1] - part[..., -2]
+
+
+def write_lattice_checkpoint(path, config, seed=0, blocksize=64):
+    """A seeded LATTICE checkpoint file (torch.save of the reference's state
+    layout) for `config`: per projection the packed fields plus an
+    orthogonal rotation pair, the fp32 embedding and fp32 norms. Returns the
+    state dict as numpy arrays."""
+    import torch
+
+    from harsh4b_b200.cache import norm_names, projection_names
+    from oracle.lattice import orthogonal, synthetic_projection
+
+    rng = np.random.default_rng([seed, 0x1A771CE])
+    hidden, inter = int(config["hidden_size"]), int(config["intermediate_size"])
+    q = int(config["num_attention_heads"]) * int(config["head_dim"])
+    kv = int(config["num_key_value_heads"]) * int(config["head_dim"])
+    shapes = {"q_proj": (q, hidden), "k_proj": (kv, hidden), "v_proj": (kv, hidden), "o_proj": (hidden, q),
+              "gate_proj": (inter, hidden), "up_proj": (inter, hidden), "down_proj": (hidden, inter)}
+
+    def factors(width):
+        dl = int(np.sqrt(width))
+        while width % dl:
+            dl -= 1
+        return dl, width // dl
+
+    state, plain = {}, {}
+    names = projection_names(config)
+    for name in names:
+        rows, width = shapes[name.rsplit(".", 1)[1]]
+        packed = synthetic_projection(rng, rows, width, blocksize)
+        dl, dr = factors(width)
+        left, right = orthogonal(rng, dl), orthogonal(rng, dr)
+        plain[name] = (packed, left, right)
+        state[name + ".weight"] = {k: (torch.from_numpy(np.ascontiguousarray(v)) if isinstance(v, np.ndarray) else v)
+                                   for k, v in packed.items()}
+        state[name + ".L"], state[name + ".R"] = torch.from_numpy(left), torch.from_numpy(right)
+    embedding = (rng.standard_normal((int(config["vocab_size"]), hidden)) * 0.05).astype(np.float32)
+    state["model.embed_tokens.weight"] = torch.from_numpy(embedding)
+    norms = {}
+    for name in norm_names(config):
+        size = int(config["head_dim"]) if ("q_norm" in name or "k_norm" in name) else hidden
+        norms[name] = (1.0 + 0.02 * rng.standard_normal(size)).astype(np.float32)
+        state[name] = torch.from_numpy(norms[name])
+    state["__latmeta__"] = {"n_linears": len(names), "encoding": "synthetic"}
+    torch.save(state, str(path))
+    return plain, embedding, norms

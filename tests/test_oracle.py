@@ -195,3 +195,34 @@ def test_sample_runtime_matches_reference_golden():
         token = sample_runtime(data["logits"][i], generated, float(data["uniform"][i]), temperature=temperature,
                                top_p=top_p, top_k=int(top_k), repetition_penalty=penalty)
         assert token == int(data["tokens"][i]), i
+
+
+def test_oracle_matches_reference_at_qwen_shapes():
+    """The oracle (device-ordered reductions, its own exp) against the
+    reference's numpy forward_token at Qwen3-4B's shapes
+    (tests/golden/qwen_shape_decode.npz), fp32 KV as the reference keeps it:
+    the same greedy token at every step, and logits no further from the
+    numpy path than the reference's own native-kernel attention path is
+    (one int8 code flipped by a last-ulp attention difference moves every
+    later logit by a few 1e-2)."""
+    import json
+
+    from _models import oracle_model
+    from harsh4b_b200.synthetic import synthetic_checkpoint
+
+    golden = np.load(Path(__file__).resolve().parent / "golden" / "qwen_shape_decode.npz")
+    checkpoint = synthetic_checkpoint(json.loads(str(golden["config"])), seed=int(golden["seed"]))
+    model = oracle_model(checkpoint, kv_dtype=np.float32)
+    prompt, tokens = golden["prompt"], golden["tokens"]
+    state = model.new_state(len(prompt) + len(tokens))
+    for token in prompt[:-1]:
+        model.forward_token(int(token), state)
+    worst = 0.0
+    for step, token in enumerate([int(prompt[-1])] + [int(t) for t in tokens]):
+        row = model.forward_token(token, state)
+        got = np.concatenate([row[golden["sample_ids"]], row[golden["top_ids"][step]]])
+        want = np.concatenate([golden["sample_logits"][step], golden["top_logits"][step]])
+        worst = max(worst, float(np.abs(got - want).max()))
+        if step < len(tokens):
+            assert int(np.argmax(row)) == int(tokens[step])
+    assert worst <= max(1e-2, float(golden["reference_path_drift"])), worst

@@ -5,7 +5,9 @@ attention (a serving process whose own pool already holds nearly all HBM, or
 a plugin whose host owns the device allocator). Called through the C ABI,
 it must agree with h4b_gqa_decode -- the entry point that takes caller
 scratch -- within the attention tolerance of the other tests, on two calls in
-a row that share the library's static scratch array.
+a row that share the library's static scratch array. Both are also checked
+against the CPU oracle's restatement of litespark_gqa_decode, so a fault the
+two device entry points share does not pass unseen.
 """
 import ctypes
 
@@ -15,6 +17,7 @@ import pytest
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
+import oracle  # noqa: E402
 from harsh4b_b200 import _lib  # noqa: E402
 
 TOL = 2e-5  # the attention tolerance of tests/test_gpu_ops.py
@@ -54,6 +57,13 @@ def test_no_alloc_attention_matches_scratch_entry_point_twice():
         want = _with_scratch(lib, q, keys, values, context, kv_heads, groups).cpu().numpy()
         got = _no_alloc(lib, q, keys, values, context, kv_heads, groups).cpu().numpy()
         np.testing.assert_allclose(got, want, rtol=TOL, atol=TOL)
+        capacity = keys.shape[0]
+        cpu = np.empty((kv_heads * groups, 128), dtype=np.float32)
+        scores = np.empty(kv_heads * groups * capacity, dtype=np.float32)
+        oracle.gqa_decode(q.cpu().numpy(), keys.cpu().numpy(), values.cpu().numpy(), scores, cpu, context,
+                          kv_heads, groups, 128, capacity)
+        np.testing.assert_allclose(got, cpu, rtol=TOL, atol=TOL)
+        np.testing.assert_allclose(want, cpu, rtol=TOL, atol=TOL)
     assert _lib.device_status() == 0
 
 
