@@ -339,6 +339,7 @@ def run_ours(args, rank, world, local_rank, dist) -> int:
     if dist is not None:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     elapsed, e2e_elapsed = float(times[0]), float(times[1])
+    tp_record = tp_subrecord(args, checkpoint, rank, world, local_rank, dist) if world > 1 else None
     if rank != 0:
         return 0
     value = world * args.steps / elapsed
@@ -377,10 +378,130 @@ def run_ours(args, rank, world, local_rank, dist) -> int:
         "device_status": status,
         "last_token": last_token,
     }
+    if tp_record is not None:
+        line["tp"] = tp_record
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(checkpoint, prompt)
     print(json.dumps(line), flush=True)
     return 0
+
+
+def tp_subrecord(args, checkpoint, rank, world, local_rank, dist, context: int = 4096,
+                 steps: int = 20, warmup: int = 3) -> dict:
+    """Config 4 on the same N GPUs, reported beside the replica line:
+    tensor-parallel batch-1 decode (tp = N) from a context of `context`
+    positions (K/V filled with N(0,1) values), the token captured in one
+    CUDA graph with the one-shot P2P exchanges. p50 latency per token (wall
+    and device), the communication alone (the token's collectives issued
+    without the kernels; this path does not overlap them, so it is exposed),
+    and whether 8 greedy tokens after a real 16-token prompt equal those of
+    the single-GPU decode with the same attention splits (the chain kernels,
+    16 splits), which the sharding must reproduce bit for bit."""
+    import numpy as np
+    import torch
+
+    from harsh4b_b200.model import CudaQwen
+    from harsh4b_b200.synthetic import synthetic_prompt
+    from harsh4b_b200.tp import TensorParallelQwen
+
+    device = torch.device("cuda", local_rank)
+    prompt = synthetic_prompt(checkpoint.config, 16, seed=args.seed)  # the same on every rank
+    tp = TensorParallelQwen(checkpoint, kv_dtype=args.kv_dtype, device=device)
+    # greedy tokens after a real prompt, against one GPU
+    check_state = tp.new_state(32)
+    token = None
+    for t in prompt[:16]:
+        token, _ = tp.forward_token(int(t), check_state, graph=False)
+    tp_tokens = [token]
+    for _ in range(7):
+        token, _ = tp.forward_token(token, check_state, graph=False)
+        tp_tokens.append(token)
+    match = None
+    if rank == 0:
+        single = CudaQwen.from_checkpoint(checkpoint, kv_dtype=args.kv_dtype, device=device, mode="chain",
+                                          attn_splits=16)
+        st = single.new_state(32)
+        for t in prompt[:16]:
+            single.forward_token(int(t), st)
+        one = [st.next_token_host()]
+        for _ in range(7):
+            single.forward_token(one[-1], st)
+            one.append(st.next_token_host())
+        match = one == tp_tokens
+        st.close()
+        del single
+    # latency from a long context
+    state = tp.new_state(context + warmup + steps + 1)
+    g = torch.Generator(device=device).manual_seed(args.seed + rank)
+    state.k_cache.normal_(generator=g)
+    state.v_cache.normal_(generator=g)
+    state.position_dev.fill_(context)
+    state.position = context
+    token = int(np.random.default_rng(args.seed).integers(0, tp.vocab))
+    for _ in range(warmup):
+        token, _ = tp.forward_token(token, state, graph=True)
+    walls, device_ms = [], []
+    dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize()
+    for _ in range(steps):
+        start, end = _event_pair(torch)
+        t0 = time.perf_counter()
+        start.record()
+        token, _ = tp.forward_token(token, state, graph=True)
+        end.record()
+        torch.cuda.synchronize()
+        walls.append(time.perf_counter() - t0)
+        device_ms.append(start.elapsed_time(end))
+    tp.release_graphs()
+    # config 4's prefill on the same ranks: a 2048-token prompt, sharded GEMMs
+    # with the [M] absmax and [M][H] int32 all-reduces between them
+    prefill_ids = [int(t) for t in np.random.default_rng([args.seed, 2048]).integers(0, tp.vocab, 2048)]
+    pre_state = tp.new_state(2048 + 1)
+    tp.prefill(prefill_ids, pre_state)  # warm-up (scratch, communicators)
+    pre_state.close()
+    pre_state = tp.new_state(2048 + 1)
+    dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize()
+    p_start, p_end = _event_pair(torch)
+    p_start.record()
+    tp.prefill(prefill_ids, pre_state)
+    p_end.record()
+    torch.cuda.synchronize()
+    prefill_ms = p_start.elapsed_time(p_end)
+    pre_state.close()
+    tp.model._prefill_scratch = None
+    H, L = tp.model.hidden, tp.model.n_layers
+    amax = torch.zeros(1, device=device)
+    acc = torch.zeros(H, dtype=torch.int32, device=device)
+    pairs = [torch.zeros(2, dtype=torch.float64, device=device) for _ in range(world)]
+
+    def comm_token():
+        for _ in range(2 * L):
+            dist.all_reduce(amax, op=dist.ReduceOp.MAX)
+            dist.all_reduce(acc, op=dist.ReduceOp.SUM)
+        dist.all_gather(pairs, pairs[rank].clone())
+
+    comm_token()
+    torch.cuda.synchronize()
+    c_start, c_end = _event_pair(torch)
+    c_start.record()
+    for _ in range(5):
+        comm_token()
+    c_end.record()
+    torch.cuda.synchronize()
+    stats = torch.tensor([statistics.median(walls) * 1000, statistics.median(device_ms),
+                          c_start.elapsed_time(c_end) / 5, prefill_ms], dtype=torch.float64, device=device)
+    dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    status = tp.model.status()
+    tp.close()
+    p50, dev, comm, pre = (round(float(v), 4) for v in stats.cpu())
+    return {"parallelism": f"tp{world}", "context": context, "p50_ms": p50, "device_ms_p50": dev,
+            "exposed_comm_ms": comm, "tok_s": round(1000.0 / p50, 2), "steps": steps,
+            "exchange": "one-shot P2P kernels over NVLink peer memory, token in one CUDA graph",
+            "greedy_match_single_gpu": match,
+            "prefill_2048": {"ms": pre, "tok_s": round(2048 / pre * 1000, 1),
+                             "exchange": "NCCL all-reduce of [M] absmax (MAX) and [M][H] int32 sums (SUM)"},
+            "device_status": status}
 
 
 GEMV_SHAPES = {"q": (4096, 2560), "k": (1024, 2560), "v": (1024, 2560), "o": (2560, 4096),
@@ -465,15 +586,24 @@ def _event_pair(torch):
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
-def run_batch(args) -> int:
+def run_batch(args, rank=0, world=1, local_rank=0, dist=None) -> int:
     """Config 3: batched greedy decode of B sequences (default 64) after a
     prompt of --prompt-len random ids each, body projections on the tcgen05
     GEMM. `value` = B x K tokens over K device-fed steps (generate_batch);
     `e2e` = the same K steps through forward_batch with the B token ids
     copied in and the B greedy ids read back every step. The prompts are fed
-    through forward_batch before timing (not timed)."""
+    through forward_batch before timing (not timed). Under torchrun every
+    rank runs its own batch of B sequences (data-parallel replicas, no
+    collective on the data path); `value` sums the ranks' tokens over the
+    max-over-ranks time."""
     import numpy as np
     import torch
+
+    torch.cuda.set_device(local_rank)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
 
     from harsh4b_b200.model import CudaQwen
     from harsh4b_b200.synthetic import qwen3_4b_config, synthetic_checkpoint
@@ -483,7 +613,7 @@ def run_batch(args) -> int:
     config = qwen3_4b_config(**({"num_hidden_layers": args.layers} if args.layers else {}))
     model = CudaQwen.from_checkpoint(synthetic_checkpoint(config, seed=args.seed), kv_dtype=args.kv_dtype,
                                      mode="chain")
-    rng = np.random.default_rng([args.seed, B, P])
+    rng = np.random.default_rng([args.seed, B, P, rank])
     prompts = rng.integers(0, model.vocab, size=(B, P))
     capacity = P + 2 * (args.warmup + args.steps) + 2
     state = model.new_batch_state(B, capacity)
@@ -494,12 +624,14 @@ def run_batch(args) -> int:
     prompt_s = time.perf_counter() - t0
     model.generate_batch(state, args.warmup)
     start, end = _event_pair(torch)
+    barrier()
     torch.cuda.synchronize()
-    with ClockSampler(torch.cuda.current_device()) as clocks:
+    with ClockSampler(local_rank) as clocks:
         start.record()
         model.generate_batch(state, args.steps)
         end.record()
         torch.cuda.synchronize()
+    barrier()
     elapsed = start.elapsed_time(end) / 1000.0
     ctx0 = P + args.warmup
     # e2e: host ids in, host greedy ids out, every step
@@ -510,6 +642,7 @@ def run_batch(args) -> int:
         host_next.copy_(state.next_tokens)
         tokens = host_next.numpy().copy()
     e_start, e_end = _event_pair(torch)
+    barrier()
     torch.cuda.synchronize()
     e_start.record()
     for _ in range(args.steps):
@@ -518,28 +651,37 @@ def run_batch(args) -> int:
         tokens = host_next.numpy().copy()
     e_end.record()
     torch.cuda.synchronize()
+    barrier()
     e2e_elapsed = e_start.elapsed_time(e_end) / 1000.0
+    times = torch.tensor([elapsed, e2e_elapsed], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    elapsed, e2e_elapsed = float(times[0]), float(times[1])
+    status = model.status()
+    if rank != 0:
+        return 0
     kv_bytes = 2 if args.kv_dtype == "float16" else 4
     per_pos = model.n_layers * 2 * model.kv_size * kv_bytes
     mean_ctx = ctx0 + (args.steps + 1) / 2
     bytes_per_step = model.weight_bytes + B * per_pos * mean_ctx
     achieved = bytes_per_step * args.steps / elapsed / 1e9
     line = {
-        "metric": "batched decode tok/s Qwen3-4B int4 (config 3)", "value": round(B * args.steps / elapsed, 1),
-        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "metric": "batched decode tok/s Qwen3-4B int4 (config 3)",
+        "value": round(world * B * args.steps / elapsed, 1),
+        "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(elapsed / args.steps * 1000, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int4xint8", "data": "synthetic",
         "config": {"workload": f"config3: batch {B}, {P}-token random prompts, greedy decode, tcgen05 GEMM body",
                    "batch": B, "prompt": P, "kv_dtype": args.kv_dtype, "layers": model.n_layers,
                    "context": [ctx0, ctx0 + args.steps], "l2": "inputs larger than L2",
-                   "prompt_feed_s": round(prompt_s, 2)},
-        "e2e": {"value": round(B * args.steps / e2e_elapsed, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
-                "d2h_bytes_per_step": 4 * B},
+                   "prompt_feed_s": round(prompt_s, 2), "parallelism": f"replicas x{world}"},
+        "e2e": {"value": round(world * B * args.steps / e2e_elapsed, 1), "unit": "tok/s",
+                "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
         "roofline": {"bound": "hbm", "kernel": "whole batched step (weights + every sequence's K/V)",
                      "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "bytes_per_step": int(bytes_per_step),
                      "peak_source": peaks["source"]},
-        "clocks": clocks.summary(), "device_status": model.status(),
+        "clocks": clocks.summary(), "device_status": status,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -853,8 +995,7 @@ def run_tp(args, rank, world, local_rank, dist) -> int:
 
 def main() -> int:
     args = parse_args()
-    single = {"gemv": run_gemv, "batch": run_batch, "prefill": run_prefill, "gemm": run_gemm,
-              "attention": run_attention}
+    single = {"gemv": run_gemv, "prefill": run_prefill, "gemm": run_gemm, "attention": run_attention}
     if args.workload in single:
         return single[args.workload](args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -888,6 +1029,8 @@ def main() -> int:
     try:
         if args.workload == "tp":
             return run_tp(args, rank, world, local_rank, dist)
+        if args.workload == "batch":
+            return run_batch(args, rank, world, local_rank, dist)
         return run_ours(args, rank, world, local_rank, dist)
     finally:
         if dist is not None:

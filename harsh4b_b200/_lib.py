@@ -117,6 +117,8 @@ _SIGNATURES = {
     "h4b_tp_gather_best": [ctypes.POINTER(TpGroupDesc), _vp, _vp, _i32, _vp, _vp],
     "h4b_prefill": [ctypes.POINTER(ModelDesc), ctypes.POINTER(StateDesc), ctypes.POINTER(PrefillScratchDesc), _i32,
                     _vp],
+    "h4b_prefill_tp_stage": [ctypes.POINTER(ModelDesc), ctypes.POINTER(StateDesc), ctypes.POINTER(PrefillScratchDesc),
+                             _i32, _i32, _i32, _vp, _vp, _i32, _vp, _vp, _vp],
     "h4b_lattice_scratch_bytes": [_i32],
     "h4b_lattice_to_int4": [ctypes.POINTER(LatticeProjectionDesc), _vp, _vp, _vp, ctypes.POINTER(_i32), _vp],
     "h4b_rows_to_int4": [_vp, _i32, _i32, _i32, _vp, _vp, _vp],

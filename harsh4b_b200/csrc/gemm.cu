@@ -32,6 +32,7 @@ struct GemmArgs {
     const float* w_scale;   // [N]
     float* out;             // [M][N]
     int M, N, K;
+    int32_t* out_i32 = nullptr;  // when set: the exact int32 sums [M][N] instead of `out`
 };
 
 // cp.async with a source size: bytes past src_bytes are zero-filled.
@@ -129,6 +130,12 @@ __global__ void __launch_bounds__(256) int4_gemm_kernel(const GemmArgs g) {
             const int m = m0 + 8 * j + 2 * tig + c;
             if (m >= g.M) continue;
             const int bias = -8 * g.act_sum[m];
+            if (g.out_i32) {
+                int32_t* irow = g.out_i32 + static_cast<size_t>(m) * g.N;
+                irow[r0] = acc[j][c] + bias;
+                irow[r0 + 8] = acc[j][2 + c] + bias;
+                continue;
+            }
             const float as = g.act_scale[m];
             float* orow = g.out + static_cast<size_t>(m) * g.N;
             orow[r0] = __fmul_rn(__fmul_rn(static_cast<float>(acc[j][c] + bias), as), ws0);
@@ -139,18 +146,26 @@ __global__ void __launch_bounds__(256) int4_gemm_kernel(const GemmArgs g) {
 
 // Per-token quantisation of M rows (the quantize_activation contract per row)
 // plus each row's int8 sum: one CTA per row.
+// With `given_max`, row r is quantised with the absmax given_max[r] (a
+// maximum taken over more values than this row holds, e.g. over the ranks of
+// a tensor-parallel group) instead of its own.
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* v, int K, int8_t* q, float* scales,
-                                                            int32_t* sums) {
+                                                            int32_t* sums, const float* given_max = nullptr) {
     __shared__ float red[8];
     __shared__ int ired[8];
     const float* row = v + static_cast<size_t>(blockIdx.x) * K;
-    float mx = 0.f;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) mx = fmaxf(mx, fabsf(row[i]));
-    mx = warp_max(mx);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    float m = red[0];
-    for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
+    float m;
+    if (given_max) {
+        m = given_max[blockIdx.x];
+    } else {
+        float mx = 0.f;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) mx = fmaxf(mx, fabsf(row[i]));
+        mx = warp_max(mx);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+        __syncthreads();
+        m = red[0];
+        for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
+    }
     const float qs = quant_multiplier(m);
     int s = 0;
     int8_t* qrow = q + static_cast<size_t>(blockIdx.x) * K;

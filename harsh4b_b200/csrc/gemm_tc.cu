@@ -65,6 +65,7 @@ struct TcArgs {
     const float* w_scale;    // [N]
     float* out;              // [M][N]
     int M, N, K;
+    int32_t* out_i32;        // when set: the exact int32 sums [M][N] instead of `out`
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -275,8 +276,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int j = 0; j < 16; ++j) {
                     const int m = m0 + c0 + j;
                     if (m < g.M) {
-                        g.out[static_cast<size_t>(m) * g.N + row] =
-                            __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[j])), g.act_scale[m]), ws);
+                        if (g.out_i32)
+                            g.out_i32[static_cast<size_t>(m) * g.N + row] = static_cast<int>(v[j]);
+                        else
+                            g.out[static_cast<size_t>(m) * g.N + row] =
+                                __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[j])), g.act_scale[m]), ws);
                     }
                 }
             }
@@ -383,7 +387,7 @@ int launch_tc(const GemmArgs& g, cudaStream_t stream) {
     if (!byte_matrix_map(&wmap, g.w, static_cast<uint64_t>(g.K) / 2, g.N, kTcK / 2, kTcRows, false) ||
         !byte_matrix_map(&xmap, g.x, g.K, g.M, kTcK, TOK, true))
         return H4B_EUNSUPPORTED;
-    const TcArgs a{g.act_scale, g.w_scale, g.out, g.M, g.N, g.K};
+    const TcArgs a{g.act_scale, g.w_scale, g.out, g.M, g.N, g.K, g.out_i32};
     const dim3 grid(g.N / kTcRows, (g.M + TOK - 1) / TOK);
     int4_gemm_tc_kernel<TOK><<<grid, kTcThreads, C::kSmem, stream>>>(wmap, xmap, a);
     H4B_CUDA_TRY(cudaGetLastError());

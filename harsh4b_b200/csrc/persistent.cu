@@ -93,7 +93,6 @@ struct MkArgs {
     int max_splits;        // splits per kv head at most
     int stage_splits;      // splits whose partials fit the K/V staging area
     int xq_bytes, rows_cap;
-    int inflight;          // bulk copies the producer keeps in flight at most
 };
 
 struct Seg {
@@ -1015,18 +1014,6 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
                             break;
                         }
                     }
-                    if (seq >= static_cast<uint32_t>(a.inflight)) {
-                        // At most `inflight` copies outstanding: wait until the
-                        // copy `inflight` tiles back has landed. Its full
-                        // barrier stays in that completed phase until this
-                        // warp re-arms the slot, `stages` tiles later.
-                        const uint32_t back = seq - a.inflight;
-                        if (!mbar_wait(&full[back % a.stages], (back / a.stages) & 1)) {
-                            atomicOr(&flags[0], 1);
-                            stop = true;
-                            break;
-                        }
-                    }
                     const int rows_t = min(sg.tile_rows, sg.nrows - t * sg.tile_rows);
                     const uint32_t bytes = static_cast<uint32_t>(rows_t) * sg.kb;
                     if (seq >= 40 && seq < 140) H4B_TRACE_ANY(1400 + seq - 40);
@@ -1220,7 +1207,6 @@ static int plan_persistent(const h4b_model* m, const h4b_state* s, MkPlan* p) {
     const MkSmem base = mk_smem_layout(a.xq_bytes, m->hidden, a.rows_cap, kv_bytes, 0, 0);
     const int budget = 227 * 1024 - base.total;
     a.stages = kMkStages;
-    a.inflight = std::min(a.stages, tuning_env("H4B_INFLIGHT", a.stages));
     a.slot_bytes = std::min(kMkMaxSlotBytes, budget / kMkStages / 1024 * 1024);
     if (a.slot_bytes < max_width / 2) return H4B_EUNSUPPORTED;  // one row must fit a slot
     p->smem = mk_smem_layout(a.xq_bytes, m->hidden, a.rows_cap, kv_bytes, a.stages, a.slot_bytes).total;

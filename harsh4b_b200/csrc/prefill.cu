@@ -85,32 +85,47 @@ int validate_prefill(const h4b_model* m, const h4b_state* s, const h4b_prefill_s
     return 0;
 }
 
-int prefill(const h4b_model* m, const h4b_state* s, const h4b_prefill_scratch* p, int count, cudaStream_t stream) {
-    int rc = validate_prefill(m, s, p, count);
-    if (rc) return rc;
-    const int H = m->hidden, I = m->intermediate, d = m->head_dim;
-    const int q_size = m->heads * d, kv_size = m->kv_heads * d, qkv_rows = q_size + 2 * kv_size;
-    const size_t kv_layer = static_cast<size_t>(m->kv_heads) * s->capacity * d;  // elements
-    const size_t eb = s->kv_dtype == 0 ? 4 : 2;
-    auto gemm = [&](const uint8_t* w, const float* ws, float* out, int rows, int width) {
-        GemmArgs g{p->x8, p->act_scale, p->act_sum, w, ws, out, count, rows, width};
-        return launch_int4_gemm(g, stream);
-    };
-    auto norm_quant = [&](const float* gamma) {
-        batch_rmsnorm_quant_kernel<<<count, 256, 0, stream>>>(p->x, gamma, m->eps, H, p->x8, p->act_scale, p->act_sum);
-        return cudaGetLastError() == cudaSuccess ? 0 : H4B_EINVAL;
-    };
-    auto add_x = [&]() {
-        const long long n = static_cast<long long>(count) * H;
-        add_kernel<<<static_cast<int>((n + 255) / 256), 256, 0, stream>>>(p->x, p->proj, static_cast<int>(n));
-        return cudaGetLastError() == cudaSuccess ? 0 : H4B_EINVAL;
-    };
+// The parts of a prefill layer, shared by the single-GPU loop (prefill)
+// and the tensor-parallel stages (prefill_tp_stage).
+struct PrefillRun {
+    const h4b_model* m;
+    const h4b_state* s;
+    const h4b_prefill_scratch* p;
+    int count;
+    cudaStream_t stream;
 
-    prefill_setup_kernel<<<std::min((count + 255) / 256, 148), 256, 0, stream>>>(s->position, count, s->capacity,
-                                                                               p->positions, s->argmax_key);
-    batch_embed_kernel<<<count, 256, 0, stream>>>(p->tokens, m->w_embed, m->s_embed, m->vocab, H, p->x);
-    H4B_CUDA_TRY(cudaGetLastError());
-    for (int l = 0; l < m->layers; ++l) {
+    int gemm(const uint8_t* w, const float* ws, float* out, int rows, int width, int32_t* out_i32 = nullptr) const {
+        GemmArgs g{p->x8, p->act_scale, p->act_sum, w, ws, out, count, rows, width};
+        g.out_i32 = out_i32;
+        return launch_int4_gemm(g, stream);
+    }
+    int norm_quant(const float* gamma) const {
+        batch_rmsnorm_quant_kernel<<<count, 256, 0, stream>>>(p->x, gamma, m->eps, m->hidden, p->x8, p->act_scale,
+                                                              p->act_sum);
+        H4B_CUDA_TRY(cudaGetLastError());
+        return 0;
+    }
+    int add_x() const {
+        const long long n = static_cast<long long>(count) * m->hidden;
+        add_kernel<<<static_cast<int>((n + 255) / 256), 256, 0, stream>>>(p->x, p->proj, static_cast<int>(n));
+        H4B_CUDA_TRY(cudaGetLastError());
+        return 0;
+    }
+    int setup(const uint8_t* table, const float* table_scales, int table_vocab) const {
+        prefill_setup_kernel<<<std::min((count + 255) / 256, 148), 256, 0, stream>>>(s->position, count, s->capacity,
+                                                                                   p->positions, s->argmax_key);
+        batch_embed_kernel<<<count, 256, 0, stream>>>(p->tokens, table, table_scales, table_vocab, m->hidden, p->x);
+        H4B_CUDA_TRY(cudaGetLastError());
+        return 0;
+    }
+    // RMSNorm, quantisation, the qkv GEMM, q/k norm + RoPE + K/V append and
+    // attention of every prompt row: p->attended.
+    int attention_block(int l) const {
+        const int H = m->hidden, d = m->head_dim;
+        const int q_size = m->heads * d, kv_size = m->kv_heads * d, qkv_rows = q_size + 2 * kv_size;
+        const size_t kv_layer = static_cast<size_t>(m->kv_heads) * s->capacity * d;  // elements
+        const size_t eb = s->kv_dtype == 0 ? 4 : 2;
+        int rc;
         if ((rc = norm_quant(m->norm_in + static_cast<size_t>(l) * H))) return rc;
         if ((rc = gemm(m->w_qkv + static_cast<size_t>(l) * qkv_rows * (H / 2), m->s_qkv + static_cast<size_t>(l) * qkv_rows,
                        p->qkv, qkv_rows, H)))
@@ -146,12 +161,12 @@ int prefill(const h4b_model* m, const h4b_state* s, const h4b_prefill_scratch* p
             a.out = p->attended + static_cast<size_t>(c0) * q_size; a.out_batch_stride = q_size;
             if ((rc = launch_attention(a, s->kv_dtype, n, stream, false))) return rc;
         }
-        quantize_rows_kernel<<<count, 256, 0, stream>>>(p->attended, q_size, p->x8, p->act_scale, p->act_sum);
-        H4B_CUDA_TRY(cudaGetLastError());
-        if ((rc = gemm(m->w_o + static_cast<size_t>(l) * H * (q_size / 2), m->s_o + static_cast<size_t>(l) * H, p->proj,
-                       H, q_size)))
-            return rc;
-        if ((rc = add_x())) return rc;
+        return 0;
+    }
+    // RMSNorm, quantisation, the gate/up GEMM and SwiGLU: p->act.
+    int mlp_block(int l) const {
+        const int H = m->hidden, I = m->intermediate;
+        int rc;
         if ((rc = norm_quant(m->norm_post + static_cast<size_t>(l) * H))) return rc;
         if ((rc = gemm(m->w_gate_up + static_cast<size_t>(l) * 2 * I * (H / 2),
                        m->s_gate_up + static_cast<size_t>(l) * 2 * I, p->gate_up, 2 * I, H)))
@@ -159,18 +174,121 @@ int prefill(const h4b_model* m, const h4b_state* s, const h4b_prefill_scratch* p
         const long long n_act = static_cast<long long>(count) * I;
         batch_swiglu_kernel<<<static_cast<int>((n_act + 255) / 256), 256, 0, stream>>>(p->gate_up, I, count, p->act);
         H4B_CUDA_TRY(cudaGetLastError());
+        return 0;
+    }
+    // The last prompt row: final RMSNorm, LM head, greedy token (the decode stages).
+    int finish() const {
+        H4B_CUDA_TRY(cudaMemcpyAsync(s->x, p->x + static_cast<size_t>(count - 1) * m->hidden,
+                                     sizeof(float) * m->hidden, cudaMemcpyDeviceToDevice, stream));
+        int rc;
+        if ((rc = launch_stage(m, s, STAGE_LM_HEAD, 0, stream, false))) return rc;
+        prefill_finish_kernel<<<1, 32, 0, stream>>>(s->argmax_key, s->next_token, s->token, s->position, count);
+        H4B_CUDA_TRY(cudaGetLastError());
+        return 0;
+    }
+};
+
+int prefill(const h4b_model* m, const h4b_state* s, const h4b_prefill_scratch* p, int count, cudaStream_t stream) {
+    int rc = validate_prefill(m, s, p, count);
+    if (rc) return rc;
+    const int H = m->hidden, I = m->intermediate, q_size = m->heads * m->head_dim;
+    const PrefillRun r{m, s, p, count, stream};
+    if ((rc = r.setup(m->w_embed, m->s_embed, m->vocab))) return rc;
+    for (int l = 0; l < m->layers; ++l) {
+        if ((rc = r.attention_block(l))) return rc;
+        quantize_rows_kernel<<<count, 256, 0, stream>>>(p->attended, q_size, p->x8, p->act_scale, p->act_sum);
+        H4B_CUDA_TRY(cudaGetLastError());
+        if ((rc = r.gemm(m->w_o + static_cast<size_t>(l) * H * (q_size / 2), m->s_o + static_cast<size_t>(l) * H, p->proj,
+                         H, q_size)))
+            return rc;
+        if ((rc = r.add_x())) return rc;
+        if ((rc = r.mlp_block(l))) return rc;
         quantize_rows_kernel<<<count, 256, 0, stream>>>(p->act, I, p->x8, p->act_scale, p->act_sum);
         H4B_CUDA_TRY(cudaGetLastError());
-        if ((rc = gemm(m->w_down + static_cast<size_t>(l) * H * (I / 2), m->s_down + static_cast<size_t>(l) * H, p->proj,
-                       H, I)))
+        if ((rc = r.gemm(m->w_down + static_cast<size_t>(l) * H * (I / 2), m->s_down + static_cast<size_t>(l) * H, p->proj,
+                         H, I)))
             return rc;
-        if ((rc = add_x())) return rc;
+        if ((rc = r.add_x())) return rc;
     }
-    // the last prompt row: final RMSNorm, LM head, greedy token (the decode stages)
-    H4B_CUDA_TRY(cudaMemcpyAsync(s->x, p->x + static_cast<size_t>(count - 1) * H, sizeof(float) * H,
-                                 cudaMemcpyDeviceToDevice, stream));
-    if ((rc = launch_stage(m, s, STAGE_LM_HEAD, 0, stream, false))) return rc;
-    prefill_finish_kernel<<<1, 32, 0, stream>>>(s->argmax_key, s->next_token, s->token, s->position, count);
+    return r.finish();
+}
+
+// ---- tensor-parallel prefill stages ------------------------------------------
+// Each rank holds a slice (its heads, its MLP units, K-slices of o and down,
+// its vocabulary rows); x is replicated. Between the stages the caller runs
+// the cross-rank reductions: a MAX over `absmax` after stages 1 and 3, an
+// exact int32 SUM over `acc` after stages 2 and 4.
+
+__global__ void __launch_bounds__(256) row_absmax_kernel(const float* v, int K, float* out) {
+    __shared__ float red[8];
+    const float* row = v + static_cast<size_t>(blockIdx.x) * K;
+    float mx = 0.f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) mx = fmaxf(mx, fabsf(row[i]));
+    mx = warp_max(mx);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float m = red[0];
+        for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
+        out[blockIdx.x] = m;
+    }
+}
+
+// x[m][r] += float(acc[m][r]) * act_scale[m] * w_scale[r] (the GEMM epilogue
+// order, then the residual add).
+__global__ void residual_rows_kernel(float* x, const int32_t* acc, const float* act_scale, const float* w_scale,
+                                     int rows, int H) {
+    const long long n = static_cast<long long>(rows) * H;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int mrow = static_cast<int>(i / H), r = static_cast<int>(i - static_cast<long long>(mrow) * H);
+        x[i] = __fadd_rn(x[i], __fmul_rn(__fmul_rn(static_cast<float>(acc[i]), act_scale[mrow]), w_scale[r]));
+    }
+}
+
+int prefill_tp_stage(const h4b_model* m, const h4b_state* s, const h4b_prefill_scratch* p, int count, int layer,
+                     int stage, const uint8_t* table, const float* table_scales, int table_vocab, float* absmax,
+                     int32_t* acc, cudaStream_t stream) {
+    int rc = validate_prefill(m, s, p, count);
+    if (rc) return rc;
+    if (!absmax || !acc) return H4B_EINVAL;
+    if (stage >= 1 && stage <= 5 && (layer < 0 || layer >= m->layers)) return H4B_EINVAL;
+    const int H = m->hidden, I = m->intermediate, q_size = m->heads * m->head_dim;
+    const size_t l = static_cast<size_t>(layer);
+    const PrefillRun r{m, s, p, count, stream};
+    const int grid = std::max(1, std::min(static_cast<int>((static_cast<long long>(count) * H + 255) / 256),
+                                          8 * sm_count()));
+    switch (stage) {
+        case 0:
+            if (!table || !table_scales || table_vocab < 1) return H4B_EINVAL;
+            return r.setup(table, table_scales, table_vocab);
+        case 1:
+            if ((rc = r.attention_block(layer))) return rc;
+            row_absmax_kernel<<<count, 256, 0, stream>>>(p->attended, q_size, absmax);
+            break;
+        case 2:
+            quantize_rows_kernel<<<count, 256, 0, stream>>>(p->attended, q_size, p->x8, p->act_scale, p->act_sum,
+                                                            absmax);
+            H4B_CUDA_TRY(cudaGetLastError());
+            return r.gemm(m->w_o + l * H * (q_size / 2), m->s_o + l * H, p->proj, H, q_size, acc);
+        case 3:
+            residual_rows_kernel<<<grid, 256, 0, stream>>>(p->x, acc, p->act_scale, m->s_o + l * H, count, H);
+            H4B_CUDA_TRY(cudaGetLastError());
+            if ((rc = r.mlp_block(layer))) return rc;
+            row_absmax_kernel<<<count, 256, 0, stream>>>(p->act, I, absmax);
+            break;
+        case 4:
+            quantize_rows_kernel<<<count, 256, 0, stream>>>(p->act, I, p->x8, p->act_scale, p->act_sum, absmax);
+            H4B_CUDA_TRY(cudaGetLastError());
+            return r.gemm(m->w_down + l * H * (I / 2), m->s_down + l * H, p->proj, H, I, acc);
+        case 5:
+            residual_rows_kernel<<<grid, 256, 0, stream>>>(p->x, acc, p->act_scale, m->s_down + l * H, count, H);
+            break;
+        case 6:
+            return r.finish();
+        default:
+            return H4B_EINVAL;
+    }
     H4B_CUDA_TRY(cudaGetLastError());
     return 0;
 }
@@ -180,4 +298,11 @@ int prefill(const h4b_model* m, const h4b_state* s, const h4b_prefill_scratch* p
 extern "C" int h4b_prefill(const h4b_model* model, const h4b_state* state, const h4b_prefill_scratch* scratch,
                            int count, void* stream) {
     return h4b::prefill(model, state, scratch, count, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h4b_prefill_tp_stage(const h4b_model* model, const h4b_state* state, const h4b_prefill_scratch* scratch,
+                                    int count, int layer, int stage, const uint8_t* table, const float* table_scales,
+                                    int table_vocab, float* absmax, int32_t* acc, void* stream) {
+    return h4b::prefill_tp_stage(model, state, scratch, count, layer, stage, table, table_scales, table_vocab, absmax,
+                                 acc, static_cast<cudaStream_t>(stream));
 }

@@ -69,7 +69,7 @@ class CudaDecodeState:
     """Caller-owned KV cache and scratch on the device (QwenDecodeState,
     cpu_lightspark.py:275-309). One CUDA graph per state replays a token."""
 
-    def __init__(self, model: "CudaQwen", capacity: int, attn_splits: int | None = None):
+    def __init__(self, model: "CudaQwen", capacity: int, attn_splits: int | None = None, kv=None):
         if capacity < 1:
             raise ValueError("decode capacity must be positive")
         if capacity > model.max_pos:
@@ -80,8 +80,16 @@ class CudaDecodeState:
         dev = model.device
         code, kv_torch = KV_DTYPES[model.kv_dtype]
         shape = (model.n_layers, model.kv_heads, self.capacity, model.head_dim)
-        self.k_cache = torch.zeros(shape, dtype=kv_torch, device=dev)
-        self.v_cache = torch.zeros(shape, dtype=kv_torch, device=dev)
+        if kv is None:
+            self.k_cache = torch.zeros(shape, dtype=kv_torch, device=dev)
+            self.v_cache = torch.zeros(shape, dtype=kv_torch, device=dev)
+        else:
+            # K/V held elsewhere (e.g. one sequence slot of a batch state)
+            self.k_cache, self.v_cache = kv
+            for t in kv:
+                if tuple(t.shape) != shape or t.dtype != kv_torch or t.device != dev or not t.is_contiguous():
+                    raise ValueError("external K/V buffers must be contiguous [layers][kv_heads][capacity][head_dim] "
+                                     "in the model's KV dtype on its device")
         self.splits = int(attn_splits or model.attn_splits)
         partial_splits = self.splits
         i32 = dict(dtype=torch.int32, device=dev)

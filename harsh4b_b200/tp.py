@@ -16,6 +16,12 @@ Partitioning (g ranks; g divides the q heads, the kv heads, the MLP width /
   token is the best (value, global index) over the ranks (all-gather);
 * embedding, RMSNorm, residual stream: replicated.
 
+Prefill (:meth:`TensorParallelQwen.prefill`) shards the same way with M
+prompt rows at a time: every rank runs its slice's GEMMs over all rows
+(h4b_prefill_tp_stage), the per-row absmax of the o / down inputs is reduced
+with MAX over the ranks ([M] floats) and their int32 row sums with SUM
+([M][H] int32, 21 MB at M = 2048), both as NCCL all-reduces.
+
 The exchanges run either as single-kernel one-shot transfers over NVLink
 peer memory (comm="p2p", csrc/tp.cu: the absmax MAX, the int32 SUM fused
 with the residual epilogue, the greedy candidates) or as NCCL collectives
@@ -251,6 +257,66 @@ class TensorParallelQwen:
         self._best[0:1].copy_(state.logits.index_select(0, local))
         self._best[1:2].copy_(local + self.vocab_offset)
         dist.all_gather_into_tensor(self._gathered, self._best, group=self.group)
+
+    def prefill(self, token_ids, state, max_tokens: int = 2048, attn_splits: int = 1):
+        """Feed a prompt on every rank (all ranks pass the same ids): the
+        sharded h4b_prefill_tp_stage sequence with NCCL all-reduces of the
+        per-row absmax (MAX) and of the o / down int32 row sums (SUM)
+        between the stages. Returns (greedy token, local logits slice) of the
+        last prompt row; the state then stands where forward_token over the
+        same ids with `attn_splits` splits per prompt query leaves it."""
+        import ctypes
+
+        from ._lib import check, lib
+        from .model import PrefillScratch
+
+        torch, dist, m = self.torch, self.dist, self.model
+        ids = np.asarray([int(t) for t in token_ids], dtype=np.int32)
+        if ids.size == 0:
+            raise ValueError("empty prompt")
+        if state.position + ids.size > state.capacity:
+            raise ValueError("decode state capacity exhausted")
+        if ids.min() < 0 or ids.max() >= self.vocab:
+            raise ValueError("token ID outside the vocabulary")
+        rows = min(int(max_tokens), int(ids.size))
+        scratch = m._prefill_scratch
+        if scratch is None or scratch.max_tokens < rows or scratch.splits != int(attn_splits):
+            scratch = m._prefill_scratch = PrefillScratch(m, rows, int(attn_splits))
+        absmax = torch.empty(scratch.max_tokens, dtype=torch.float32, device=self.device)
+        acc = torch.empty(scratch.max_tokens, m.hidden, dtype=torch.int32, device=self.device)
+        stream = torch.cuda.current_stream(self.device)
+
+        def stage(count, layer, index):
+            check(lib().h4b_prefill_tp_stage(ctypes.byref(m.desc), ctypes.byref(state.desc), ctypes.byref(scratch.desc),
+                                             count, layer, index, self.table.data_ptr(), self.table_scales.data_ptr(),
+                                             self.vocab, absmax.data_ptr(), acc.data_ptr(), stream.cuda_stream),
+                  "h4b_prefill_tp_stage")
+
+        MAX, SUM = dist.ReduceOp.MAX, dist.ReduceOp.SUM
+        for start in range(0, ids.size, scratch.max_tokens):
+            part = ids[start:start + scratch.max_tokens]
+            n = int(part.size)
+            scratch.tokens[:n].copy_(torch.from_numpy(part))
+            stage(n, 0, 0)
+            for layer in range(m.n_layers):
+                stage(n, layer, 1)
+                dist.all_reduce(absmax[:n], op=MAX, group=self.group)
+                stage(n, layer, 2)
+                dist.all_reduce(acc[:n], op=SUM, group=self.group)
+                stage(n, layer, 3)
+                dist.all_reduce(absmax[:n], op=MAX, group=self.group)
+                stage(n, layer, 4)
+                dist.all_reduce(acc[:n], op=SUM, group=self.group)
+                stage(n, layer, 5)
+            stage(n, 0, 6)
+            state.position += n
+        local = state.next_token_dev.to(torch.int64)
+        self._best[0:1].copy_(state.logits.index_select(0, local))
+        self._best[1:2].copy_(local + self.vocab_offset)
+        dist.all_gather_into_tensor(self._gathered, self._best, group=self.group)
+        pairs = self._gathered.cpu().numpy().reshape(self.world, 2)
+        token = global_argmax(pairs[:, 0], pairs[:, 1].astype(np.int64))
+        return token, state.logits
 
     def _p2p(self, name: str, *args) -> None:
         import ctypes

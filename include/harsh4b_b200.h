@@ -363,6 +363,31 @@ typedef struct h4b_prefill_scratch {
 int h4b_prefill(const h4b_model *model, const h4b_state *state, const h4b_prefill_scratch *scratch, int count,
                 void *stream);
 
+/* One stage of a tensor-parallel prefill on this rank's slice of the model
+ * (its q/k/v heads, its MLP units, K-slices of o_proj and down_proj, its
+ * vocabulary rows; x replicated): the reference's prefill loop
+ * (cpu_lightspark.py:809-810) over `count` prompt rows, as h4b_prefill, with
+ * the o and down projections split along K. Stages, per layer in order:
+ *   0 (once, layer ignored): positions, embedding of scratch->tokens from the
+ *     full table `table` / `table_scales` (table_vocab rows);
+ *   1: attention block (RMSNorm, quantisation, qkv GEMM, q/k norm, RoPE,
+ *      K/V append, attention); absmax[i] = max |attended row i| here;
+ *   2: attended rows quantised with the scale of absmax[i] (the maximum over
+ *      all ranks after a MAX reduction), o GEMM: acc[i][r] = exact int32 sum
+ *      over this rank's K slice;
+ *   3: x += float(acc) * act_scale * w_scale (acc summed over the ranks),
+ *      then the MLP block (RMSNorm, quantisation, gate/up GEMM, SwiGLU);
+ *      absmax[i] = max |act row i| here;
+ *   4: act quantised with absmax (the global maximum), down GEMM into acc;
+ *   5: x += float(acc) * act_scale * w_scale (acc summed over the ranks);
+ *   6 (once): last row through the final RMSNorm and this rank's LM-head rows;
+ *      state->logits, argmax key, next_token (a local index) and position.
+ * The caller reduces absmax with MAX after stages 1 and 3 and acc with an
+ * int32 SUM after stages 2 and 4. absmax: float[count], acc: int32[count][hidden]. */
+int h4b_prefill_tp_stage(const h4b_model *model, const h4b_state *state, const h4b_prefill_scratch *scratch,
+                         int count, int layer, int stage, const uint8_t *table, const float *table_scales,
+                         int table_vocab, float *absmax, int32_t *acc, void *stream);
+
 /* ---- format producer: LATTICE checkpoint -> packed int4 cache ------------- */
 
 /* One LATTICE projection as stored in the checkpoint (all pointers are

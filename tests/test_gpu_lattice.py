@@ -2,11 +2,13 @@
 against the reference's conversion (golden fixtures) and the CPU
 restatement, and the model built from a LATTICE checkpoint file.
 
-Tolerance: the rotation is accumulated in fp64 on the device and in fp32 by
-the reference's BLAS, so a code may differ by one where w / scale lies
-within a few ulp of a rounding boundary (|w / scale - (k + 1/2)| < 1e-4 here),
-and a row scale by an ulp or two; the dense-row (embedding) conversion has no
-product and must be bit-exact.
+Tolerance: the rotation is accumulated in fp64 on the device, so against
+the restatement's fp64 rotation the scales agree to 2.5e-7 (they are
+bit-equal in practice); the reference rotates in fp32 through its BLAS,
+whose rounding moves a row maximum by up to ~1e-6 relative (measured: 4-7
+ulp), so against it the scales agree to 2e-6 and a code may differ by one
+where w / scale lies within 1e-4 of a rounding boundary. The dense-row
+(embedding) conversion has no product and must be bit-exact.
 """
 import json
 from pathlib import Path
@@ -31,9 +33,9 @@ def _unpack(packed):
     return out
 
 
-def assert_codes_close(got_packed, got_scales, want_packed, want_scales, weight):
-    """Scales within 2 ulp; codes equal except near-ties, where they may differ by one."""
-    np.testing.assert_allclose(got_scales, want_scales, rtol=2.5e-7, atol=0)
+def assert_codes_close(got_packed, got_scales, want_packed, want_scales, weight, rtol=2.5e-7):
+    """Scales within rtol; codes equal except near-ties, where they may differ by one."""
+    np.testing.assert_allclose(got_scales, want_scales, rtol=rtol, atol=0)
     got, want = _unpack(np.asarray(got_packed)), _unpack(np.asarray(want_packed))
     diff = got.astype(np.int16) - want.astype(np.int16)
     assert np.abs(diff).max(initial=0) <= 1
@@ -58,7 +60,7 @@ def test_projection_matches_reference_golden():
         p = _projection(golden, i)
         packed, scales = convert_projection(p, p["left"], p["right"])
         _, _, weight = L.convert_projection(p, p["left"], p["right"])
-        assert_codes_close(packed.cpu().numpy(), scales.cpu().numpy(), p["packed"], p["scales"], weight)
+        assert_codes_close(packed.cpu().numpy(), scales.cpu().numpy(), p["packed"], p["scales"], weight, rtol=2e-6)
 
 
 def test_embedding_rows_bit_exact_with_reference_golden():
@@ -86,7 +88,7 @@ def test_projection_qwen_widths_against_restatement(rows, width, dims, blocksize
     assert_codes_close(packed, scales, want, want_scales, weight)
     # the reference's fp32 order: a handful of tie flips at most
     want32, scales32, weight32 = L.convert_projection(p, left, right)
-    flips = assert_codes_close(packed, scales, want32, scales32, weight32)
+    flips = assert_codes_close(packed, scales, want32, scales32, weight32, rtol=2e-6)
     assert flips <= max(2, rows * width // 10000)
 
 
