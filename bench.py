@@ -430,6 +430,10 @@ def tp_subrecord(args, checkpoint, rank, world, local_rank, dist, context: int =
         match = one == tp_tokens
         st.close()
         del single
+    # every rank waits for rank 0's single-GPU check: the P2P exchanges poll
+    # for their peers with a bounded wait
+    torch.cuda.synchronize()
+    dist.barrier(device_ids=[local_rank])
     # latency from a long context
     state = tp.new_state(context + warmup + steps + 1)
     g = torch.Generator(device=device).manual_seed(args.seed + rank)

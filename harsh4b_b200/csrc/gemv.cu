@@ -26,6 +26,8 @@
 // reading a nibble n as u = n ^ 8 = s + 8 (0..15) turns the even and odd
 // codes into two dp4a operands with no sign extension, and the bias
 // 8 * sum(x) is folded into the lane's starting accumulator.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace h4b {
@@ -485,7 +487,18 @@ static int instantiated_slots(int needed) {
     return 0;
 }
 
+// Bytes of the shared-memory weight ring (tuning builds may override it
+// with H4B_GEMV_RING_KB).
+static int gemv_ring_bytes() {
+#ifdef H4B_TUNING
+    const char* e = std::getenv("H4B_GEMV_RING_KB");
+    if (e && *e) return std::max(16, std::atoi(e)) * 1024;
+#endif
+    return kRingBytes;
+}
+
 int plan_gemv(int rows, int width, int row_align, GemvPlan* p) {
+    const int ring_bytes = gemv_ring_bytes();
     if (rows <= 0 || width <= 0 || (width & 31) || rows % row_align) return H4B_EINVAL;
     const int chunks = width >> 5;
     const int slots = instantiated_slots((chunks + 31) / 32);
@@ -503,10 +516,10 @@ int plan_gemv(int rows, int width, int row_align, GemvPlan* p) {
     // start waiting for a tile while the slot's previous tile, owned by
     // another warp, is still in flight -- and the mbarrier parity of that
     // older phase would read as complete.)
-    tile_rows = max(1, min(tile_rows, kRingBytes / (kConsumerWarps * kb)));
+    tile_rows = max(1, min(tile_rows, ring_bytes / (kConsumerWarps * kb)));
     const int stage_bytes = tile_rows * kb;
-    if (stage_bytes > 64 * 1024 || kConsumerWarps * stage_bytes > kRingBytes) return H4B_EUNSUPPORTED;
-    const int stages = min(kMaxStages, kRingBytes / stage_bytes) / kConsumerWarps * kConsumerWarps;
+    if (stage_bytes > 64 * 1024 || kConsumerWarps * stage_bytes > ring_bytes) return H4B_EUNSUPPORTED;
+    const int stages = min(kMaxStages, ring_bytes / stage_bytes) / kConsumerWarps * kConsumerWarps;
     const int rows_cap = (per_cta + 31) & ~31;
     const SmemLayout L = smem_layout(width, rows_cap, stages, stage_bytes, true);
     if (L.total > 227 * 1024) return H4B_EUNSUPPORTED;

@@ -1068,6 +1068,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         const float* sc_s = sc_base + (g & 1) * a.rows_cap;
         H4B_TRACE(8 + 3 * g);
         if (g >= 8 && g < 12) H4B_TRACE_CTA(4 * (g - 8));
+        if (g == last) H4B_TRACE_CTA(23);  // the LM head segment
 #ifdef H4B_PHASE_TRACE
         if (g >= 8 && g < 12 && threadIdx.x == 0) {
             // one L2 round trip of a word that is already there (this CTA's own launch counter)
@@ -1104,6 +1105,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         }
         H4B_TRACE(8 + 3 * g + 1);
         if (g >= 8 && g < 12) H4B_TRACE_CTA(4 * (g - 8) + 1);
+        if (g == last) H4B_TRACE_CTA(24);  // the LM head segment
         if (g >= 8 && g < 12) H4B_TRACE(1700 + (g - 8));
 
         // ---- tiles ----
@@ -1112,6 +1114,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
         seq += sg.ntiles;
         H4B_TRACE(8 + 3 * g + 2);
         if (g >= 8 && g < 12) H4B_TRACE_CTA(4 * (g - 8) + 2);
+        if (g == last) H4B_TRACE_CTA(25);  // the LM head segment
         if (mk_stop(flags)) return;
 
         // ---- epilogue ----
@@ -1148,6 +1151,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_persistent_kernel(const 
             mk_finish_token(a, sg, sc_s, act, acc_s, xw, tl, pos, flags);
         }
         if (g >= 8 && g < 12) H4B_TRACE_CTA(4 * (g - 8) + 3);
+        if (g == last) H4B_TRACE_CTA(26);  // the LM head segment
     }
 }
 

@@ -80,7 +80,7 @@ def test_batched_backend_streams_concurrent_requests_and_cancels():
 
     checkpoint = synthetic_checkpoint(tiny_config(), seed=9)
     model = CudaQwen.from_checkpoint(checkpoint, kv_dtype="float16")
-    backend = BatchedCudaBackend(model=model, tokenizer=_Tokenizer(model.vocab, stop_ids=()), slots=4, capacity=80)
+    backend = BatchedCudaBackend(model=model, tokenizer=_Tokenizer(model.vocab, stop_ids=()), slots=4, capacity=128)
     outputs, errors = {}, []
     cancel = threading.Event()
 
