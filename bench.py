@@ -34,11 +34,18 @@ sys.path.insert(0, str(ROOT))
 METRIC = "batch-1 decode tok/s Qwen3-4B int4; body-GEMV HBM GB/s vs ~8 TB/s"
 PROMPT = 128
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic
-# byte, from the ncu capture in profiles/decode_persistent_full_4layer.md: the
-# persistent decode kernel on a 4-layer Qwen3-4B-shaped model (weights + LM
-# head + KV). Traffic grows in proportion to the bytes streamed, so the ratio
-# scales a launch of the full model. (No capture of the chain-mode GEMV yet.)
-NCU_TRAFFIC_PER_BYTE = {"persistent": 1.0550, "gemv": None}
+# byte, from ncu captures: the persistent decode kernel on a 4-layer
+# Qwen3-4B-shaped model (weights + LM head + KV,
+# profiles/decode_persistent_full_4layer.md; traffic grows in proportion to
+# the bytes streamed, so the ratio scales a launch of the full model), and
+# the body GEMV kernel on the gate_up shape
+# (profiles/gemv_kernel_gate_up_lm_head_config1.md).
+NCU_TRAFFIC_PER_BYTE = {"persistent": 1.0550, "gemv": 1.001}
+# The persistent kernel's phases from the phase-trace build
+# (profiles/decode_persistent_phases_config0.md): per segment, weight + scale
+# bytes over the longest CTA's tile phase (GB/s), and over the segment span.
+PERSISTENT_PHASES = {"qkv": (5136, 1031), "o": (3731, 356), "gate_up": (4703, 2518), "down": (4099, 1396),
+                     "lm_head": (4989, 4440)}
 
 
 def parse_args():
@@ -354,7 +361,11 @@ def run_ours(args, rank, world, local_rank, dist) -> int:
                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                     "traffic": round(bytes_per_token * ratio) if ratio else None, "bytes_per_launch": bytes_per_token,
                     "avg_launch_us": round(elapsed / args.steps * 1e6, 2), "launches": args.steps,
-                    "peak_source": peaks["source"], "gemv_isolated": gemv_alone}
+                    "peak_source": peaks["source"], "gemv_isolated": gemv_alone,
+                    "gemv_phases": {"source": "phase-trace build, profiles/decode_persistent_phases_config0.md",
+                                    "unit": "GB/s", **{k: {"tile_phase": v[0], "segment": v[1],
+                                                           "tile_phase_frac": round(v[0] / peaks["hbm_gbs"], 3)}
+                                                       for k, v in PERSISTENT_PHASES.items()}}}
     else:
         roofline = dict(gemv_alone, peak_source=peaks["source"])
     line = {
