@@ -287,6 +287,18 @@ __device__ __forceinline__ float group_max(float v, float* scratch, int warps, i
     return total;
 }
 
+// group_max without the closing barrier: `scratch` must not be written
+// again before the caller's next barrier on `bar`.
+__device__ __forceinline__ float group_max_open(float v, float* scratch, int warps, int bar) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_max(v);
+    if (lane == 0) scratch[warp] = v;
+    named_sync(bar, warps * 32);
+    float total = scratch[0];
+    for (int w = 1; w < warps; ++w) total = fmaxf(total, scratch[w]);
+    return total;
+}
+
 // Non-negative floats order like their bit patterns, so an unsigned
 // atomicMax on the bits is an exact, order-independent float max.
 __device__ __forceinline__ void atomic_max_nonneg(float* slot, float value) {

@@ -316,7 +316,8 @@ __device__ float mk_prologue_rms_g(const float* xs, const unsigned long long* xw
     named_sync(1, kMkConsumers);
     float total = 0.f;
     for (int w = 0; w < kRmsLanes / 32; ++w) total += red[w];
-    named_sync(1, kMkConsumers);
+    // (no barrier: the maximum below goes to red[16..], and red[0..7] is
+    // next written after the closing barrier)
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(n)), eps)));
     float local = 0.f;
 #pragma unroll
@@ -336,7 +337,7 @@ __device__ float mk_prologue_rms_g(const float* xs, const unsigned long long* xw
             }
         }
     }
-    const float m = group_max(local, red, kMkWarps, 1);
+    const float m = group_max_open(local, red + 16, kMkWarps, 1);  // closed by the barrier at the end
     const float qs = quant_multiplier(m);
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
@@ -410,7 +411,7 @@ __device__ float mk_prologue_quant(const unsigned long long* vw, const unsigned 
         }
     }
     if (trace_ev >= 0) H4B_TRACE_ANY(trace_ev + 1);
-    const float m = group_max(mx, red, kMkWarps, 1);
+    const float m = group_max_open(mx, red, kMkWarps, 1);  // closed by the barrier at the end
     const float qs = quant_multiplier(m);
 #pragma unroll
     for (int k = 0; k < kMkQuantGroups; ++k) {
