@@ -62,6 +62,109 @@ __global__ void __launch_bounds__(32) prefill_rope_append_kernel(float* qkv, int
     store4<KV>(vcache + at, *(reinterpret_cast<const float4*>(v) + lane));
 }
 
+// Prefill attention with one split per query, for a block of kPrefillQB
+// consecutive prompt queries and one kv head per CTA: every K/V sub-tile of
+// the block's longest context is staged into shared memory once and folded
+// into the running (m, l, o) of every (query, q head) pair that reaches it.
+// A pair sees the same sub-tiles, with the same token counts, in the same
+// order as gqa_split_kernel gives that query alone with one split, so the
+// output is bit for bit the same; only the K/V loads are shared (the block's
+// queries have nearly the same context), which cuts L2 traffic by the block
+// size. 8 warps; pair j = (query j / G, head j % G) belongs to warp j % 8 and
+// keeps its state in registers. G = q heads per kv head (4 for Qwen3-4B).
+constexpr int kPrefillQB = 16;
+constexpr int kPrefillWarps = 8;
+constexpr int kPrefillGroups = 4;
+
+template <typename KV>
+__host__ __device__ constexpr int prefill_block_smem_bytes() {
+    return 2 * kSubTile * kv_row_stride<KV>() * static_cast<int>(sizeof(KV)) +
+           kPrefillQB * kPrefillGroups * kHeadDim * 4;
+}
+
+template <typename KV>
+__global__ void __launch_bounds__(kPrefillWarps * 32) prefill_attention_block_kernel(
+    const float* qkv, int qkv_stride, const KV* kcache, const KV* vcache, long long head_stride,
+    long long time_stride, const int32_t* positions, int count, float* out, int out_stride) {
+    constexpr int groups = kPrefillGroups;
+    constexpr int kPrefillMaxPairs = kPrefillQB * groups / kPrefillWarps;
+    extern __shared__ __align__(16) uint8_t pb_smem[];
+    KV* ks = reinterpret_cast<KV*>(pb_smem);
+    KV* vs = ks + kSubTile * kv_row_stride<KV>();
+    float* qs = reinterpret_cast<float*>(vs + kSubTile * kv_row_stride<KV>());  // [qb][groups][d]
+    // the longest contexts (the last query blocks) first, so the tail is short
+    const int kvh = blockIdx.x, q0 = (gridDim.y - 1 - blockIdx.y) * kPrefillQB;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nq = min(kPrefillQB, count - q0);
+    const int pairs = nq * groups;
+    const KV* kc = kcache + kvh * head_stride;
+    const KV* vc = vcache + kvh * head_stride;
+    // the block's queries (already normalised and rotated by the append kernel)
+    for (int i = threadIdx.x; i < pairs * (kHeadDim / 4); i += blockDim.x) {
+        const int pair = i / (kHeadDim / 4), piece = i % (kHeadDim / 4);
+        const int qi = pair / groups, h = pair % groups;
+        const float4* src = reinterpret_cast<const float4*>(
+            qkv + static_cast<long long>(q0 + qi) * qkv_stride + static_cast<long long>(kvh * groups + h) * kHeadDim);
+        reinterpret_cast<float4*>(qs + pair * kHeadDim)[piece] = src[piece];
+    }
+    int max_ctx = 0;
+    for (int qi = 0; qi < nq; ++qi) max_ctx = max(max_ctx, positions[q0 + qi] + 1);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(kHeadDim)));
+    float m[kPrefillMaxPairs], l[kPrefillMaxPairs];
+    float4 o[kPrefillMaxPairs];
+#pragma unroll
+    for (int j = 0; j < kPrefillMaxPairs; ++j) {
+        m[j] = -INFINITY;
+        l[j] = 0.f;
+        o[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    #pragma unroll 1
+    for (int base = 0; base < max_ctx; base += kSubTile) {
+        const int n_max = min(kSubTile, max_ctx - base);
+        __syncthreads();  // the previous sub-tile (and, first, the queries) are settled
+        stage_subtile<KV>(kc, vc, time_stride, base, n_max, -1, ks, vs, threadIdx.x, blockDim.x);
+        async_copy_wait_all();
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < kPrefillMaxPairs; ++j) {
+            const int pair = warp + kPrefillWarps * j;
+            if (pair >= pairs) continue;
+            const int ctx = positions[q0 + pair / groups] + 1;  // 0 for a row that does not fit
+            if (base >= ctx) continue;
+            attend_subtile<KV>(qs + pair * kHeadDim, ks, vs, min(kSubTile, ctx - base), scale, lane, m[j], l[j], o[j]);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kPrefillMaxPairs; ++j) {
+        const int pair = warp + kPrefillWarps * j;
+        if (pair >= pairs) continue;
+        const int qi = pair / groups, h = pair % groups;
+        if (positions[q0 + qi] < 0) continue;
+        const float inv = __fdiv_rn(1.0f, l[j]);
+        const float4 r = make_float4(o[j].x * inv, o[j].y * inv, o[j].z * inv, o[j].w * inv);
+        *reinterpret_cast<float4*>(out + static_cast<long long>(q0 + qi) * out_stride +
+                                   static_cast<long long>(kvh * groups + h) * kHeadDim + 4 * lane) = r;
+    }
+}
+
+// Shared-memory opt-in of the block kernels above 48 KB, per device,
+// recording only a success.
+static int prefill_block_opt_in() {
+    static std::atomic<bool> opted_in[kMaxDevices];
+    int dev = 0;
+    H4B_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return H4B_EUNSUPPORTED;
+    if (!opted_in[dev].load(std::memory_order_acquire)) {
+        H4B_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_block_kernel<float>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, prefill_block_smem_bytes<float>()));
+        H4B_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_block_kernel<__half>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          prefill_block_smem_bytes<__half>()));
+        opted_in[dev].store(true, std::memory_order_release);
+    }
+    return 0;
+}
+
 __global__ void prefill_finish_kernel(const unsigned long long* argmax_key, int32_t* next_token, int32_t* token,
                                       int32_t* position, int count) {
     if (threadIdx.x == 0) {
@@ -145,6 +248,24 @@ struct PrefillRun {
                 m->norm_k + static_cast<size_t>(l) * d, m->rope_cos, m->rope_sin, m->eps, p->positions,
                 reinterpret_cast<__half*>(kc), reinterpret_cast<__half*>(vc), head_stride, d);
         H4B_CUDA_TRY(cudaGetLastError());
+        if (p->attn_splits == 1 && m->heads / m->kv_heads == kPrefillGroups) {
+            // one split per query: query blocks share their K/V sub-tiles
+            int rc2 = prefill_block_opt_in();
+            if (rc2) return rc2;
+            const dim3 grid(m->kv_heads, (count + kPrefillQB - 1) / kPrefillQB);
+            if (s->kv_dtype == 0)
+                prefill_attention_block_kernel<float><<<grid, kPrefillWarps * 32, prefill_block_smem_bytes<float>(),
+                                                         stream>>>(
+                    p->qkv, qkv_rows, reinterpret_cast<const float*>(kc), reinterpret_cast<const float*>(vc),
+                    head_stride, d, p->positions, count, p->attended, q_size);
+            else
+                prefill_attention_block_kernel<__half><<<grid, kPrefillWarps * 32, prefill_block_smem_bytes<__half>(),
+                                                          stream>>>(
+                    p->qkv, qkv_rows, reinterpret_cast<const __half*>(kc), reinterpret_cast<const __half*>(vc),
+                    head_stride, d, p->positions, count, p->attended, q_size);
+            H4B_CUDA_TRY(cudaGetLastError());
+            return 0;
+        }
         for (int c0 = 0; c0 < count; c0 += p->attn_queries) {
             const int n = std::min(p->attn_queries, count - c0);
             AttnArgs a = {};
