@@ -184,8 +184,11 @@ int decode_batch(const h4b_model* m, const h4b_batch_state* s, cudaStream_t stre
     if (rc) return rc;
     const int B = s->batch, H = m->hidden, I = m->intermediate, d = m->head_dim;
     const int q_size = m->heads * d, kv_size = m->kv_heads * d, qkv_rows = q_size + 2 * kv_size;
+    // split-K room: gemm_acc holds B rows of max(qkv rows, hidden) int32
+    const int acc_rows = std::max(m->heads * m->head_dim + 2 * m->kv_heads * m->head_dim, m->hidden);
     auto gemm = [&](const uint8_t* w, const float* ws, float* out, int rows, int width) {
         GemmArgs g{s->x8, s->act_scale, s->act_sum, w, ws, out, B, rows, width};
+        g.split_acc = rows <= acc_rows ? s->gemm_acc : nullptr;
         return launch_int4_gemm(g, stream);
     };
     auto norm_quant = [&](const float* gamma) {

@@ -33,6 +33,10 @@ struct GemmArgs {
     float* out;             // [M][N]
     int M, N, K;
     int32_t* out_i32 = nullptr;  // when set: the exact int32 sums [M][N] instead of `out`
+    // tcgen05 split-K (only with a float `out`): when set, [M][N] int32 zeros
+    // the K slices are added into (exact, in any order); a finalize kernel
+    // applies the epilogue and leaves the buffer zero again.
+    int32_t* split_acc = nullptr;
 };
 
 // cp.async with a source size: bytes past src_bytes are zero-filled.

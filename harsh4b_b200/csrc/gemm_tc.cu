@@ -66,6 +66,7 @@ struct TcArgs {
     float* out;              // [M][N]
     int M, N, K;
     int32_t* out_i32;        // when set: the exact int32 sums [M][N] instead of `out`
+    int32_t* split_acc;      // split-K (gridDim.z > 1): K slices add their int32 sums here
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -150,7 +151,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * kTcRows, m0 = blockIdx.y * TOK;
-    const int steps = g.K / kTcK;
+    // this CTA's K slice (split-K over gridDim.z): steps [kbeg, kbeg + steps)
+    const int all_steps = g.K / kTcK;
+    const int kbeg = static_cast<int>(static_cast<long long>(blockIdx.z) * all_steps / gridDim.z);
+    const int steps = static_cast<int>(static_cast<long long>(blockIdx.z + 1) * all_steps / gridDim.z) - kbeg;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; ++s) {
@@ -197,8 +201,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&full[s], C::kPackedBytes + C::kBBytes);
-                    tma_load_2d(stage(s) + C::kPackedOff, &wmap, it * (kTcK / 2), n0, &full[s]);
-                    tma_load_2d(stage(s) + C::kBOff, &xmap, it * kTcK, m0, &full[s]);
+                    tma_load_2d(stage(s) + C::kPackedOff, &wmap, (kbeg + it) * (kTcK / 2), n0, &full[s]);
+                    tma_load_2d(stage(s) + C::kBOff, &xmap, (kbeg + it) * kTcK, m0, &full[s]);
                     issued = it + 1;
                 }
             }
@@ -276,7 +280,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int j = 0; j < 16; ++j) {
                     const int m = m0 + c0 + j;
                     if (m < g.M) {
-                        if (g.out_i32)
+                        if (g.split_acc)
+                            atomicAdd(g.split_acc + static_cast<size_t>(m) * g.N + row, static_cast<int>(v[j]));
+                        else if (g.out_i32)
                             g.out_i32[static_cast<size_t>(m) * g.N + row] = static_cast<int>(v[j]);
                         else
                             g.out[static_cast<size_t>(m) * g.N + row] =
@@ -364,6 +370,19 @@ bool byte_matrix_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_
     return true;
 }
 
+// out[m][n] = float(acc) * act_scale[m] * w_scale[n] (the GEMM epilogue's
+// order) from the split-K sums, which it leaves zero for the next GEMM.
+__global__ void split_finalize_kernel(int32_t* acc, const float* act_scale, const float* w_scale, float* out, int M,
+                                      int N) {
+    const long long total = static_cast<long long>(M) * N;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int m = static_cast<int>(i / N), n = static_cast<int>(i - static_cast<long long>(m) * N);
+        out[i] = __fmul_rn(__fmul_rn(static_cast<float>(acc[i]), act_scale[m]), w_scale[n]);
+        acc[i] = 0;
+    }
+}
+
 bool tc_gemm_supported(const GemmArgs& g) {
     return g.N % kTcRows == 0 && g.K % kTcK == 0 && (reinterpret_cast<uintptr_t>(g.w) & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(g.x) & 15) == 0 && tensor_map_encoder() != nullptr;
@@ -387,10 +406,24 @@ int launch_tc(const GemmArgs& g, cudaStream_t stream) {
     if (!byte_matrix_map(&wmap, g.w, static_cast<uint64_t>(g.K) / 2, g.N, kTcK / 2, kTcRows, false) ||
         !byte_matrix_map(&xmap, g.x, g.K, g.M, kTcK, TOK, true))
         return H4B_EUNSUPPORTED;
-    const TcArgs a{g.act_scale, g.w_scale, g.out, g.M, g.N, g.K, g.out_i32};
-    const dim3 grid(g.N / kTcRows, (g.M + TOK - 1) / TOK);
+    // Few output tiles (o / down / qkv at M <= 64 give 20-48 of them): split K
+    // so the grid fills the SMs, each slice at least 4 k-steps, the int32
+    // sums added in the caller's zeroed buffer and finalised below.
+    const int tiles = (g.N / kTcRows) * ((g.M + TOK - 1) / TOK);
+    const int steps = g.K / kTcK;
+    int ksplit = 1;
+    if (g.split_acc && !g.out_i32 && tiles < sm_count() / 2)
+        ksplit = std::max(1, std::min(sm_count() / tiles, steps / 4));
+    const TcArgs a{g.act_scale, g.w_scale, g.out, g.M, g.N, g.K, g.out_i32, ksplit > 1 ? g.split_acc : nullptr};
+    const dim3 grid(g.N / kTcRows, (g.M + TOK - 1) / TOK, ksplit);
     int4_gemm_tc_kernel<TOK><<<grid, kTcThreads, C::kSmem, stream>>>(wmap, xmap, a);
     H4B_CUDA_TRY(cudaGetLastError());
+    if (ksplit > 1) {
+        const long long n = static_cast<long long>(g.M) * g.N;
+        split_finalize_kernel<<<static_cast<int>(std::min<long long>((n + 255) / 256, 8ll * sm_count())), 256, 0,
+                                stream>>>(g.split_acc, g.act_scale, g.w_scale, g.out, g.M, g.N);
+        H4B_CUDA_TRY(cudaGetLastError());
+    }
     return 0;
 }
 

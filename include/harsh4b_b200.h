@@ -277,6 +277,8 @@ typedef struct h4b_batch_state {
     float *qkv, *attended, *proj, *gate_up, *act, *logits;
     float *attn_partials;
     int *attn_counters;
+    int32_t *gemm_acc;  /* optional: [batch][(heads + 2 kv_heads) * head_dim] int32 zeros for split-K GEMMs
+                           (the o, down and qkv projections at small batch); left zero after every step */
 } h4b_batch_state;
 
 int h4b_validate_batch(const h4b_model *model, const h4b_batch_state *state);
