@@ -183,9 +183,11 @@ def body_gemv_roofline(torch, model, state, peak_gbs) -> dict:
             "lm_head_gbs": round(head_bytes / head_s / 1e9, 1), "lm_head_us": round(head_s * 1e6, 2)}
 
 
-def cpu_baseline(checkpoint, prompt, budget_s=20.0) -> dict:
-    """The oracle (restated reference CPU path) on this host's cores: decode
-    tokens after a short prefill until ~budget_s of decode work is done."""
+def oracle_decode_timing(checkpoint, prompt, warmup: int, steps: int) -> dict:
+    """The reference's CPU decode as restated by the oracle, on all host
+    cores: the prompt fed untimed (all of it unless that would take more
+    than ~90 s here), `warmup` untimed greedy tokens, then `steps` timed
+    greedy tokens -- the same contexts as the GPU arm's timed steps."""
     import oracle
 
     threads = oracle.configure_threads(os.cpu_count())
@@ -193,25 +195,32 @@ def cpu_baseline(checkpoint, prompt, budget_s=20.0) -> dict:
     from _models import oracle_model
 
     model = oracle_model(checkpoint)
-    prefill = 8
-    state = model.new_state(prefill + 256)
-    for token in prompt[:prefill]:
+    state = model.new_state(len(prompt) + warmup + steps + 1)
+    t0 = time.perf_counter()
+    logits = model.forward_token(int(prompt[0]), state)
+    per_token = time.perf_counter() - t0
+    prefill = min(len(prompt), max(1, int(90.0 / max(per_token, 1e-3))))
+    for token in prompt[1:prefill]:
         logits = model.forward_token(int(token), state)
     token = int(logits.argmax())
-    # two untimed decode tokens (the reference excludes warm-up tokens too)
-    for _ in range(2):
+    for _ in range(warmup):
         token = int(model.forward_token(token, state).argmax())
-    times = []
     started = time.perf_counter()
-    while time.perf_counter() - started < budget_s and len(times) < 200:
-        t0 = time.perf_counter()
+    for _ in range(steps):
         token = int(model.forward_token(token, state).argmax())
-        times.append(time.perf_counter() - t0)
-    value = len(times) / sum(times)
-    return {"value": round(value, 3), "unit": "tok/s", "cores": oracle.max_threads(), "kind": "port",
-            "sample": f"{len(times)} greedy decode tokens at batch 1 after an {prefill}-token prefill "
-                      f"(context {prefill + 3}..{prefill + 2 + len(times)}), config-0 weights, "
-                      f"{threads} OpenMP threads", "cpu": cpu_model()}
+    elapsed = time.perf_counter() - started
+    return {"value": round(steps / elapsed, 3), "elapsed": elapsed, "prefill": prefill, "threads": threads,
+            "cores": oracle.max_threads(),
+            "sample": f"{steps} greedy decode tokens at batch 1 after a {prefill}-token prefill and {warmup} "
+                      f"warm-up tokens (context {prefill + warmup + 1}..{prefill + warmup + steps}), "
+                      f"config-0 weights, {threads} OpenMP threads"}
+
+
+def cpu_baseline(checkpoint, prompt, warmup: int, steps: int) -> dict:
+    """The oracle on this host's cores over the GPU arm's own timed steps."""
+    t = oracle_decode_timing(checkpoint, prompt, warmup, steps)
+    return {"value": t["value"], "unit": "tok/s", "cores": t["cores"], "kind": "port", "sample": t["sample"],
+            "cpu": cpu_model()}
 
 
 def cpu_model() -> str:
@@ -229,35 +238,11 @@ def run_reference(args, rank) -> int:
         return 0
     from harsh4b_b200.synthetic import qwen3_4b_config, synthetic_checkpoint, synthetic_prompt
 
-    import oracle
-
-    oracle.configure_threads(os.cpu_count())
-    sys.path.insert(0, str(ROOT / "tests"))
-    from _models import oracle_model
-
     config = qwen3_4b_config()
     checkpoint = synthetic_checkpoint(config, seed=args.seed)
     prompt = synthetic_prompt(config, PROMPT, seed=args.seed)
-    model = oracle_model(checkpoint)
-    state = model.new_state(PROMPT + args.warmup + args.steps + 1)
-    # Bound the untimed prefill: all 128 prompt tokens unless that would take
-    # more than ~90 s on this host (then the context starts shorter).
-    t0 = time.perf_counter()
-    logits = model.forward_token(int(prompt[0]), state)
-    per_token = time.perf_counter() - t0
-    prefill = min(PROMPT, max(1, int(90.0 / max(per_token, 1e-3))))
-    for token in prompt[1:prefill]:
-        logits = model.forward_token(int(token), state)
-    token = int(logits.argmax())
-    for _ in range(args.warmup):
-        token = int(model.forward_token(token, state).argmax())
-    started = time.perf_counter()
-    for _ in range(args.steps):
-        token = int(model.forward_token(token, state).argmax())
-    elapsed = time.perf_counter() - started
-    value = args.steps / elapsed
-    sample = (f"{args.steps} greedy decode tokens at batch 1 after a {prefill}-token prefill and "
-              f"{args.warmup} warm-up tokens, config-0 weights (seed {args.seed})")
+    t = oracle_decode_timing(checkpoint, prompt, args.warmup, args.steps)
+    value, elapsed, prefill, sample = t["value"], t["elapsed"], t["prefill"], t["sample"]
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1000, 3), "higher_is_better": True,
@@ -265,7 +250,7 @@ def run_reference(args, rank) -> int:
         "config": {"workload": "config0: Qwen3-4B int4 synthetic checkpoint, 128-token random prompt, "
                                "batch-1 greedy decode", "prompt": prefill, "kv_dtype": "float32",
                    "parallelism": "replicas"},
-        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": oracle.max_threads(), "kind": "port",
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": t["cores"], "kind": "port",
                          "sample": sample, "cpu": cpu_model()},
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -392,7 +377,7 @@ def run_ours(args, rank, world, local_rank, dist) -> int:
     if tp_record is not None:
         line["tp"] = tp_record
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(checkpoint, prompt)
+        line["cpu_baseline"] = cpu_baseline(checkpoint, prompt, args.warmup, args.steps)
     print(json.dumps(line), flush=True)
     return 0
 
