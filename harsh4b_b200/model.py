@@ -19,7 +19,7 @@ import torch
 
 from ._lib import (BatchStateDesc, ModelDesc, PrefillScratchDesc, StateDesc, check, device_status, lib,
                    STATUS_WAIT_TIMEOUT)
-from .cache import Checkpoint, read_cache
+from .cache import Checkpoint, norm_names, read_cache
 
 KV_DTYPES = {"float32": (0, torch.float32), "float16": (1, torch.float16)}
 MODES = ("persistent", "chain")
@@ -335,6 +335,11 @@ class CudaQwen:
     @classmethod
     def from_checkpoint(cls, checkpoint: Checkpoint, **kwargs) -> "CudaQwen":
         checkpoint.validate()
+        missing = [n for n in norm_names(checkpoint.config) if n not in checkpoint.norms]
+        if missing:
+            raise ValueError(f"no norm vectors for {missing[0]} (and {len(missing) - 1} more): a cache built by the "
+                             "reference keeps them in the LATTICE checkpoint -- build the model with "
+                             "harsh4b_b200.lattice.build_b200_model(checkpoint) or fill Checkpoint.norms")
         layers = [checkpoint.layer(i) for i in range(int(checkpoint.config["num_hidden_layers"]))]
         return cls(checkpoint.config, layers, checkpoint.embedding, checkpoint.embedding_scales,
                    checkpoint.norms["model.norm.weight"], **kwargs)

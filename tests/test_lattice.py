@@ -91,3 +91,20 @@ def test_cache_identity_matches_reference(tmp_path):
     path = tmp_path / "model.lat.pt"
     path.write_bytes(b"checkpoint bytes")
     assert cache_identity(path) == cpu_lightspark._cache_identity(path)
+
+
+def test_reference_style_cache_without_norms_is_rejected_clearly(tmp_path):
+    """A cache written the way the reference writes it (no norm vectors)
+    cannot build a model on its own; the error names the way that works."""
+    from harsh4b_b200.cache import read_cache, write_cache
+    from harsh4b_b200.synthetic import synthetic_checkpoint, tiny_config
+
+    checkpoint = synthetic_checkpoint(tiny_config(num_hidden_layers=1), seed=1)
+    checkpoint.norms = {}
+    write_cache(tmp_path, checkpoint)
+    loaded = read_cache(tmp_path)
+    assert loaded.norms == {}
+    from harsh4b_b200.model import CudaQwen
+
+    with pytest.raises(ValueError, match="build_b200_model"):
+        CudaQwen.from_checkpoint(loaded)
