@@ -72,6 +72,8 @@ def parse_args():
                         help="attention workload: batch x context [x splits] cases")
     parser.add_argument("--batch", type=int, default=64, help="batch workload: sequences")
     parser.add_argument("--prompt-len", type=int, default=2048, help="batch / prefill workloads: prompt tokens")
+    parser.add_argument("--prefill-attention", choices=("tensor", "exact"), default="tensor",
+                        help="prefill workload: tcgen05 attention (tolerance) or the decode-order fp32 kernel")
     parser.add_argument("--context", type=int, default=4096, help="tp workload: context before decoding")
     parser.add_argument("--layers", type=int, default=None,
                         help="override the layer count (a smaller model for profiling captures; not the headline)")
@@ -706,7 +708,7 @@ def run_prefill(args) -> int:
     state = model.new_state(P + 1)
     for _ in range(args.warmup):
         state.reset()
-        model.prefill(ids, state, max_tokens=P)
+        model.prefill(ids, state, max_tokens=P, attention=args.prefill_attention)
     times = []
     with ClockSampler(torch.cuda.current_device()) as clocks:
         for _ in range(args.steps):
@@ -714,7 +716,7 @@ def run_prefill(args) -> int:
             start, end = _event_pair(torch)
             with torch.cuda.stream(state.stream):
                 start.record(state.stream)
-            model.prefill(ids, state, max_tokens=P)
+            model.prefill(ids, state, max_tokens=P, attention=args.prefill_attention)
             with torch.cuda.stream(state.stream):
                 end.record(state.stream)
             torch.cuda.synchronize()
@@ -732,7 +734,7 @@ def run_prefill(args) -> int:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4xint8", "data": "synthetic",
         "config": {"workload": f"config4 prefill: {P}-token random prompt, one h4b_prefill call",
                    "prompt": P, "kv_dtype": args.kv_dtype, "layers": model.n_layers,
-                   "l2": "inputs larger than L2"},
+                   "attention": args.prefill_attention, "l2": "inputs larger than L2"},
         "roofline": {"bound": "tensor", "kernel": "whole prefill (int8 ops of every GEMM)",
                      "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOP/s",
                      "frac": round(achieved / int8_peak, 4), "ops_per_step": int(ops_per_prefill),

@@ -54,7 +54,7 @@ class PrefillScratchDesc(ctypes.Structure):
 
     _fields_ = [("max_tokens", _i32), ("attn_queries", _i32), ("attn_splits", _i32)] + [
         (n, _vp) for n in ("x", "x8", "act_scale", "act_sum", "qkv", "attended", "gate_up", "act", "proj", "tokens",
-                           "positions", "attn_partials", "attn_counters")]
+                           "positions", "attn_partials", "attn_counters")] + [("attn_kernel", _i32)]
 
 
 class LatticeProjectionDesc(ctypes.Structure):

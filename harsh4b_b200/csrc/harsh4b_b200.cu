@@ -7,6 +7,7 @@
 #include "sample.cu"
 #include "gemm.cu"
 #include "gemm_tc.cu"
+#include "prefill_tc.cu"
 #include "batch.cu"
 #include "prefill.cu"
 #include "tp.cu"

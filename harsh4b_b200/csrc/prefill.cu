@@ -185,6 +185,7 @@ int validate_prefill(const h4b_model* m, const h4b_state* s, const h4b_prefill_s
     for (const void* q : required)
         if (!q || (reinterpret_cast<uintptr_t>(q) & 15)) return H4B_EINVAL;
     if (p->attn_splits > 1 && (!p->attn_partials || !p->attn_counters)) return H4B_EINVAL;
+    if (p->attn_kernel != H4B_PREFILL_ATTN_EXACT && p->attn_kernel != H4B_PREFILL_ATTN_TENSOR) return H4B_EINVAL;
     return 0;
 }
 
@@ -248,6 +249,11 @@ struct PrefillRun {
                 m->norm_k + static_cast<size_t>(l) * d, m->rope_cos, m->rope_sin, m->eps, p->positions,
                 reinterpret_cast<__half*>(kc), reinterpret_cast<__half*>(vc), head_stride, d);
         H4B_CUDA_TRY(cudaGetLastError());
+        if (p->attn_splits == 1 && p->attn_kernel == H4B_PREFILL_ATTN_TENSOR &&
+            prefill_tc_supported(s->kv_dtype, d, m->heads / m->kv_heads))
+            return launch_prefill_attention_tc(p->qkv, qkv_rows, reinterpret_cast<const __half*>(kc),
+                                               reinterpret_cast<const __half*>(vc), m->kv_heads, s->capacity,
+                                               p->positions, count, p->attended, q_size, stream);
         if (p->attn_splits == 1 && m->heads / m->kv_heads == kPrefillGroups) {
             // one split per query: query blocks share their K/V sub-tiles
             int rc2 = prefill_block_opt_in();

@@ -23,6 +23,8 @@ from .cache import Checkpoint, norm_names, read_cache
 
 KV_DTYPES = {"float32": (0, torch.float32), "float16": (1, torch.float16)}
 MODES = ("persistent", "chain")
+# prefill attention kernels (h4b_prefill_scratch.attn_kernel)
+PREFILL_ATTENTION = {"exact": 0, "tensor": 1}
 PERSISTENT_ATTN_CHUNK = 32  # tokens per attention split in the persistent step (persistent.cu)
 SWIGLU_BLOCK = 4  # rows per gate/up interleave block (matches the kernel)
 
@@ -389,12 +391,19 @@ class CudaQwen:
         return state.logits
 
     def prefill(self, token_ids, state: CudaDecodeState, max_tokens: int = 2048,
-                attn_splits: int = 1) -> torch.Tensor:
+                attn_splits: int = 1, attention: str = "tensor") -> torch.Tensor:
         """Feed a prompt in one pass per `max_tokens` rows (h4b_prefill): the
         body projections run as tensor-core GEMMs over the prompt rows, each
         prompt query's attention in `attn_splits` context splits. Returns the
-        last token's logits; the state then stands where forward_token over
-        the same ids with that split count leaves it, bit for bit."""
+        last token's logits.
+
+        attention="exact": the state then stands where forward_token over the
+        same ids with that split count leaves it, bit for bit.
+        attention="tensor" (one split, fp16 cache, head_dim 128, 4 q heads
+        per kv head; otherwise as "exact"): tcgen05 attention with split fp16
+        operands, within the 1e-3 relative tolerance of the fp32 path."""
+        if attention not in PREFILL_ATTENTION:
+            raise ValueError(f"attention must be one of {sorted(PREFILL_ATTENTION)}")
         ids = np.asarray([int(t) for t in token_ids], dtype=np.int32)
         if ids.size == 0:
             raise ValueError("empty prompt")
@@ -408,6 +417,7 @@ class CudaQwen:
         scratch = self._prefill_scratch
         if scratch is None or scratch.max_tokens < rows or scratch.splits != int(attn_splits):
             scratch = self._prefill_scratch = PrefillScratch(self, rows, int(attn_splits))
+        scratch.desc.attn_kernel = PREFILL_ATTENTION[attention]
         current = torch.cuda.current_stream(self.device)
         state.stream.wait_stream(current)
         with torch.cuda.stream(state.stream):

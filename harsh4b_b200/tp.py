@@ -258,17 +258,21 @@ class TensorParallelQwen:
         self._best[1:2].copy_(local + self.vocab_offset)
         dist.all_gather_into_tensor(self._gathered, self._best, group=self.group)
 
-    def prefill(self, token_ids, state, max_tokens: int = 2048, attn_splits: int = 1):
+    def prefill(self, token_ids, state, max_tokens: int = 2048, attn_splits: int = 1, attention: str = "tensor"):
         """Feed a prompt on every rank (all ranks pass the same ids): the
         sharded h4b_prefill_tp_stage sequence with NCCL all-reduces of the
         per-row absmax (MAX) and of the o / down int32 row sums (SUM)
         between the stages. Returns (greedy token, local logits slice) of the
-        last prompt row; the state then stands where forward_token over the
-        same ids with `attn_splits` splits per prompt query leaves it."""
+        last prompt row. With attention="exact" the state then stands where
+        forward_token over the same ids with `attn_splits` splits per prompt
+        query leaves it; "tensor" is CudaQwen.prefill's tensor-core attention."""
         import ctypes
 
         from ._lib import check, lib
-        from .model import PrefillScratch
+        from .model import PREFILL_ATTENTION, PrefillScratch
+
+        if attention not in PREFILL_ATTENTION:
+            raise ValueError(f"attention must be one of {sorted(PREFILL_ATTENTION)}")
 
         torch, dist, m = self.torch, self.dist, self.model
         ids = np.asarray([int(t) for t in token_ids], dtype=np.int32)
@@ -282,6 +286,7 @@ class TensorParallelQwen:
         scratch = m._prefill_scratch
         if scratch is None or scratch.max_tokens < rows or scratch.splits != int(attn_splits):
             scratch = m._prefill_scratch = PrefillScratch(m, rows, int(attn_splits))
+        scratch.desc.attn_kernel = PREFILL_ATTENTION[attention]
         absmax = torch.empty(scratch.max_tokens, dtype=torch.float32, device=self.device)
         acc = torch.empty(scratch.max_tokens, m.hidden, dtype=torch.int32, device=self.device)
         stream = torch.cuda.current_stream(self.device)

@@ -352,7 +352,17 @@ typedef struct h4b_prefill_scratch {
     int32_t *positions; /* [max_tokens] */
     float *attn_partials;
     int *attn_counters;
+    /* H4B_PREFILL_ATTN_EXACT (0): fp32 attention in the decode kernel's
+     * order, every row bit-identical to a decode step. H4B_PREFILL_ATTN_TENSOR
+     * (1): tcgen05 tensor-core attention with split fp16 operands (fp32
+     * outputs within the 1e-3 relative tolerance, not bit-identical) where
+     * the cache is fp16, head_dim 128 and 4 q heads share a kv head, else as
+     * 0. Used when attn_splits == 1. */
+    int attn_kernel;
 } h4b_prefill_scratch;
+
+#define H4B_PREFILL_ATTN_EXACT 0
+#define H4B_PREFILL_ATTN_TENSOR 1
 
 /* Feeds scratch->tokens[0, count) to the session at positions *position ..
  * *position + count - 1 (LiteSparkQwen.forward_token called count times,
@@ -361,7 +371,9 @@ typedef struct h4b_prefill_scratch {
  * over all prompt rows. Afterwards state->logits holds the last row's
  * logits, next_token/token its greedy token and *position has advanced by
  * count -- bit for bit what count h4b_decode_step calls leave when the
- * session's attention splits equal scratch->attn_splits. */
+ * session's attention splits equal scratch->attn_splits and
+ * scratch->attn_kernel is H4B_PREFILL_ATTN_EXACT (with the tensor-core
+ * attention, within its tolerance). */
 int h4b_prefill(const h4b_model *model, const h4b_state *state, const h4b_prefill_scratch *scratch, int count,
                 void *stream);
 

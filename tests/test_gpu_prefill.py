@@ -27,7 +27,7 @@ def _oracle_run(reference, prompt, steps):
 
 def _cuda_run(model, prompt, steps, splits, max_tokens=2048, prefill_splits=None):
     state = model.new_state(len(prompt) + steps, attn_splits=splits)
-    last = model.prefill(prompt, state, max_tokens=max_tokens,
+    last = model.prefill(prompt, state, max_tokens=max_tokens, attention="exact",
                          attn_splits=splits if prefill_splits is None else prefill_splits).cpu().numpy().copy()
     assert state.position == len(prompt)
     greedy, after = [], []

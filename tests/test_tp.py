@@ -216,7 +216,7 @@ def _tp_prefill_rank(rank, world, port, results):
         model = TensorParallelQwen(ck, kv_dtype="float16", attn_splits=16, comm="nccl")
         prompt = synthetic_prompt(config, PREFILL, seed=SEED)
         state = model.new_state(PREFILL + STEPS)
-        token, local = model.prefill(prompt, state, max_tokens=PREFILL_CHUNK)
+        token, local = model.prefill(prompt, state, max_tokens=PREFILL_CHUNK, attention="exact")
         rows, greedy = [], [token]
 
         def gather(local):
