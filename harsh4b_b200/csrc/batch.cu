@@ -97,7 +97,7 @@ __global__ void batch_swiglu_kernel(const float* gate_up, int I, int B, float* a
     const int blk = p / kSwigluBlock, j = p % kSwigluBlock;
     const float* row = gate_up + b * 2 * I;
     const float g = row[2 * kSwigluBlock * blk + j], u = row[2 * kSwigluBlock * blk + kSwigluBlock + j];
-    act[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_cw(-g))), u);
+    act[i] = swiglu_one(g, u);
 }
 
 // Greedy token per row (first maximum, numpy argmax semantics).
@@ -186,18 +186,14 @@ int decode_batch(const h4b_model* m, const h4b_batch_state* s, cudaStream_t stre
     const int q_size = m->heads * d, kv_size = m->kv_heads * d, qkv_rows = q_size + 2 * kv_size;
     // split-K room: gemm_acc holds B rows of max(qkv rows, hidden) int32
     const int acc_rows = std::max(m->heads * m->head_dim + 2 * m->kv_heads * m->head_dim, m->hidden);
-    auto gemm = [&](const uint8_t* w, const float* ws, float* out, int rows, int width) {
+    auto gemm = [&](const uint8_t* w, const float* ws, float* out, int rows, int width, bool residual = false) {
         GemmArgs g{s->x8, s->act_scale, s->act_sum, w, ws, out, B, rows, width};
         g.split_acc = rows <= acc_rows ? s->gemm_acc : nullptr;
+        g.residual = residual;
         return launch_int4_gemm(g, stream);
     };
     auto norm_quant = [&](const float* gamma) {
         batch_rmsnorm_quant_kernel<<<B, 256, 0, stream>>>(s->x, gamma, m->eps, H, s->x8, s->act_scale, s->act_sum);
-        return cudaGetLastError() == cudaSuccess ? 0 : H4B_EINVAL;
-    };
-    auto add_x = [&]() {
-        const int n = B * H;
-        add_kernel<<<(n + 255) / 256, 256, 0, stream>>>(s->x, s->proj, n);
         return cudaGetLastError() == cudaSuccess ? 0 : H4B_EINVAL;
     };
     batch_embed_kernel<<<B, 256, 0, stream>>>(s->tokens, m->w_embed, m->s_embed, m->vocab, H, s->x);
@@ -208,25 +204,23 @@ int decode_batch(const h4b_model* m, const h4b_batch_state* s, cudaStream_t stre
                        s->qkv, qkv_rows, H)))
             return rc;
         if ((rc = batch_attention(m, s, l, stream))) return rc;
-        quantize_rows_kernel<<<B, 256, 0, stream>>>(s->attended, q_size, s->x8, s->act_scale, s->act_sum);
-        H4B_CUDA_TRY(cudaGetLastError());
-        if ((rc = gemm(m->w_o + static_cast<size_t>(l) * H * (q_size / 2), m->s_o + static_cast<size_t>(l) * H, s->proj,
-                       H, q_size)))
+        // residual adds in the o / down GEMM epilogues, SwiGLU in the
+        // quantisation of its rows (the separate kernels' operations)
+        if ((rc = launch_quantize_rows<false>(s->attended, q_size, B, s->x8, s->act_scale, s->act_sum, nullptr,
+                                              stream)))
             return rc;
-        if ((rc = add_x())) return rc;
+        if ((rc = gemm(m->w_o + static_cast<size_t>(l) * H * (q_size / 2), m->s_o + static_cast<size_t>(l) * H, s->x,
+                       H, q_size, true)))
+            return rc;
         if ((rc = norm_quant(m->norm_post + static_cast<size_t>(l) * H))) return rc;
         if ((rc = gemm(m->w_gate_up + static_cast<size_t>(l) * 2 * I * (H / 2),
                        m->s_gate_up + static_cast<size_t>(l) * 2 * I, s->gate_up, 2 * I, H)))
             return rc;
-        const long long n_act = static_cast<long long>(B) * I;
-        batch_swiglu_kernel<<<static_cast<int>((n_act + 255) / 256), 256, 0, stream>>>(s->gate_up, I, B, s->act);
-        H4B_CUDA_TRY(cudaGetLastError());
-        quantize_rows_kernel<<<B, 256, 0, stream>>>(s->act, I, s->x8, s->act_scale, s->act_sum);
-        H4B_CUDA_TRY(cudaGetLastError());
-        if ((rc = gemm(m->w_down + static_cast<size_t>(l) * H * (I / 2), m->s_down + static_cast<size_t>(l) * H, s->proj,
-                       H, I)))
+        if ((rc = launch_quantize_rows<true>(s->gate_up, I, B, s->x8, s->act_scale, s->act_sum, s->act, stream)))
             return rc;
-        if ((rc = add_x())) return rc;
+        if ((rc = gemm(m->w_down + static_cast<size_t>(l) * H * (I / 2), m->s_down + static_cast<size_t>(l) * H, s->x,
+                       H, I, true)))
+            return rc;
     }
     if ((rc = norm_quant(m->norm_final))) return rc;
     if ((rc = gemm(m->w_embed, m->s_embed, s->logits, m->vocab, H))) return rc;

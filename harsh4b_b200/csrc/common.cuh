@@ -342,6 +342,11 @@ __device__ __forceinline__ float exp_cw(float x) {
     return __fmul_rn(p, __int_as_float((static_cast<int>(n) + 127) << 23));
 }
 
+// SiLU(gate) * up in the order every SwiGLU of this library uses.
+__device__ __forceinline__ float swiglu_one(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_cw(-g))), u);
+}
+
 // Argmax key: larger value wins, ties go to the smaller index (numpy's
 // first-occurrence rule). Values are mapped to an order-preserving uint.
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {

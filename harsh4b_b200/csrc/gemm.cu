@@ -37,6 +37,9 @@ struct GemmArgs {
     // the K slices are added into (exact, in any order); a finalize kernel
     // applies the epilogue and leaves the buffer zero again.
     int32_t* split_acc = nullptr;
+    // with a float `out`: out[m][n] = out[m][n] + value (the residual add,
+    // x + proj in that order) instead of out[m][n] = value
+    bool residual = false;
 };
 
 // cp.async with a source size: bytes past src_bytes are zero-filled.
@@ -142,8 +145,10 @@ __global__ void __launch_bounds__(256) int4_gemm_kernel(const GemmArgs g) {
             }
             const float as = g.act_scale[m];
             float* orow = g.out + static_cast<size_t>(m) * g.N;
-            orow[r0] = __fmul_rn(__fmul_rn(static_cast<float>(acc[j][c] + bias), as), ws0);
-            orow[r0 + 8] = __fmul_rn(__fmul_rn(static_cast<float>(acc[j][2 + c] + bias), as), ws8);
+            const float v0 = __fmul_rn(__fmul_rn(static_cast<float>(acc[j][c] + bias), as), ws0);
+            const float v8 = __fmul_rn(__fmul_rn(static_cast<float>(acc[j][2 + c] + bias), as), ws8);
+            orow[r0] = g.residual ? __fadd_rn(orow[r0], v0) : v0;
+            orow[r0 + 8] = g.residual ? __fadd_rn(orow[r0 + 8], v8) : v8;
         }
     }
 }
@@ -188,6 +193,112 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* v, int 
         sums[blockIdx.x] = t;
         scales[blockIdx.x] = dequant_scale(m);
     }
+}
+
+// quantize_rows_kernel's result, bit for bit, with the row read once into
+// registers (float4 loads, kGroups groups of 4 per thread). With kSwiglu the
+// row is act = silu(gate) * up from the interleaved gate/up row
+// (batch_swiglu_kernel's arithmetic; [gate x4][up x4] per group), and act
+// itself is never stored. The maximum and the code sum are order-free.
+template <int kThreads, int kGroups, bool kSwiglu>
+__global__ void __launch_bounds__(kThreads) quantize_rows_reg_kernel(const float* v, int K, int8_t* q,
+                                                                    float* scales, int32_t* sums) {
+    __shared__ float red[kThreads / 32];
+    __shared__ int ired[kThreads / 32];
+    const int groups = K / 4;
+    const float4* row = reinterpret_cast<const float4*>(v + static_cast<size_t>(blockIdx.x) * (kSwiglu ? 2 : 1) * K);
+    float4 a[kGroups];
+    float mx = 0.f;
+#pragma unroll
+    for (int k = 0; k < kGroups; ++k) {
+        const int gi = threadIdx.x + k * kThreads;
+        a[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (gi < groups) {
+            if constexpr (kSwiglu) {
+                const float4 g = row[2 * gi], u = row[2 * gi + 1];
+                a[k] = make_float4(swiglu_one(g.x, u.x), swiglu_one(g.y, u.y), swiglu_one(g.z, u.z),
+                                   swiglu_one(g.w, u.w));
+            } else {
+                a[k] = row[gi];
+            }
+            mx = fmaxf(fmaxf(mx, fabsf(a[k].x)), fmaxf(fabsf(a[k].y), fmaxf(fabsf(a[k].z), fabsf(a[k].w))));
+        }
+    }
+    mx = warp_max(mx);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    float m = red[0];
+#pragma unroll
+    for (int w = 1; w < kThreads / 32; ++w) m = fmaxf(m, red[w]);
+    const float qs = quant_multiplier(m);
+    int s = 0;
+    uint32_t* qrow = reinterpret_cast<uint32_t*>(q + static_cast<size_t>(blockIdx.x) * K);
+#pragma unroll
+    for (int k = 0; k < kGroups; ++k) {
+        const int gi = threadIdx.x + k * kThreads;
+        if (gi < groups) {
+            const int c0 = quantize_one(a[k].x, qs), c1 = quantize_one(a[k].y, qs);
+            const int c2 = quantize_one(a[k].z, qs), c3 = quantize_one(a[k].w, qs);
+            qrow[gi] = (static_cast<uint32_t>(c0) & 0xFFu) | ((static_cast<uint32_t>(c1) & 0xFFu) << 8) |
+                       ((static_cast<uint32_t>(c2) & 0xFFu) << 16) | (static_cast<uint32_t>(c3) << 24);
+            s += c0 + c1 + c2 + c3;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) ired[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int t = 0;
+        for (int w = 0; w < kThreads / 32; ++w) t += ired[w];
+        sums[blockIdx.x] = t;
+        scales[blockIdx.x] = dequant_scale(m);
+    }
+}
+
+constexpr int kQuantThreads = 512, kQuantMaxGroups = 8;
+
+__global__ void batch_swiglu_kernel(const float* gate_up, int I, int B, float* act);  // batch.cu
+
+template <bool kSwiglu, int G>
+void launch_quantize_reg(const float* v, int K, int rows, int8_t* q, float* scales, int32_t* sums,
+                         cudaStream_t stream) {
+    quantize_rows_reg_kernel<kQuantThreads, G, kSwiglu><<<rows, kQuantThreads, 0, stream>>>(v, K, q, scales, sums);
+}
+
+// Per-row quantisation of `rows` rows of K values (kSwiglu: of the SwiGLU of
+// `rows` interleaved gate/up rows of 2K values) into q / scales / sums; the
+// register kernel when a row fits, else the general kernels (kSwiglu then
+// needs `act`, [rows][K], for the intermediate values).
+template <bool kSwiglu>
+int launch_quantize_rows(const float* v, int K, int rows, int8_t* q, float* scales, int32_t* sums, float* act,
+                         cudaStream_t stream) {
+    const int per = (K / 4 + kQuantThreads - 1) / kQuantThreads;
+    if (K % 4 == 0 && per <= kQuantMaxGroups && (reinterpret_cast<uintptr_t>(v) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(q) & 3) == 0) {
+        switch (per) {
+            case 0:
+            case 1: launch_quantize_reg<kSwiglu, 1>(v, K, rows, q, scales, sums, stream); break;
+            case 2: launch_quantize_reg<kSwiglu, 2>(v, K, rows, q, scales, sums, stream); break;
+            case 3: launch_quantize_reg<kSwiglu, 3>(v, K, rows, q, scales, sums, stream); break;
+            case 4: launch_quantize_reg<kSwiglu, 4>(v, K, rows, q, scales, sums, stream); break;
+            case 5: launch_quantize_reg<kSwiglu, 5>(v, K, rows, q, scales, sums, stream); break;
+            case 6: launch_quantize_reg<kSwiglu, 6>(v, K, rows, q, scales, sums, stream); break;
+            default: launch_quantize_reg<kSwiglu, 8>(v, K, rows, q, scales, sums, stream); break;
+        }
+        H4B_CUDA_TRY(cudaGetLastError());
+        return 0;
+    }
+    const float* src = v;
+    if constexpr (kSwiglu) {
+        if (!act) return H4B_EUNSUPPORTED;
+        const long long n = static_cast<long long>(rows) * K;
+        batch_swiglu_kernel<<<static_cast<int>((n + 255) / 256), 256, 0, stream>>>(v, K, rows, act);
+        src = act;
+    }
+    quantize_rows_kernel<<<rows, 256, 0, stream>>>(src, K, q, scales, sums);
+    H4B_CUDA_TRY(cudaGetLastError());
+    return 0;
 }
 
 int launch_int4_gemm_mma(const GemmArgs& g, cudaStream_t stream) {

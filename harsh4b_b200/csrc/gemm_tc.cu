@@ -67,6 +67,7 @@ struct TcArgs {
     int M, N, K;
     int32_t* out_i32;        // when set: the exact int32 sums [M][N] instead of `out`
     int32_t* split_acc;      // split-K (gridDim.z > 1): K slices add their int32 sums here
+    int residual;            // out[m][n] = out[m][n] + value instead of value
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -284,9 +285,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             atomicAdd(g.split_acc + static_cast<size_t>(m) * g.N + row, static_cast<int>(v[j]));
                         else if (g.out_i32)
                             g.out_i32[static_cast<size_t>(m) * g.N + row] = static_cast<int>(v[j]);
-                        else
-                            g.out[static_cast<size_t>(m) * g.N + row] =
+                        else {
+                            float* o = g.out + static_cast<size_t>(m) * g.N + row;
+                            const float value =
                                 __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[j])), g.act_scale[m]), ws);
+                            *o = g.residual ? __fadd_rn(*o, value) : value;
+                        }
                     }
                 }
             }
@@ -371,14 +375,16 @@ bool byte_matrix_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_
 }
 
 // out[m][n] = float(acc) * act_scale[m] * w_scale[n] (the GEMM epilogue's
-// order) from the split-K sums, which it leaves zero for the next GEMM.
+// order; with `residual`, added to out[m][n]) from the split-K sums, which it
+// leaves zero for the next GEMM.
 __global__ void split_finalize_kernel(int32_t* acc, const float* act_scale, const float* w_scale, float* out, int M,
-                                      int N) {
+                                      int N, int residual) {
     const long long total = static_cast<long long>(M) * N;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
         const int m = static_cast<int>(i / N), n = static_cast<int>(i - static_cast<long long>(m) * N);
-        out[i] = __fmul_rn(__fmul_rn(static_cast<float>(acc[i]), act_scale[m]), w_scale[n]);
+        const float value = __fmul_rn(__fmul_rn(static_cast<float>(acc[i]), act_scale[m]), w_scale[n]);
+        out[i] = residual ? __fadd_rn(out[i], value) : value;
         acc[i] = 0;
     }
 }
@@ -414,14 +420,16 @@ int launch_tc(const GemmArgs& g, cudaStream_t stream) {
     int ksplit = 1;
     if (g.split_acc && !g.out_i32 && tiles < sm_count() / 2)
         ksplit = std::max(1, std::min(sm_count() / tiles, steps / 4));
-    const TcArgs a{g.act_scale, g.w_scale, g.out, g.M, g.N, g.K, g.out_i32, ksplit > 1 ? g.split_acc : nullptr};
+    const TcArgs a{g.act_scale, g.w_scale, g.out, g.M, g.N, g.K, g.out_i32, ksplit > 1 ? g.split_acc : nullptr,
+                   g.residual ? 1 : 0};
     const dim3 grid(g.N / kTcRows, (g.M + TOK - 1) / TOK, ksplit);
     int4_gemm_tc_kernel<TOK><<<grid, kTcThreads, C::kSmem, stream>>>(wmap, xmap, a);
     H4B_CUDA_TRY(cudaGetLastError());
     if (ksplit > 1) {
         const long long n = static_cast<long long>(g.M) * g.N;
         split_finalize_kernel<<<static_cast<int>(std::min<long long>((n + 255) / 256, 8ll * sm_count())), 256, 0,
-                                stream>>>(g.split_acc, g.act_scale, g.w_scale, g.out, g.M, g.N);
+                                stream>>>(g.split_acc, g.act_scale, g.w_scale, g.out, g.M, g.N,
+                                         g.residual ? 1 : 0);
         H4B_CUDA_TRY(cudaGetLastError());
     }
     return 0;

@@ -33,16 +33,19 @@ __global__ void prefill_setup_kernel(const int32_t* position, int count, int cap
     if (blockIdx.x == 0 && threadIdx.x == 0) *argmax_key = 0ull;
 }
 
-// One warp per (prompt token, head): heads [0, q_heads) are queries,
-// [q_heads, q_heads + kv_heads) keys (+ the matching value row).
+// One warp per (prompt token, head), eight to a CTA: heads [0, q_heads)
+// are queries, [q_heads, q_heads + kv_heads) keys (+ the matching value row).
+constexpr int kRopeWarps = 8;
+
 template <typename KV>
-__global__ void __launch_bounds__(32) prefill_rope_append_kernel(float* qkv, int qkv_stride, int q_heads, int kv_heads,
-                                                                 const float* q_norm, const float* k_norm,
-                                                                 const float* rope_cos, const float* rope_sin,
-                                                                 float eps, const int32_t* positions, KV* kcache,
-                                                                 KV* vcache, long long head_stride,
-                                                                 long long time_stride) {
-    const int i = blockIdx.x, head = blockIdx.y, lane = threadIdx.x;
+__global__ void __launch_bounds__(32 * kRopeWarps) prefill_rope_append_kernel(
+    float* qkv, int qkv_stride, int q_heads, int kv_heads, const float* q_norm, const float* k_norm,
+    const float* rope_cos, const float* rope_sin, float eps, const int32_t* positions, int count, KV* kcache,
+    KV* vcache, long long head_stride, long long time_stride) {
+    const int heads = q_heads + kv_heads;
+    const long long w = static_cast<long long>(blockIdx.x) * kRopeWarps + (threadIdx.x >> 5);
+    if (w >= static_cast<long long>(count) * heads) return;
+    const int i = static_cast<int>(w / heads), head = static_cast<int>(w % heads), lane = threadIdx.x & 31;
     const int pos = positions[i];
     if (pos < 0) return;
     const float* cs = rope_cos + static_cast<long long>(pos) * (kHeadDim / 2);
@@ -198,20 +201,16 @@ struct PrefillRun {
     int count;
     cudaStream_t stream;
 
-    int gemm(const uint8_t* w, const float* ws, float* out, int rows, int width, int32_t* out_i32 = nullptr) const {
+    int gemm(const uint8_t* w, const float* ws, float* out, int rows, int width, int32_t* out_i32 = nullptr,
+             bool residual = false) const {
         GemmArgs g{p->x8, p->act_scale, p->act_sum, w, ws, out, count, rows, width};
         g.out_i32 = out_i32;
+        g.residual = residual;
         return launch_int4_gemm(g, stream);
     }
     int norm_quant(const float* gamma) const {
         batch_rmsnorm_quant_kernel<<<count, 256, 0, stream>>>(p->x, gamma, m->eps, m->hidden, p->x8, p->act_scale,
                                                               p->act_sum);
-        H4B_CUDA_TRY(cudaGetLastError());
-        return 0;
-    }
-    int add_x() const {
-        const long long n = static_cast<long long>(count) * m->hidden;
-        add_kernel<<<static_cast<int>((n + 255) / 256), 256, 0, stream>>>(p->x, p->proj, static_cast<int>(n));
         H4B_CUDA_TRY(cudaGetLastError());
         return 0;
     }
@@ -236,17 +235,18 @@ struct PrefillRun {
             return rc;
         char* kc = static_cast<char*>(s->k_cache) + l * kv_layer * eb;
         char* vc = static_cast<char*>(s->v_cache) + l * kv_layer * eb;
-        const dim3 heads_grid(count, m->heads + m->kv_heads);
+        const long long pairs = static_cast<long long>(count) * (m->heads + m->kv_heads);
+        const int rope_grid = static_cast<int>((pairs + kRopeWarps - 1) / kRopeWarps);
         const long long head_stride = static_cast<long long>(s->capacity) * d;
         if (s->kv_dtype == 0)
-            prefill_rope_append_kernel<float><<<heads_grid, 32, 0, stream>>>(
+            prefill_rope_append_kernel<float><<<rope_grid, 32 * kRopeWarps, 0, stream>>>(
                 p->qkv, qkv_rows, m->heads, m->kv_heads, m->norm_q + static_cast<size_t>(l) * d,
-                m->norm_k + static_cast<size_t>(l) * d, m->rope_cos, m->rope_sin, m->eps, p->positions,
+                m->norm_k + static_cast<size_t>(l) * d, m->rope_cos, m->rope_sin, m->eps, p->positions, count,
                 reinterpret_cast<float*>(kc), reinterpret_cast<float*>(vc), head_stride, d);
         else
-            prefill_rope_append_kernel<__half><<<heads_grid, 32, 0, stream>>>(
+            prefill_rope_append_kernel<__half><<<rope_grid, 32 * kRopeWarps, 0, stream>>>(
                 p->qkv, qkv_rows, m->heads, m->kv_heads, m->norm_q + static_cast<size_t>(l) * d,
-                m->norm_k + static_cast<size_t>(l) * d, m->rope_cos, m->rope_sin, m->eps, p->positions,
+                m->norm_k + static_cast<size_t>(l) * d, m->rope_cos, m->rope_sin, m->eps, p->positions, count,
                 reinterpret_cast<__half*>(kc), reinterpret_cast<__half*>(vc), head_stride, d);
         H4B_CUDA_TRY(cudaGetLastError());
         if (p->attn_splits == 1 && p->attn_kernel == H4B_PREFILL_ATTN_TENSOR &&
@@ -290,14 +290,15 @@ struct PrefillRun {
         }
         return 0;
     }
-    // RMSNorm, quantisation, the gate/up GEMM and SwiGLU: p->act.
-    int mlp_block(int l) const {
+    // RMSNorm, quantisation, the gate/up GEMM and (swiglu) SwiGLU: p->act.
+    int mlp_block(int l, bool swiglu = true) const {
         const int H = m->hidden, I = m->intermediate;
         int rc;
         if ((rc = norm_quant(m->norm_post + static_cast<size_t>(l) * H))) return rc;
         if ((rc = gemm(m->w_gate_up + static_cast<size_t>(l) * 2 * I * (H / 2),
                        m->s_gate_up + static_cast<size_t>(l) * 2 * I, p->gate_up, 2 * I, H)))
             return rc;
+        if (!swiglu) return 0;
         const long long n_act = static_cast<long long>(count) * I;
         batch_swiglu_kernel<<<static_cast<int>((n_act + 255) / 256), 256, 0, stream>>>(p->gate_up, I, count, p->act);
         H4B_CUDA_TRY(cudaGetLastError());
@@ -321,21 +322,23 @@ int prefill(const h4b_model* m, const h4b_state* s, const h4b_prefill_scratch* p
     const int H = m->hidden, I = m->intermediate, q_size = m->heads * m->head_dim;
     const PrefillRun r{m, s, p, count, stream};
     if ((rc = r.setup(m->w_embed, m->s_embed, m->vocab))) return rc;
+    // The residual adds ride in the o / down GEMM epilogues (x + proj, in
+    // that order), SwiGLU in the quantisation of its rows: the same
+    // operations as the separate kernels, bit for bit.
     for (int l = 0; l < m->layers; ++l) {
         if ((rc = r.attention_block(l))) return rc;
-        quantize_rows_kernel<<<count, 256, 0, stream>>>(p->attended, q_size, p->x8, p->act_scale, p->act_sum);
-        H4B_CUDA_TRY(cudaGetLastError());
-        if ((rc = r.gemm(m->w_o + static_cast<size_t>(l) * H * (q_size / 2), m->s_o + static_cast<size_t>(l) * H, p->proj,
-                         H, q_size)))
+        if ((rc = launch_quantize_rows<false>(p->attended, q_size, count, p->x8, p->act_scale, p->act_sum, nullptr,
+                                              stream)))
             return rc;
-        if ((rc = r.add_x())) return rc;
-        if ((rc = r.mlp_block(l))) return rc;
-        quantize_rows_kernel<<<count, 256, 0, stream>>>(p->act, I, p->x8, p->act_scale, p->act_sum);
-        H4B_CUDA_TRY(cudaGetLastError());
-        if ((rc = r.gemm(m->w_down + static_cast<size_t>(l) * H * (I / 2), m->s_down + static_cast<size_t>(l) * H, p->proj,
-                         H, I)))
+        if ((rc = r.gemm(m->w_o + static_cast<size_t>(l) * H * (q_size / 2), m->s_o + static_cast<size_t>(l) * H, p->x,
+                         H, q_size, nullptr, true)))
             return rc;
-        if ((rc = r.add_x())) return rc;
+        if ((rc = r.mlp_block(l, false))) return rc;
+        if ((rc = launch_quantize_rows<true>(p->gate_up, I, count, p->x8, p->act_scale, p->act_sum, p->act, stream)))
+            return rc;
+        if ((rc = r.gemm(m->w_down + static_cast<size_t>(l) * H * (I / 2), m->s_down + static_cast<size_t>(l) * H, p->x,
+                         H, I, nullptr, true)))
+            return rc;
     }
     return r.finish();
 }

@@ -22,15 +22,21 @@
 // Warps: 0-3 are the row warps (thread = query row; TMEM lane quarter =
 // warp), 4 loads K tiles and owns the tensor memory, 5 loads V tiles, 6
 // issues the MMAs (one elected thread). Per key tile j, with the score
-// accumulator S, the probability tile P and the output accumulator O each
-// double-buffered (b = j % 2) and K, V in kStages stages:
+// accumulator S and the probability tile P double-buffered (b = j % 2), K and
+// V in kStages stages and one output accumulator O in tensor memory:
 //   MMA:   S[b] = Qhi K_j^T + Qlo K_j^T                  -> s_full[b], k_empty
 //   rows:  load S[b] (-> s_free[b]); masked maximum, p; P[b] = (phi, plo)
 //                                                         -> p_full[b]
-//   MMA:   O[b] = Phi V_j + Plo V_j                      -> o_full[b], v_empty
-//   rows:  o_acc = o_acc * alpha_j + O[b]  (-> o_free[b]), one tile behind
-// The MMA thread issues S for tile j + 2 before P.V for tile j, so the tensor
-// cores compute the next scores while the row warps work on the softmax.
+//   MMA:   O += Phi V_j + Plo V_j                        -> o_full, v_empty
+// The MMA thread issues P.V for tile j, then S for tile j + 2: the tensor
+// cores compute the next scores while the row warps work on the softmax, and
+// s_full for tile j also stands for the completion of P.V j - 2 (a commit
+// tracks every earlier MMA of its thread).
+// O is scaled lazily: each row keeps a reference maximum m_ref and forms
+// p = 2^(s - m_ref + 8); only when a tile's maximum passes m_ref + 7 (p would
+// leave fp16's range) does the row move m_ref up, and the warp then rescales
+// its O rows in tensor memory (after the P.V MMAs issued so far completed)
+// before publishing the tile's P. The result, o / l, is the same quotient.
 //
 // Every wait is bounded (mbar_wait). A role whose wait runs out reports
 // kStatusWaitTimeout, marks the CTA as failed and stops; the producers wait
@@ -63,11 +69,14 @@ constexpr int kPtcBarOff = kPtcPOff + 4 * kPtcRegion;
 constexpr int kPtcBarBytes = 256;
 constexpr int kPtcSmem = kPtcBarOff + kPtcBarBytes + 1024;  // + alignment slack
 static_assert(kPtcSmem <= 232448, "shared memory per CTA");
-static_assert((4 * kPtcStages + 10) * 8 + 8 <= kPtcBarBytes, "barrier area");
+static_assert((4 * kPtcStages + 9) * 8 + 8 <= kPtcBarBytes, "barrier area");
 
-// Tensor memory columns: S[0], S[1] (64 each), O[0], O[1] (128 each).
-constexpr uint32_t kPtcTmemCols = 512;
+// Tensor memory columns: S[0], S[1] (64 each), then O (128).
+constexpr uint32_t kPtcTmemCols = 256;
 constexpr uint32_t kPtcSCol = 0, kPtcOCol = 2 * kPtcKeys;
+// Lazy rescaling: p = 2^(s - m_ref + kPtcOffset), m_ref moves when a score
+// passes m_ref + kPtcSlack, so p < 2^(kPtcOffset + kPtcSlack) = 2^15 < fp16 max.
+constexpr float kPtcOffset = 8.f, kPtcSlack = 7.f;
 
 // Instruction descriptors (kind::f16): D f32 (bits 4-5 = 1), A and B f16
 // (format 0), N >> 3 at bit 17, M >> 4 at bit 24; P.V reads B (the V tile)
@@ -132,6 +141,17 @@ __device__ __forceinline__ void tmem_wait_regs(float (&v)[N]) {
                      : "memory");
 }
 
+// 16 columns of this warp's TMEM lane quarter from v[off .. off + 15].
+template <int N>
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[N], int off) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "f"(v[off + 0]), "f"(v[off + 1]), "f"(v[off + 2]), "f"(v[off + 3]), "f"(v[off + 4]),
+          "f"(v[off + 5]), "f"(v[off + 6]), "f"(v[off + 7]), "f"(v[off + 8]), "f"(v[off + 9]), "f"(v[off + 10]),
+          "f"(v[off + 11]), "f"(v[off + 12]), "f"(v[off + 13]), "f"(v[off + 14]), "f"(v[off + 15])
+        : "memory");
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -166,9 +186,8 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
     uint64_t* s_full = v_empty + kPtcStages;  // [2]
     uint64_t* s_free = s_full + 2;             // [2]
     uint64_t* p_full = s_free + 2;             // [2]
-    uint64_t* o_full = p_full + 2;             // [2]
-    uint64_t* o_free = o_full + 2;             // [2]
-    uint64_t* q_ready = o_free + 2;
+    uint64_t* o_full = p_full + 2;             // one phase per P.V tile
+    uint64_t* q_ready = o_full + 1;
     uint64_t* mma_done = q_ready + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -192,9 +211,8 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
             mbar_init(&s_full[b], 1);
             mbar_init(&s_free[b], kPtcRowWarps);
             mbar_init(&p_full[b], kPtcRowWarps);
-            mbar_init(&o_full[b], 1);
-            mbar_init(&o_free[b], kPtcRowWarps);
         }
+        mbar_init(o_full, 1);
         mbar_init(q_ready, kPtcRowWarps);
         mbar_init(mma_done, 1);
         *failed = wait_failed_before() ? 1 : 0;
@@ -268,7 +286,6 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
                 const int s = j % kPtcStages, b = j & 1;
                 if (*failed) return false;
                 if (!mbar_wait(&p_full[b], (j >> 1) & 1)) return false;
-                if (j >= 2 && !mbar_wait(&o_free[b], ((j - 2) >> 1) & 1)) return false;
                 if (!mbar_wait(&v_full[s], (j / kPtcStages) & 1)) return false;
                 tc_fence_after();
 #pragma unroll
@@ -278,17 +295,17 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
                         // A: 16 keys = 32 bytes along the P row; B: 16 keys = 2 groups of 8 rows = 2048 bytes
                         const uint64_t a = sw128_desc(p_region(b, part)) + 2 * kk;
                         const uint64_t bd = sw128_mn_desc(v_half(s, 0) + kk * 2048, kPtcHalfTile);
-                        tc_mma_f16(tmem + kPtcOCol + b * kPtcDim, a, bd, kPtcIdescPV, (part | kk) != 0);
+                        tc_mma_f16(tmem + kPtcOCol, a, bd, kPtcIdescPV, (j | part | kk) != 0);
                     }
                 tc_commit(&v_empty[s]);
-                tc_commit(&o_full[b]);
+                tc_commit(o_full);
                 return true;
             };
             bool ok = true;
             if (tiles > 0) {
                 ok = !*failed && mbar_wait(q_ready, 0);
                 ok = ok && issue_s(0) && (tiles < 2 || issue_s(1));
-                for (int j = 0; ok && j < tiles; ++j) ok = (j + 2 >= tiles || issue_s(j + 2)) && issue_pv(j);
+                for (int j = 0; ok && j < tiles; ++j) ok = issue_pv(j) && (j + 2 >= tiles || issue_s(j + 2));
             }
             if (!ok) *failed = 1;
             tc_commit(mma_done);  // arrives once every MMA issued above has completed
@@ -324,31 +341,8 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
         // log2(e) / sqrt(128): scores in base-2 units
         const float score_scale = 1.4426950408889634f * 0.08838834764831845f;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * h) << 16);
-        float o_acc[kPtcDim];
-#pragma unroll
-        for (int c = 0; c < kPtcDim; ++c) o_acc[c] = 0.f;
-        float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+        float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
-
-        // o_acc = o_acc * alpha + O[tile jj % 2], then O[jj % 2] is free
-        auto correct = [&](int jj, float alpha) {
-            const int bb = jj & 1;
-            ok = __all_sync(0xffffffffu, ok && !*failed && mbar_wait(&o_full[bb], (jj >> 1) & 1));
-            if (!ok) return;
-            tc_fence_after();
-#pragma unroll
-            for (int c0 = 0; c0 < kPtcDim; c0 += 32) {
-                float v[32];
-                tmem_ld16_nowait(lane_base + kPtcOCol + bb * kPtcDim + c0, v, 0);
-                tmem_ld16_nowait(lane_base + kPtcOCol + bb * kPtcDim + c0 + 16, v, 16);
-                tmem_wait_regs(v);
-#pragma unroll
-                for (int k = 0; k < 32; ++k) o_acc[c0 + k] = __fmaf_rn(o_acc[c0 + k], alpha, v[k]);
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&o_free[bb]);
-        };
 
         for (int j = 0; j < tiles && ok; ++j) {
             const int b = j & 1;
@@ -363,50 +357,74 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_free[b]);
 
-            // causal mask and the tile maximum
+            // causal mask (only tiles that reach past some row's position) and
+            // the tile maximum, in raw q.k units (the scale is positive)
             const int kbase = j * kPtcKeys;
-            float mx = -INFINITY;
+            if (!__all_sync(0xffffffffu, kbase + kPtcKeys - 1 <= pos)) {
 #pragma unroll
-            for (int c = 0; c < kPtcKeys; ++c) {
-                sv[c] = kbase + c <= pos ? sv[c] * score_scale : -INFINITY;
-                mx = fmaxf(mx, sv[c]);
+                for (int c = 0; c < kPtcKeys; ++c) sv[c] = kbase + c <= pos ? sv[c] : -INFINITY;
             }
-            const float m_new = fmaxf(m, mx);
-            const float alpha = m == -INFINITY ? 0.f : ex2_approx(m - m_new);
-            const float base = m_new == -INFINITY ? 0.f : m_new - 8.f;
-            m = m_new;
+            float mx = sv[0];
+#pragma unroll
+            for (int c = 1; c < kPtcKeys; ++c) mx = fmaxf(mx, sv[c]);
+            const float tmax = mx * score_scale;  // -inf stays -inf
+            const bool move = tmax > m_ref + kPtcSlack;
+            const bool rescale = move && m_ref != -INFINITY;
+            if (__any_sync(0xffffffffu, rescale)) {
+                // O (every P.V issued so far: tiles < j) times 2^(m_ref - tmax)
+                ok = __all_sync(0xffffffffu, !*failed && mbar_wait(o_full, (j - 1) & 1));
+                if (!ok) break;
+                tc_fence_after();
+                const float alpha = rescale ? ex2_approx(m_ref - tmax) : 1.f;
+#pragma unroll
+                for (int c0 = 0; c0 < kPtcDim; c0 += 32) {
+                    float v[32];
+                    tmem_ld16_nowait(lane_base + kPtcOCol + c0, v, 0);
+                    tmem_ld16_nowait(lane_base + kPtcOCol + c0 + 16, v, 16);
+                    tmem_wait_regs(v);
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) v[k] *= alpha;
+                    tmem_st16(lane_base + kPtcOCol + c0, v, 0);
+                    tmem_st16(lane_base + kPtcOCol + c0 + 16, v, 16);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                l *= alpha;
+            }
+            if (move) m_ref = tmax;
+            // p = 2^(s * scale - (m_ref - offset)); masked keys give 2^-inf = 0
+            const float nbase = m_ref == -INFINITY ? 0.f : kPtcOffset - m_ref;
             float sum = 0.f;
             uint8_t* ph = p_region(b, 0);
             uint8_t* pl = p_region(b, 1);
 #pragma unroll
             for (int c = 0; c < kPtcKeys / 8; ++c) {
-                float p[8];
+                float pv[8];
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
-                    p[k] = ex2_approx(sv[8 * c + k] - base);  // exp2(-inf) = 0 for masked keys
-                    sum += p[k];
+                    pv[k] = ex2_approx(__fmaf_rn(sv[8 * c + k], score_scale, nbase));
+                    sum += pv[k];
                 }
                 uint4 hi, lo;
-                split_pair(p[0], p[1], hi.x, lo.x);
-                split_pair(p[2], p[3], hi.y, lo.y);
-                split_pair(p[4], p[5], hi.z, lo.z);
-                split_pair(p[6], p[7], hi.w, lo.w);
+                split_pair(pv[0], pv[1], hi.x, lo.x);
+                split_pair(pv[2], pv[3], hi.y, lo.y);
+                split_pair(pv[4], pv[5], hi.z, lo.z);
+                split_pair(pv[6], pv[7], hi.w, lo.w);
                 const int off = sw128_offset(r, c);
                 *reinterpret_cast<uint4*>(ph + off) = hi;
                 *reinterpret_cast<uint4*>(pl + off) = lo;
             }
-            l = __fmaf_rn(l, alpha, sum);
+            l += sum;
             if (j == tiles - 1 && max_ctx < kbase + kPtcKeys) {
                 // Keys [max_ctx, tile end) get p = 0 from every row, but their V
                 // rows (cache entries past the context, or the TMA's zero fill
                 // past the capacity) must not be NaN: 0 * NaN would reach the
                 // sum. Zero them once the tile has landed; each row warp zeroes
                 // its own share before its p_full arrival, and the P.V MMAs
-                // wait for all four. The row warps have already seen tile
-                // j - kPtcStages's P.V complete, so v_full's current phase is
-                // this tile's.
+                // wait for all four. s_full for this tile stood for the
+                // completion of P.V j - 2, so v_full's current phase is this
+                // tile's.
                 const int s = j % kPtcStages;
-                ok = __all_sync(0xffffffffu, ok && !*failed && mbar_wait(&v_full[s], (j / kPtcStages) & 1));
+                ok = __all_sync(0xffffffffu, !*failed && mbar_wait(&v_full[s], (j / kPtcStages) & 1));
                 if (!ok) break;
                 const int first = max_ctx - kbase;
                 const int chunks = (kPtcKeys - first) * 8;  // 16-byte chunks per d half
@@ -417,21 +435,34 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
                 }
             }
             fence_proxy_async_smem();  // P (and the zeroed V rows) -> visible to the tensor cores
+            tc_fence_before();         // ... after the O rescale's tensor-memory stores
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[b]);
-            if (j >= 1) correct(j - 1, alpha_prev);
-            alpha_prev = alpha;
         }
-        if (ok && tiles > 0) correct(tiles - 1, alpha_prev);
-        if (ok && valid && pos >= 0) {
+        // every MMA complete (the last commit of the MMA thread): O is final
+        ok = __all_sync(0xffffffffu, ok && tiles > 0 && !*failed && mbar_wait(mma_done, 0));
+        if (ok) {
+            tc_fence_after();
             const float inv = __fdiv_rn(1.0f, l);
-            float* orow = out + static_cast<long long>(q0 + i) * out_stride +
+            float* orow = out + static_cast<long long>(q0 + (valid ? i : 0)) * out_stride +
                           static_cast<long long>(kvh * kPtcGroups + h) * kPtcDim;
 #pragma unroll
-            for (int c = 0; c < kPtcDim; c += 4)
-                *reinterpret_cast<float4*>(orow + c) =
-                    make_float4(o_acc[c] * inv, o_acc[c + 1] * inv, o_acc[c + 2] * inv, o_acc[c + 3] * inv);
+            for (int c0 = 0; c0 < kPtcDim; c0 += 32) {
+                float v[32];
+                tmem_ld16_nowait(lane_base + kPtcOCol + c0, v, 0);
+                tmem_ld16_nowait(lane_base + kPtcOCol + c0 + 16, v, 16);
+                tmem_wait_regs(v);
+                if (valid && pos >= 0) {
+#pragma unroll
+                    for (int c = 0; c < 32; c += 4)
+                        *reinterpret_cast<float4*>(orow + c0 + c) =
+                            make_float4(v[c] * inv, v[c + 1] * inv, v[c + 2] * inv, v[c + 3] * inv);
+                }
+            }
+        } else if (tiles > 0 && lane == 0) {
+            *failed = 1;
         }
+        ok = ok || tiles == 0;
         if (!ok && lane == 0) *failed = 1;
     }
     tc_fence_before();
