@@ -277,21 +277,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int c0 = slice * kCols; c0 < (slice + 1) * kCols; c0 += 16) {
                 uint32_t v[16];
                 tmem_ld16(base + c0, v);
+                if (g.split_acc || g.out_i32) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int m = m0 + c0 + j;
+                        if (m >= g.M) continue;
+                        if (g.split_acc)
+                            atomicAdd(g.split_acc + static_cast<size_t>(m) * g.N + row, static_cast<int>(v[j]));
+                        else
+                            g.out_i32[static_cast<size_t>(m) * g.N + row] = static_cast<int>(v[j]);
+                    }
+                    continue;
+                }
+                // every load (token scales, residual values) before the first
+                // store, so the loads overlap instead of queueing behind the
+                // stores they might alias
+                float as[16], prev[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int m = min(m0 + c0 + j, g.M - 1);
+                    as[j] = g.act_scale[m];
+                    prev[j] = g.residual ? g.out[static_cast<size_t>(m) * g.N + row] : 0.f;
+                }
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int m = m0 + c0 + j;
-                    if (m < g.M) {
-                        if (g.split_acc)
-                            atomicAdd(g.split_acc + static_cast<size_t>(m) * g.N + row, static_cast<int>(v[j]));
-                        else if (g.out_i32)
-                            g.out_i32[static_cast<size_t>(m) * g.N + row] = static_cast<int>(v[j]);
-                        else {
-                            float* o = g.out + static_cast<size_t>(m) * g.N + row;
-                            const float value =
-                                __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[j])), g.act_scale[m]), ws);
-                            *o = g.residual ? __fadd_rn(*o, value) : value;
-                        }
-                    }
+                    if (m >= g.M) continue;
+                    const float value = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[j])), as[j]), ws);
+                    g.out[static_cast<size_t>(m) * g.N + row] = g.residual ? __fadd_rn(prev[j], value) : value;
                 }
             }
         }
