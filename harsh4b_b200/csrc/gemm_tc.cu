@@ -292,18 +292,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 // every load (token scales, residual values) before the first
                 // store, so the loads overlap instead of queueing behind the
                 // stores they might alias
-                float as[16], prev[16];
+                const float as_lane = g.act_scale[min(m0 + c0 + (lane & 15), g.M - 1)];
+                float prev[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int m = min(m0 + c0 + j, g.M - 1);
-                    as[j] = g.act_scale[m];
-                    prev[j] = g.residual ? g.out[static_cast<size_t>(m) * g.N + row] : 0.f;
-                }
+                for (int j = 0; j < 16; ++j)
+                    prev[j] = g.residual ? g.out[static_cast<size_t>(min(m0 + c0 + j, g.M - 1)) * g.N + row] : 0.f;
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int m = m0 + c0 + j;
+                    const float as = __shfl_sync(0xffffffffu, as_lane, j);
                     if (m >= g.M) continue;
-                    const float value = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[j])), as[j]), ws);
+                    const float value = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[j])), as), ws);
                     g.out[static_cast<size_t>(m) * g.N + row] = g.residual ? __fadd_rn(prev[j], value) : value;
                 }
             }
