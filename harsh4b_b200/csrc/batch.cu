@@ -87,6 +87,93 @@ __global__ void __launch_bounds__(256) batch_rmsnorm_quant_kernel(const float* x
     }
 }
 
+// batch_rmsnorm_quant_kernel's result, bit for bit (each thread keeps the
+// same groups in the same order, and the block reductions are the same), with
+// the thread's kG groups of 8 held in registers: one read of the row instead
+// of three.
+template <int kG>
+__global__ void __launch_bounds__(256) batch_rmsnorm_quant_reg_kernel(const float* x, const float* gamma, float eps,
+                                                                      int H, int8_t* x8, float* act_scale,
+                                                                      int32_t* act_sum) {
+    __shared__ float red[32];
+    __shared__ int ired[8];
+    const int b = blockIdx.x, tid = threadIdx.x;
+    const float* row = x + static_cast<size_t>(b) * H;
+    const int groups = H >> 3;
+    float v[kG][8], gm[kG][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < kG; ++k) {
+        const int g = tid + 256 * k;
+        if (g < groups) {
+            load8(row + 8 * g, v[k]);
+            load8(gamma + 8 * g, gm[k]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss = __fmaf_rn(v[k][e], v[k][e], ss);
+        }
+    }
+    ss = group_sum(ss, red, 8, 1);
+    const float mean = __fdiv_rn(ss, static_cast<float>(H));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    float local = 0.f;
+#pragma unroll
+    for (int k = 0; k < kG; ++k) {
+        if (tid + 256 * k < groups) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                v[k][e] = __fmul_rn(__fmul_rn(v[k][e], inv), gm[k][e]);
+                local = fmaxf(local, fabsf(v[k][e]));
+            }
+        }
+    }
+    const float m = group_max(local, red, 8, 1);
+    const float qs = quant_multiplier(m);
+    int8_t* out = x8 + static_cast<size_t>(b) * H;
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < kG; ++k) {
+        const int g = tid + 256 * k;
+        if (g < groups) {
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int q = quantize_one(v[k][e], qs);
+                sum += q;
+                if (e < 4) lo |= static_cast<uint32_t>(q & 0xFF) << (8 * e);
+                else hi |= static_cast<uint32_t>(q & 0xFF) << (8 * (e - 4));
+            }
+            *reinterpret_cast<uint2*>(out + 8 * g) = make_uint2(lo, hi);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if ((tid & 31) == 0) ired[tid >> 5] = sum;
+    __syncthreads();
+    if (tid == 0) {
+        int t = 0;
+        for (int w = 0; w < 8; ++w) t += ired[w];
+        act_sum[b] = t;
+        act_scale[b] = dequant_scale(m);
+    }
+}
+
+// RMSNorm + per-row quantisation of `rows` rows of H (the register kernel
+// when a thread's share fits, else the three-pass kernel).
+int launch_rmsnorm_quant(const float* x, const float* gamma, float eps, int H, int rows, int8_t* x8,
+                         float* act_scale, int32_t* act_sum, cudaStream_t stream) {
+    const int per = (H / 8 + 255) / 256;
+    if (H % 8 == 0 && per <= 1)
+        batch_rmsnorm_quant_reg_kernel<1><<<rows, 256, 0, stream>>>(x, gamma, eps, H, x8, act_scale, act_sum);
+    else if (H % 8 == 0 && per == 2)
+        batch_rmsnorm_quant_reg_kernel<2><<<rows, 256, 0, stream>>>(x, gamma, eps, H, x8, act_scale, act_sum);
+    else if (H % 8 == 0 && per <= 4)
+        batch_rmsnorm_quant_reg_kernel<4><<<rows, 256, 0, stream>>>(x, gamma, eps, H, x8, act_scale, act_sum);
+    else
+        batch_rmsnorm_quant_kernel<<<rows, 256, 0, stream>>>(x, gamma, eps, H, x8, act_scale, act_sum);
+    H4B_CUDA_TRY(cudaGetLastError());
+    return 0;
+}
+
 // SwiGLU over rows laid out like the fused gate/up weight (blocks of 4 gate
 // rows then the 4 matching up rows): act = gate / (1 + exp(-gate)) * up.
 __global__ void batch_swiglu_kernel(const float* gate_up, int I, int B, float* act) {
@@ -193,8 +280,7 @@ int decode_batch(const h4b_model* m, const h4b_batch_state* s, cudaStream_t stre
         return launch_int4_gemm(g, stream);
     };
     auto norm_quant = [&](const float* gamma) {
-        batch_rmsnorm_quant_kernel<<<B, 256, 0, stream>>>(s->x, gamma, m->eps, H, s->x8, s->act_scale, s->act_sum);
-        return cudaGetLastError() == cudaSuccess ? 0 : H4B_EINVAL;
+        return launch_rmsnorm_quant(s->x, gamma, m->eps, H, B, s->x8, s->act_scale, s->act_sum, stream);
     };
     batch_embed_kernel<<<B, 256, 0, stream>>>(s->tokens, m->w_embed, m->s_embed, m->vocab, H, s->x);
     H4B_CUDA_TRY(cudaGetLastError());

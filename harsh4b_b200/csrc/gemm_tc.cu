@@ -151,7 +151,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kTcRows, m0 = blockIdx.y * TOK;
+    // token tiles fastest: the CTAs running at once share weight tiles and
+    // spread their reads of the larger activation tiles over several of them
+    const int n0 = blockIdx.y * kTcRows, m0 = blockIdx.x * TOK;
     // this CTA's K slice (split-K over gridDim.z): steps [kbeg, kbeg + steps)
     const int all_steps = g.K / kTcK;
     const int kbeg = static_cast<int>(static_cast<long long>(blockIdx.z) * all_steps / gridDim.z);
@@ -434,7 +436,7 @@ int launch_tc(const GemmArgs& g, cudaStream_t stream) {
         ksplit = std::max(1, std::min(sm_count() / tiles, steps / 4));
     const TcArgs a{g.act_scale, g.w_scale, g.out, g.M, g.N, g.K, g.out_i32, ksplit > 1 ? g.split_acc : nullptr,
                    g.residual ? 1 : 0};
-    const dim3 grid(g.N / kTcRows, (g.M + TOK - 1) / TOK, ksplit);
+    const dim3 grid((g.M + TOK - 1) / TOK, g.N / kTcRows, ksplit);
     int4_gemm_tc_kernel<TOK><<<grid, kTcThreads, C::kSmem, stream>>>(wmap, xmap, a);
     H4B_CUDA_TRY(cudaGetLastError());
     if (ksplit > 1) {

@@ -208,11 +208,19 @@ struct PrefillRun {
         g.residual = residual;
         return launch_int4_gemm(g, stream);
     }
+    // RMSNorm, quantisation and the gate/up GEMM, then SwiGLU fused into the
+    // quantisation of its rows for the down projection.
+    int mlp_quantised(int l) const {
+        const int H = m->hidden, I = m->intermediate;
+        int rc;
+        if ((rc = norm_quant(m->norm_post + static_cast<size_t>(l) * H))) return rc;
+        if ((rc = gemm(m->w_gate_up + static_cast<size_t>(l) * 2 * I * (H / 2),
+                       m->s_gate_up + static_cast<size_t>(l) * 2 * I, p->gate_up, 2 * I, H)))
+            return rc;
+        return launch_quantize_rows<true>(p->gate_up, I, count, p->x8, p->act_scale, p->act_sum, p->act, stream);
+    }
     int norm_quant(const float* gamma) const {
-        batch_rmsnorm_quant_kernel<<<count, 256, 0, stream>>>(p->x, gamma, m->eps, m->hidden, p->x8, p->act_scale,
-                                                              p->act_sum);
-        H4B_CUDA_TRY(cudaGetLastError());
-        return 0;
+        return launch_rmsnorm_quant(p->x, gamma, m->eps, m->hidden, count, p->x8, p->act_scale, p->act_sum, stream);
     }
     int setup(const uint8_t* table, const float* table_scales, int table_vocab) const {
         prefill_setup_kernel<<<std::min((count + 255) / 256, 148), 256, 0, stream>>>(s->position, count, s->capacity,
@@ -290,15 +298,14 @@ struct PrefillRun {
         }
         return 0;
     }
-    // RMSNorm, quantisation, the gate/up GEMM and (swiglu) SwiGLU: p->act.
-    int mlp_block(int l, bool swiglu = true) const {
+    // RMSNorm, quantisation, the gate/up GEMM and SwiGLU: p->act.
+    int mlp_block(int l) const {
         const int H = m->hidden, I = m->intermediate;
         int rc;
         if ((rc = norm_quant(m->norm_post + static_cast<size_t>(l) * H))) return rc;
         if ((rc = gemm(m->w_gate_up + static_cast<size_t>(l) * 2 * I * (H / 2),
                        m->s_gate_up + static_cast<size_t>(l) * 2 * I, p->gate_up, 2 * I, H)))
             return rc;
-        if (!swiglu) return 0;
         const long long n_act = static_cast<long long>(count) * I;
         batch_swiglu_kernel<<<static_cast<int>((n_act + 255) / 256), 256, 0, stream>>>(p->gate_up, I, count, p->act);
         H4B_CUDA_TRY(cudaGetLastError());
@@ -333,9 +340,7 @@ int prefill(const h4b_model* m, const h4b_state* s, const h4b_prefill_scratch* p
         if ((rc = r.gemm(m->w_o + static_cast<size_t>(l) * H * (q_size / 2), m->s_o + static_cast<size_t>(l) * H, p->x,
                          H, q_size, nullptr, true)))
             return rc;
-        if ((rc = r.mlp_block(l, false))) return rc;
-        if ((rc = launch_quantize_rows<true>(p->gate_up, I, count, p->x8, p->act_scale, p->act_sum, p->act, stream)))
-            return rc;
+        if ((rc = r.mlp_quantised(l))) return rc;
         if ((rc = r.gemm(m->w_down + static_cast<size_t>(l) * H * (I / 2), m->s_down + static_cast<size_t>(l) * H, p->x,
                          H, I, nullptr, true)))
             return rc;

@@ -364,9 +364,16 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
 #pragma unroll
                 for (int c = 0; c < kPtcKeys; ++c) sv[c] = kbase + c <= pos ? sv[c] : -INFINITY;
             }
-            float mx = sv[0];
+            // pairwise (the maximum is order-free; a tree keeps the dependent
+            // chain at log2(64) steps instead of 63)
+            float tm[kPtcKeys / 2];
 #pragma unroll
-            for (int c = 1; c < kPtcKeys; ++c) mx = fmaxf(mx, sv[c]);
+            for (int c = 0; c < kPtcKeys / 2; ++c) tm[c] = fmaxf(sv[c], sv[c + kPtcKeys / 2]);
+#pragma unroll
+            for (int w = kPtcKeys / 4; w >= 1; w >>= 1)
+#pragma unroll
+                for (int c = 0; c < w; ++c) tm[c] = fmaxf(tm[c], tm[c + w]);
+            const float mx = tm[0];
             const float tmax = mx * score_scale;  // -inf stays -inf
             const bool move = tmax > m_ref + kPtcSlack;
             const bool rescale = move && m_ref != -INFINITY;
@@ -393,7 +400,11 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
             if (move) m_ref = tmax;
             // p = 2^(s * scale - (m_ref - offset)); masked keys give 2^-inf = 0
             const float nbase = m_ref == -INFINITY ? 0.f : kPtcOffset - m_ref;
-            float sum = 0.f;
+            // eight partial sums (one per key of a 16-byte chunk): short
+            // dependent chains for the row sum
+            float part[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) part[k] = 0.f;
             uint8_t* ph = p_region(b, 0);
             uint8_t* pl = p_region(b, 1);
 #pragma unroll
@@ -402,7 +413,7 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
                     pv[k] = ex2_approx(__fmaf_rn(sv[8 * c + k], score_scale, nbase));
-                    sum += pv[k];
+                    part[k] += pv[k];
                 }
                 uint4 hi, lo;
                 split_pair(pv[0], pv[1], hi.x, lo.x);
@@ -413,7 +424,7 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
                 *reinterpret_cast<uint4*>(ph + off) = hi;
                 *reinterpret_cast<uint4*>(pl + off) = lo;
             }
-            l += sum;
+            l += ((part[0] + part[4]) + (part[2] + part[6])) + ((part[1] + part[5]) + (part[3] + part[7]));
             if (j == tiles - 1 && max_ctx < kbase + kPtcKeys) {
                 // Keys [max_ctx, tile end) get p = 0 from every row, but their V
                 // rows (cache entries past the context, or the TMA's zero fill
