@@ -19,6 +19,11 @@
 // with the running maximum lowered by 8, so p <= 2^8 (an exact power-of-two
 // scale that cancels in o / l) keeps the lo terms clear of fp16 subnormals.
 //
+// Operands: q (hi, lo) and the probability tiles P (hi, lo) live in tensor
+// memory, the A operands of the MMAs (row = lane, two fp16 per 32-bit
+// column); only the K and V tiles are read from shared memory, which keeps
+// the MMAs' shared-memory traffic to the tiles the TMA brings in.
+//
 // Warps: 0-3 are the row warps (thread = query row; TMEM lane quarter =
 // warp), 4 loads K tiles and owns the tensor memory, 5 loads V tiles, 6
 // issues the MMAs (one elected thread). Per key tile j, with the score
@@ -50,30 +55,26 @@ constexpr int kPtcGroups = 4;                              // q heads per kv hea
 constexpr int kPtcRows = kPtcPositions * kPtcGroups;       // MMA M = 128
 constexpr int kPtcKeys = 64;                               // keys per tile (the S MMA's N)
 constexpr int kPtcDim = 128;                               // head_dim (the P.V MMA's N)
-constexpr int kPtcStages = 2;                              // K and V tile stages
+constexpr int kPtcStages = 3;                              // K and V tile stages
 constexpr int kPtcRowWarps = 4, kPtcKWarp = 4, kPtcVWarp = 5, kPtcMmaWarp = 6;
 constexpr int kPtcThreads = 32 * 7;
 
 // Shared memory, every tile 1024-byte aligned (the 128-byte swizzle atom):
-//   Q: [part hi/lo][d half][128 rows x 128 B]             4 x 16 KB
 //   K: [stage][d half][64 keys x 128 B]                   kPtcStages x 16 KB
 //   V: [stage][d half][64 keys x 128 B]                   kPtcStages x 16 KB
-//   P: [buffer][part hi/lo][128 rows x 128 B (64 keys)]   4 x 16 KB
-constexpr int kPtcRegion = kPtcRows * 128;                 // 16 KB
 constexpr int kPtcHalfTile = kPtcKeys * 128;               // 8 KB: 64 keys x 64 dims of fp16
-constexpr int kPtcQOff = 0;
-constexpr int kPtcKOff = kPtcQOff + 4 * kPtcRegion;
+constexpr int kPtcKOff = 0;
 constexpr int kPtcVOff = kPtcKOff + kPtcStages * 2 * kPtcHalfTile;
-constexpr int kPtcPOff = kPtcVOff + kPtcStages * 2 * kPtcHalfTile;
-constexpr int kPtcBarOff = kPtcPOff + 4 * kPtcRegion;
+constexpr int kPtcBarOff = kPtcVOff + kPtcStages * 2 * kPtcHalfTile;
 constexpr int kPtcBarBytes = 256;
 constexpr int kPtcSmem = kPtcBarOff + kPtcBarBytes + 1024;  // + alignment slack
 static_assert(kPtcSmem <= 232448, "shared memory per CTA");
 static_assert((4 * kPtcStages + 9) * 8 + 8 <= kPtcBarBytes, "barrier area");
 
-// Tensor memory columns: S[0], S[1] (64 each), then O (128).
-constexpr uint32_t kPtcTmemCols = 256;
-constexpr uint32_t kPtcSCol = 0, kPtcOCol = 2 * kPtcKeys;
+// Tensor memory columns (32-bit): q hi, q lo (64 each: 128 fp16), S[0], S[1]
+// (64 fp32 each), P[0], P[1] (hi then lo, 32 each: 64 fp16), O (128 fp32).
+constexpr uint32_t kPtcTmemCols = 512;
+constexpr uint32_t kPtcQCol = 0, kPtcSCol = 128, kPtcPCol = 256, kPtcOCol = 384;
 // Lazy rescaling: p = 2^(s - m_ref + kPtcOffset), m_ref moves when a score
 // passes m_ref + kPtcSlack, so p < 2^(kPtcOffset + kPtcSlack) = 2^15 < fp16 max.
 constexpr float kPtcOffset = 8.f, kPtcSlack = 7.f;
@@ -101,6 +102,16 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t tmem, uint64_t adesc, uint64
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// The same with A in tensor memory (K-major: row = lane, two fp16 per column).
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -152,6 +163,16 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[N], i
         : "memory");
 }
 
+template <int N>
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[N], int off) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(v[off + 0]), "r"(v[off + 1]), "r"(v[off + 2]), "r"(v[off + 3]), "r"(v[off + 4]),
+          "r"(v[off + 5]), "r"(v[off + 6]), "r"(v[off + 7]), "r"(v[off + 8]), "r"(v[off + 9]), "r"(v[off + 10]),
+          "r"(v[off + 11]), "r"(v[off + 12]), "r"(v[off + 13]), "r"(v[off + 14]), "r"(v[off + 15])
+        : "memory");
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -165,12 +186,6 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint3
     const __half2 l = __floats2half2_rn(a - back.x, b - back.y);
     hi = *reinterpret_cast<const uint32_t*>(&h);
     lo = *reinterpret_cast<const uint32_t*>(&l);
-}
-
-// Byte offset of 16-byte chunk `chunk` (0-7) of row `row` inside a
-// 128-byte-swizzled K-major region of 128-byte rows.
-__device__ __forceinline__ int sw128_offset(int row, int chunk) {
-    return (row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4);
 }
 
 __global__ void __launch_bounds__(kPtcThreads, 1)
@@ -227,10 +242,8 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    auto q_region = [&](int part, int half) { return smem + kPtcQOff + (part * 2 + half) * kPtcRegion; };
     auto k_half = [&](int s, int half) { return smem + kPtcKOff + (s * 2 + half) * kPtcHalfTile; };
     auto v_half = [&](int s, int half) { return smem + kPtcVOff + (s * 2 + half) * kPtcHalfTile; };
-    auto p_region = [&](int b, int part) { return smem + kPtcPOff + (b * 2 + part) * kPtcRegion; };
 
     // Each waiter below meets every phase of the barriers it waits on in
     // order, at most one phase behind (see the row warps' V tail wait).
@@ -273,10 +286,11 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
 #pragma unroll
                 for (int part = 0; part < 2; ++part)
 #pragma unroll
-                    for (int kk = 0; kk < kPtcDim / 16; ++kk) {  // 16 dims = 32 bytes = +2 in the address field
-                        const uint64_t a = sw128_desc(q_region(part, kk >> 2)) + 2 * (kk & 3);
+                    for (int kk = 0; kk < kPtcDim / 16; ++kk) {
+                        // A: 16 dims = 8 columns of q; B: 16 dims = 32 bytes = +2 in the address field
+                        const uint32_t a = tmem + kPtcQCol + 64 * part + 8 * kk;
                         const uint64_t bd = sw128_desc(k_half(s, kk >> 2)) + 2 * (kk & 3);
-                        tc_mma_f16(tmem + kPtcSCol + b * kPtcKeys, a, bd, kPtcIdescS, (part | kk) != 0);
+                        tc_mma_f16_ts(tmem + kPtcSCol + b * kPtcKeys, a, bd, kPtcIdescS, (part | kk) != 0);
                     }
                 tc_commit(&k_empty[s]);
                 tc_commit(&s_full[b]);
@@ -292,10 +306,10 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
                 for (int part = 0; part < 2; ++part)
 #pragma unroll
                     for (int kk = 0; kk < kPtcKeys / 16; ++kk) {
-                        // A: 16 keys = 32 bytes along the P row; B: 16 keys = 2 groups of 8 rows = 2048 bytes
-                        const uint64_t a = sw128_desc(p_region(b, part)) + 2 * kk;
+                        // A: 16 keys = 8 columns of P; B: 16 keys = 2 groups of 8 rows = 2048 bytes
+                        const uint32_t a = tmem + kPtcPCol + 64 * b + 32 * part + 8 * kk;
                         const uint64_t bd = sw128_mn_desc(v_half(s, 0) + kk * 2048, kPtcHalfTile);
-                        tc_mma_f16(tmem + kPtcOCol, a, bd, kPtcIdescPV, (j | part | kk) != 0);
+                        tc_mma_f16_ts(tmem + kPtcOCol, a, bd, kPtcIdescPV, (j | part | kk) != 0);
                     }
                 tc_commit(&v_empty[s]);
                 tc_commit(o_full);
@@ -311,36 +325,34 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
             tc_commit(mma_done);  // arrives once every MMA issued above has completed
         }
     } else {  // row warps: thread = query row r = 32 h + i
-        const int h = warp, i = lane, r = 32 * h + i;
+        const int h = warp, i = lane;  // query row 32 h + i = this thread's TMEM lane
         const bool valid = i < nq;
         const int pos = valid ? positions[q0 + i] : -1;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * h) << 16);
         {
             const float* qrow = qkv + static_cast<long long>(q0 + (valid ? i : 0)) * qkv_stride +
                                 static_cast<long long>(kvh * kPtcGroups + h) * kPtcDim;
-#pragma unroll 4
-            for (int c = 0; c < kPtcDim / 8; ++c) {  // 8 dims = one 16-byte chunk per part
-                float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
-                if (valid) {
-                    x0 = reinterpret_cast<const float4*>(qrow)[2 * c];
-                    x1 = reinterpret_cast<const float4*>(qrow)[2 * c + 1];
+#pragma unroll 1
+            for (int c0 = 0; c0 < kPtcDim; c0 += 32) {  // 32 dims = 16 columns per part
+                uint32_t hi[16], lo[16];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (valid) x = reinterpret_cast<const float4*>(qrow + c0)[c];
+                    split_pair(x.x, x.y, hi[2 * c], lo[2 * c]);
+                    split_pair(x.z, x.w, hi[2 * c + 1], lo[2 * c + 1]);
                 }
-                uint4 hi, lo;
-                split_pair(x0.x, x0.y, hi.x, lo.x);
-                split_pair(x0.z, x0.w, hi.y, lo.y);
-                split_pair(x1.x, x1.y, hi.z, lo.z);
-                split_pair(x1.z, x1.w, hi.w, lo.w);
-                const int off = sw128_offset(r, c & 7);
-                *reinterpret_cast<uint4*>(q_region(0, c >> 3) + off) = hi;
-                *reinterpret_cast<uint4*>(q_region(1, c >> 3) + off) = lo;
+                tmem_st16u(lane_base + kPtcQCol + c0 / 2, hi, 0);
+                tmem_st16u(lane_base + kPtcQCol + 64 + c0 / 2, lo, 0);
             }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         }
-        fence_proxy_async_smem();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(q_ready);
 
         // log2(e) / sqrt(128): scores in base-2 units
         const float score_scale = 1.4426950408889634f * 0.08838834764831845f;
-        const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * h) << 16);
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
 
@@ -405,24 +417,22 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
             float part[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) part[k] = 0.f;
-            uint8_t* ph = p_region(b, 0);
-            uint8_t* pl = p_region(b, 1);
 #pragma unroll
-            for (int c = 0; c < kPtcKeys / 8; ++c) {
-                float pv[8];
+            for (int c0 = 0; c0 < kPtcKeys; c0 += 32) {  // 32 keys = 16 columns per part
+                uint32_t hi[16], lo[16];
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    pv[k] = ex2_approx(__fmaf_rn(sv[8 * c + k], score_scale, nbase));
-                    part[k] += pv[k];
+                for (int c = 0; c < 32; c += 8) {
+                    float pv[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        pv[k] = ex2_approx(__fmaf_rn(sv[c0 + c + k], score_scale, nbase));
+                        part[k] += pv[k];
+                    }
+#pragma unroll
+                    for (int k = 0; k < 8; k += 2) split_pair(pv[k], pv[k + 1], hi[(c + k) / 2], lo[(c + k) / 2]);
                 }
-                uint4 hi, lo;
-                split_pair(pv[0], pv[1], hi.x, lo.x);
-                split_pair(pv[2], pv[3], hi.y, lo.y);
-                split_pair(pv[4], pv[5], hi.z, lo.z);
-                split_pair(pv[6], pv[7], hi.w, lo.w);
-                const int off = sw128_offset(r, c);
-                *reinterpret_cast<uint4*>(ph + off) = hi;
-                *reinterpret_cast<uint4*>(pl + off) = lo;
+                tmem_st16u(lane_base + kPtcPCol + 64 * b + c0 / 2, hi, 0);
+                tmem_st16u(lane_base + kPtcPCol + 64 * b + 32 + c0 / 2, lo, 0);
             }
             l += ((part[0] + part[4]) + (part[2] + part[6])) + ((part[1] + part[5]) + (part[3] + part[7]));
             if (j == tiles - 1 && max_ctx < kbase + kPtcKeys) {
@@ -445,8 +455,9 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
                         make_uint4(0u, 0u, 0u, 0u);
                 }
             }
-            fence_proxy_async_smem();  // P (and the zeroed V rows) -> visible to the tensor cores
-            tc_fence_before();         // ... after the O rescale's tensor-memory stores
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");  // P (and any O rescale) written
+            fence_proxy_async_smem();  // the zeroed V rows -> visible to the tensor cores
+            tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[b]);
         }
