@@ -4,23 +4,27 @@
 // the same contract and result bits as gemm.cu (integer sums are exact).
 //
 // Tile: 128 weight rows (the MMA's M) x TOK tokens (its N: 64, 128 or 256),
-// K advancing 128 per pipeline stage. A CTA has eighteen warps:
-//   warp 16 lane 0: TMA producer -- per stage, the packed weight tile
-//           (128 rows x 64 bytes, no swizzle) and the activation tile (TOK
-//           rows x 128 bytes, 128-byte swizzle) land on the stage's `full`
-//           mbarrier; warp 16 also allocates and frees the tensor memory;
-//   warps 0-15: unpack the packed tile into signed int8 codes in the
-//           K-major 128-byte-swizzled layout the MMA reads, then arrive on
-//           `aready`. They work as four groups of four warps, group g taking
-//           stages g, g + 4, ...: four stages unpack at once and every
-//           scheduler holds four unpack warps, so the unpack (which paces
-//           the pipeline) is not one stage's dependent latency at a time.
-//           After the last stage they are the epilogue, warp w reading TMEM
-//           lane quarter w % 4 (32 rows) for column slice w / 4;
-//   warp 17 lane 0: issues tcgen05.mma kind::i8 (A s8 weights, B s8
-//           activations, D s32 in TMEM), 4 per stage (K = 32 each), and
-//           tcgen05.commit to the stage's `empty` mbarrier, which frees the
-//           stage for the producer; a final commit signals the epilogue.
+// K advancing 128 per pipeline stage. A CTA has 4 G + 2 warps (G unpack
+// groups: 5 at TOK 256, else 4):
+//   warp 4 G lane 0: TMA producer -- per stage, the packed weight tile
+//           (128 rows x 64 bytes, 64-byte swizzle) and the activation tile
+//           (TOK rows x 128 bytes, 128-byte swizzle) land on the stage's
+//           `full` mbarrier; the warp also allocates and frees the tensor
+//           memory. Shared memory holds only this ring (5 stages at TOK
+//           256, 8 at 128, 12 at 64);
+//   warps 0 .. 4 G - 1: unpack groups of four warps, group g taking stages
+//           g, g + G, ...: thread = weight row (its warp's TMEM lane quarter),
+//           it reads the row's 64 packed bytes, expands them to 128 signed
+//           int8 codes and stores them with tcgen05.st into the group's
+//           unpacked tile in tensor memory (32 columns, four codes per
+//           column) -- the MMA's A operand -- then arrives on `aready`. After
+//           the last stage the first sixteen warps are the epilogue, warp w
+//           reading TMEM lane quarter w % 4 (32 rows) for column slice w / 4;
+//   warp 4 G + 1 lane 0: issues tcgen05.mma kind::i8 (A s8 weights from
+//           tensor memory, B s8 activations from shared memory, D s32 in
+//           TMEM), 4 per stage (K = 32 each), and tcgen05.commit to the
+//           stage's `empty` and the group's `afree`; a final commit signals
+//           the epilogue.
 // Every wait is bounded (mbar_wait). A role whose wait runs out reports
 // kStatusWaitTimeout, marks the CTA as failed and stops issuing; the
 // producer still waits for the copies it issued, the MMA thread still
@@ -33,31 +37,34 @@ namespace h4b {
 
 constexpr int kTcRows = 128;     // weight rows per CTA (MMA M)
 constexpr int kTcK = 128;        // k per stage: one 128-byte swizzle atom of int8
-constexpr int kTcUnpackGroups = 4, kTcGroupWarps = 4;
-constexpr int kTcUnpackWarps = kTcUnpackGroups * kTcGroupWarps;
-constexpr int kTcThreads = 32 * (kTcUnpackWarps + 2);  // + producer warp + MMA warp
-constexpr int kTcProducerWarp = kTcUnpackWarps, kTcMmaWarp = kTcUnpackWarps + 1;
+constexpr int kTcGroupWarps = 4;  // an unpack group: one warp per TMEM lane quarter
 
 template <int TOK>
 struct TcCfg {
-    static constexpr int kABytes = kTcRows * kTcK;           // one unpacked weight tile, int8
+    // Unpack groups: group g owns the k-steps g, g + kGroups, ... and one
+    // unpacked weight tile in tensor memory. The stage count is a multiple of
+    // the groups, so a group always revisits its own stages round by round.
+    static constexpr int kGroups = TOK == 256 ? 5 : 4;
+    static constexpr int kStages = TOK == 256 ? 5 : (TOK == 128 ? 8 : 12);
+    static constexpr int kUnpackWarps = kGroups * kTcGroupWarps;
+    static constexpr int kProducerWarp = kUnpackWarps, kMmaWarp = kUnpackWarps + 1;
+    static constexpr int kThreads = 32 * (kUnpackWarps + 2);
     static constexpr int kBBytes = TOK * kTcK;               // activations, int8
     static constexpr int kPackedBytes = kTcRows * kTcK / 2;  // packed weights
     static constexpr int kBOff = 0, kPackedOff = kBBytes;    // inside a TMA stage
     static constexpr int kStageBytes = kBBytes + kPackedBytes;
-    // A multiple of the unpack groups: group g then owns stages g, g + 4, ...
-    // and visits each in round order (see the kernel comment).
-    static constexpr int kStages = TOK == 64 ? 8 : 4;
-    static constexpr int kAOff = 0;                                  // kTcUnpackGroups unpacked tiles
-    static constexpr int kStageOff = kTcUnpackGroups * kABytes;      // then the TMA stages
-    static constexpr int kBarrierOff = kStageOff + kStages * kStageBytes;
-    static constexpr int kBarrierBytes = 256;
+    static constexpr int kBarrierOff = kStages * kStageBytes;
+    static constexpr int kBarrierBytes = 512;
     static constexpr int kSmem = kBarrierOff + kBarrierBytes + 1024;  // + alignment slack
-    static constexpr uint32_t kTmemCols = TOK;
-    static_assert(kStageBytes % 1024 == 0 && kABytes % 1024 == 0, "tiles keep the 1024-byte swizzle alignment");
-    static_assert(kStages % kTcUnpackGroups == 0, "each group must own whole stages");
+    // tensor memory: the accumulator (TOK columns), then one unpacked weight
+    // tile per group (128 rows x 128 int8 = 32 columns)
+    static constexpr uint32_t kACol = TOK;
+    static constexpr uint32_t kTmemCols = TOK + 32 * kGroups <= 256 ? 256 : 512;
+    static_assert(kStageBytes % 1024 == 0, "tiles keep the 1024-byte swizzle alignment");
+    static_assert(kStages % kGroups == 0, "each group must own whole stages");
     static_assert(kSmem <= 232448, "shared memory per CTA");
-    static_assert(2 * kStages * 8 + 2 * kTcUnpackGroups * 8 + 16 <= kBarrierBytes, "barrier area");
+    static_assert(TOK + 32 * kGroups <= kTmemCols, "tensor memory");
+    static_assert(2 * kStages * 8 + 2 * kGroups * 8 + 16 <= kBarrierBytes, "barrier area");
 };
 
 struct TcArgs {
@@ -107,6 +114,17 @@ __device__ __forceinline__ void tc_mma_i8(uint32_t tmem, uint64_t adesc, uint64_
         : "memory");
 }
 
+// The same with A (the unpacked weights) in tensor memory: row = lane, four
+// int8 codes per 32-bit column in k order.
+__device__ __forceinline__ void tc_mma_i8_ts(uint32_t tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  ::"r"(smem_addr(bar)) : "memory");
@@ -133,7 +151,7 @@ __device__ __forceinline__ uint32_t nib_s8(uint32_t w, uint32_t selector) {
 }
 
 template <int TOK>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
     int4_gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                         const TcArgs g) {
     using C = TcCfg<TOK>;
@@ -145,8 +163,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarrierOff);  // TMA stage landed
     uint64_t* empty = full + C::kStages;                                   // TMA stage consumed by the MMAs
     uint64_t* aready = empty + C::kStages;                                 // unpacked tile g written
-    uint64_t* afree = aready + kTcUnpackGroups;                            // unpacked tile g read by the MMAs
-    uint64_t* accfull = afree + kTcUnpackGroups;
+    uint64_t* afree = aready + C::kGroups;                                 // unpacked tile g read by the MMAs
+    uint64_t* accfull = afree + C::kGroups;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accfull + 1);
     volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -164,7 +182,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int a = 0; a < kTcUnpackGroups; ++a) {
+        for (int a = 0; a < C::kGroups; ++a) {
             mbar_init(&aready[a], kTcGroupWarps);
             mbar_init(&afree[a], 1);
         }
@@ -172,7 +190,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         *failed = wait_failed_before() ? 1 : 0;
         fence_mbar_init();
     }
-    if (warp == kTcProducerWarp) {
+    if (warp == C::kProducerWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      ::"r"(smem_addr(tmem_slot)), "r"(C::kTmemCols) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -181,15 +199,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    auto stage = [&](int s) { return smem + C::kStageOff + s * C::kStageBytes; };
-    auto atile = [&](int a) { return smem + C::kAOff + a * C::kABytes; };
+    auto stage = [&](int s) { return smem + s * C::kStageBytes; };
 
     // Every waiter below meets each barrier's phases in order (a parity wait
     // cannot tell a phase from the one two rounds later): the producer and
     // the MMA thread walk all iterations in order; unpack group g handles
-    // iterations g, g + 4, ..., whose TMA stages (it % kStages, a multiple
-    // of 4 apart) and unpacked tile (g) are its own.
-    if (warp == kTcProducerWarp) {
+    // iterations g, g + kGroups, ..., whose TMA stages (it % kStages, a
+    // multiple of kGroups apart) and unpacked tile (g) are its own.
+    if (warp == C::kProducerWarp) {
         if (lane == 0) {  // TMA producer
             int issued = 0;
             if (!*failed) {
@@ -213,54 +230,73 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int it = issued > C::kStages ? issued - C::kStages : 0; it < issued; ++it)
                 mbar_wait(&full[it % C::kStages], (it / C::kStages) & 1);
         }
-    } else if (warp == kTcMmaWarp) {
+    } else if (warp == C::kMmaWarp) {
         if (lane == 0) {  // MMA issuer
             constexpr uint32_t idesc = tc_idesc<TOK>();
             for (int it = 0; it < steps && !*failed; ++it) {
-                const int s = it % C::kStages, a = it % kTcUnpackGroups;
+                const int s = it % C::kStages, a = it % C::kGroups;
                 if (!mbar_wait(&full[s], (it / C::kStages) & 1) ||
-                    !mbar_wait(&aready[a], (it / kTcUnpackGroups) & 1)) {
+                    !mbar_wait(&aready[a], (it / C::kGroups) & 1)) {
                     *failed = 1;
                     break;
                 }
                 tc_fence_after();
-                const uint64_t adesc = sw128_desc(atile(a)), bdesc = sw128_desc(stage(s) + C::kBOff);
+                const uint64_t bdesc = sw128_desc(stage(s) + C::kBOff);
+                const uint32_t atmem = tmem + C::kACol + 32 * a;
 #pragma unroll
-                for (int kk = 0; kk < kTcK / 32; ++kk)  // +32 bytes along K = +2 in the start-address field
-                    tc_mma_i8(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (it | kk) != 0);
+                for (int kk = 0; kk < kTcK / 32; ++kk)  // K = 32: 8 columns of A, +32 bytes (+2) along B
+                    tc_mma_i8_ts(tmem, atmem + 8 * kk, bdesc + 2 * kk, idesc, (it | kk) != 0);
                 tc_commit(&empty[s]);
                 tc_commit(&afree[a]);
             }
             tc_commit(accfull);  // arrives once every MMA issued above has completed
         }
     } else {  // unpack groups, then the epilogue
-        const int group = warp / kTcGroupWarps;
-        const int t = threadIdx.x - group * 32 * kTcGroupWarps;  // thread within the group
-        for (int it = group; it < steps; it += kTcUnpackGroups) {
+        // group g = warp / 4; the warp's lane quarter (warp % 4) holds weight
+        // rows 32 (warp % 4) + lane of the tile, one row per thread
+        const int group = warp / kTcGroupWarps, quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        for (int it = group; it < steps; it += C::kGroups) {
             const int s = it % C::kStages;
-            const int use = it / kTcUnpackGroups;  // this group's tile use count
+            const int use = it / C::kGroups;  // this group's tile use count
             const bool ok = __all_sync(0xffffffffu, !*failed && (use == 0 || mbar_wait(&afree[group], (use - 1) & 1)) &&
                                                         mbar_wait(&full[s], (it / C::kStages) & 1));
             if (!ok) {
                 if (lane == 0) *failed = 1;
                 break;
             }
-            const uint8_t* packed = stage(s) + C::kPackedOff;
-            uint8_t* a = atile(group);
+            tc_fence_after();
+            // the packed tile lands 64-byte swizzled: chunk c of row r at
+            // r * 64 + 16 (c ^ ((r >> 1) & 3)), so a warp's rows hit distinct banks
+            const uint8_t* prow = stage(s) + C::kPackedOff + row * 64;
+            uint32_t codes[32];
 #pragma unroll
-            for (int i = 0; i < kTcRows * kTcK / 2 / 16 / (32 * kTcGroupWarps); ++i) {
-                const int c = i * 32 * kTcGroupWarps + t;  // 16-byte packed chunk: row c / 4, k bytes 32 * (c % 4) ..
-                const int row = c >> 2, piece = c & 3, sw = row & 7;
-                const uint4 w = *reinterpret_cast<const uint4*>(packed + c * 16);
-                const uint4 lo = make_uint4(nib_s8(w.x, 0x1100), nib_s8(w.x, 0x3322), nib_s8(w.y, 0x1100),
-                                            nib_s8(w.y, 0x3322));
-                const uint4 hi = make_uint4(nib_s8(w.z, 0x1100), nib_s8(w.z, 0x3322), nib_s8(w.w, 0x1100),
-                                            nib_s8(w.w, 0x3322));
-                uint8_t* rowp = a + (row >> 3) * 1024 + sw * 128;
-                *reinterpret_cast<uint4*>(rowp + (((2 * piece) ^ sw) << 4)) = lo;
-                *reinterpret_cast<uint4*>(rowp + (((2 * piece + 1) ^ sw) << 4)) = hi;
+            for (int c = 0; c < 4; ++c) {  // 16 packed bytes = 32 codes = 8 columns
+                const uint4 w = *reinterpret_cast<const uint4*>(prow + ((c ^ ((row >> 1) & 3)) << 4));
+                codes[8 * c + 0] = nib_s8(w.x, 0x1100);
+                codes[8 * c + 1] = nib_s8(w.x, 0x3322);
+                codes[8 * c + 2] = nib_s8(w.y, 0x1100);
+                codes[8 * c + 3] = nib_s8(w.y, 0x3322);
+                codes[8 * c + 4] = nib_s8(w.z, 0x1100);
+                codes[8 * c + 5] = nib_s8(w.z, 0x3322);
+                codes[8 * c + 6] = nib_s8(w.w, 0x1100);
+                codes[8 * c + 7] = nib_s8(w.w, 0x3322);
             }
-            fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core's reads
+            const uint32_t acol = lane_base + C::kACol + 32 * group;
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                asm volatile(
+                    "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+                    "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+                    ::"r"(acol + 16 * h), "r"(codes[16 * h + 0]), "r"(codes[16 * h + 1]), "r"(codes[16 * h + 2]),
+                      "r"(codes[16 * h + 3]), "r"(codes[16 * h + 4]), "r"(codes[16 * h + 5]), "r"(codes[16 * h + 6]),
+                      "r"(codes[16 * h + 7]), "r"(codes[16 * h + 8]), "r"(codes[16 * h + 9]), "r"(codes[16 * h + 10]),
+                      "r"(codes[16 * h + 11]), "r"(codes[16 * h + 12]), "r"(codes[16 * h + 13]),
+                      "r"(codes[16 * h + 14]), "r"(codes[16 * h + 15])
+                    : "memory");
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();  // tensor-memory stores -> ordered before the MMAs that read them
             __syncwarp();
             if (lane == 0) mbar_arrive(&aready[group]);
         }
@@ -268,8 +304,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // columns (tokens) of slice w / 4
         const bool done = __all_sync(0xffffffffu, mbar_wait(accfull, 0) && !*failed);
         tc_fence_after();
-        if (done) {
-            constexpr int kSlices = kTcUnpackWarps / 4, kCols = TOK / kSlices;
+        if (done && warp < 16) {  // the first sixteen warps: four column slices per lane quarter
+            constexpr int kSlices = 4, kCols = TOK / kSlices;
             static_assert(kCols % 16 == 0, "column slices of whole 16-column loads");
             const int quarter = warp & 3, slice = warp >> 2;
             const int row = n0 + quarter * 32 + lane;
@@ -312,7 +348,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == kTcProducerWarp) {
+    if (warp == C::kProducerWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols)
                      : "memory");
@@ -362,10 +398,10 @@ struct MapKeyHash {
 // A row-major uint8 matrix [outer][inner] as a 2-D tensor map with box
 // [box_outer][box_inner]; rows past `outer` read as zeros.
 bool byte_matrix_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
-                     uint32_t box_outer, bool swizzle128) {
+                     uint32_t box_outer, int swizzle_bytes) {
     static std::mutex lock;
     static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
-    const MapKey key{base, inner, outer, box_inner, box_outer, swizzle128 ? 1u : 0u};
+    const MapKey key{base, inner, outer, box_inner, box_outer, static_cast<uint32_t>(swizzle_bytes)};
     std::lock_guard<std::mutex> guard(lock);
     auto hit = cache.find(key);
     if (hit != cache.end()) {
@@ -380,7 +416,8 @@ bool byte_matrix_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_
     const cuuint32_t elem[2] = {1, 1};
     if (encode(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
                CU_TENSOR_MAP_INTERLEAVE_NONE,
-               swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+               swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                    : (swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE),
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return false;
     if (cache.size() > 8192) cache.clear();
@@ -423,8 +460,8 @@ int launch_tc(const GemmArgs& g, cudaStream_t stream) {
         opted_in[dev].store(true, std::memory_order_release);
     }
     CUtensorMap wmap, xmap;
-    if (!byte_matrix_map(&wmap, g.w, static_cast<uint64_t>(g.K) / 2, g.N, kTcK / 2, kTcRows, false) ||
-        !byte_matrix_map(&xmap, g.x, g.K, g.M, kTcK, TOK, true))
+    if (!byte_matrix_map(&wmap, g.w, static_cast<uint64_t>(g.K) / 2, g.N, kTcK / 2, kTcRows, 64) ||
+        !byte_matrix_map(&xmap, g.x, g.K, g.M, kTcK, TOK, 128))
         return H4B_EUNSUPPORTED;
     // Few output tiles (o / down / qkv at M <= 64 give 20-48 of them): split K
     // so the grid fills the SMs, each slice at least 4 k-steps, the int32
@@ -437,7 +474,7 @@ int launch_tc(const GemmArgs& g, cudaStream_t stream) {
     const TcArgs a{g.act_scale, g.w_scale, g.out, g.M, g.N, g.K, g.out_i32, ksplit > 1 ? g.split_acc : nullptr,
                    g.residual ? 1 : 0};
     const dim3 grid((g.M + TOK - 1) / TOK, g.N / kTcRows, ksplit);
-    int4_gemm_tc_kernel<TOK><<<grid, kTcThreads, C::kSmem, stream>>>(wmap, xmap, a);
+    int4_gemm_tc_kernel<TOK><<<grid, C::kThreads, C::kSmem, stream>>>(wmap, xmap, a);
     H4B_CUDA_TRY(cudaGetLastError());
     if (ksplit > 1) {
         const long long n = static_cast<long long>(g.M) * g.N;
