@@ -722,6 +722,7 @@ def run_prefill(args) -> int:
             torch.cuda.synchronize()
             times.append(start.elapsed_time(end) / 1000.0)
     elapsed = sum(times)
+    attention = prefill_attention_record(model, state, P, args.prefill_attention)
     H, I, Q, KV = model.hidden, model.intermediate, model.q_size, model.kv_size
     body_macs = model.n_layers * (H * (Q + 2 * KV) + Q * H + H * 2 * I + I * H)
     ops_per_prefill = 2 * body_macs * P + 2 * model.vocab * H
@@ -739,10 +740,47 @@ def run_prefill(args) -> int:
                      "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOP/s",
                      "frac": round(achieved / int8_peak, 4), "ops_per_step": int(ops_per_prefill),
                      "peak_source": "2 x measured bf16 dense (int8 dense rate is twice bf16 on B200)"},
-        "clocks": clocks.summary(), "device_status": model.status(),
+        "attention": attention, "clocks": clocks.summary(), "device_status": model.status(),
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def prefill_attention_record(model, state, P: int, attention: str, reps: int = 20) -> dict:
+    """The prompt attention kernel alone (h4b_prefill_attention on the last
+    layer, after a prefill of P tokens from position 0), CUDA-event timed on
+    the state's stream: algorithmic flops = 2 products x 2 flops x head_dim
+    x sum of the rows' contexts x q heads."""
+    import ctypes
+
+    import torch
+
+    from harsh4b_b200._lib import check, lib
+
+    scratch = model._prefill_scratch
+    call = lambda: check(lib().h4b_prefill_attention(ctypes.byref(model.desc), ctypes.byref(state.desc),
+                                                     ctypes.byref(scratch.desc), P, model.n_layers - 1,
+                                                     state.stream.cuda_stream), "h4b_prefill_attention")
+    with torch.cuda.stream(state.stream):
+        for _ in range(3):
+            call()
+        start, end = _event_pair(torch)
+        start.record(state.stream)
+        for _ in range(reps):
+            call()
+        end.record(state.stream)
+    torch.cuda.synchronize()
+    us = start.elapsed_time(end) * 1000.0 / reps
+    flops = 4 * model.head_dim * (P * (P + 1) // 2) * model.heads
+    peak = measured_bf16_tflops()
+    achieved = flops / us / 1e6
+    tensor = attention == "tensor"
+    kernel = "prefill_attention_tc_kernel" if tensor else "prefill_attention_block_kernel"
+    return {"kernel": kernel, "bound": "tensor" if tensor else "fp32 FMA (CUDA cores, the decode order)",
+            "us_per_layer": round(us, 2), "flops_per_layer": flops,
+            "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+            "peak_source": "measured bf16 dense burst (fp16 runs at the bf16 rate)",
+            "note": "algorithmic flops; the tensor kernel issues twice as many MMA flops (q and p as hi + lo fp16)"}
 
 
 def measured_bf16_tflops() -> float:

@@ -107,6 +107,8 @@ _SIGNATURES = {
     "h4b_residual_acc": [_vp, _vp, _vp, _vp, _i32, _vp],
     "h4b_decode_batch": [ctypes.POINTER(ModelDesc), ctypes.POINTER(BatchStateDesc), _vp],
     "h4b_batch_attention": [ctypes.POINTER(ModelDesc), ctypes.POINTER(BatchStateDesc), _i32, _vp],
+    "h4b_prefill_attention": [ctypes.POINTER(ModelDesc), ctypes.POINTER(StateDesc), ctypes.POINTER(PrefillScratchDesc),
+                              _i32, _i32, _vp],
     "h4b_tp_buffer_bytes": [_i32, _i32],
     "h4b_ipc_alloc": [ctypes.c_longlong, ctypes.POINTER(_vp), _vp],
     "h4b_ipc_open": [_vp, ctypes.POINTER(_vp)],

@@ -257,6 +257,19 @@ struct PrefillRun {
                 m->norm_k + static_cast<size_t>(l) * d, m->rope_cos, m->rope_sin, m->eps, p->positions, count,
                 reinterpret_cast<__half*>(kc), reinterpret_cast<__half*>(vc), head_stride, d);
         H4B_CUDA_TRY(cudaGetLastError());
+        return attention_only(l);
+    }
+    // The prompt rows' attention of layer l alone (q rows in p->qkv, already
+    // normalised and rotated; K/V appended): p->attended.
+    int attention_only(int l) const {
+        const int d = m->head_dim;
+        const int q_size = m->heads * d, kv_size = m->kv_heads * d, qkv_rows = q_size + 2 * kv_size;
+        const size_t kv_layer = static_cast<size_t>(m->kv_heads) * s->capacity * d;  // elements
+        const size_t eb = s->kv_dtype == 0 ? 4 : 2;
+        char* kc = static_cast<char*>(s->k_cache) + l * kv_layer * eb;
+        char* vc = static_cast<char*>(s->v_cache) + l * kv_layer * eb;
+        const long long head_stride = static_cast<long long>(s->capacity) * d;
+        int rc;
         if (p->attn_splits == 1 && p->attn_kernel == H4B_PREFILL_ATTN_TENSOR &&
             prefill_tc_supported(s->kv_dtype, d, m->heads / m->kv_heads))
             return launch_prefill_attention_tc(p->qkv, qkv_rows, reinterpret_cast<const __half*>(kc),
@@ -433,6 +446,15 @@ int prefill_tp_stage(const h4b_model* m, const h4b_state* s, const h4b_prefill_s
 extern "C" int h4b_prefill(const h4b_model* model, const h4b_state* state, const h4b_prefill_scratch* scratch,
                            int count, void* stream) {
     return h4b::prefill(model, state, scratch, count, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h4b_prefill_attention(const h4b_model* model, const h4b_state* state,
+                                     const h4b_prefill_scratch* scratch, int count, int layer, void* stream) {
+    int rc = h4b::validate_prefill(model, state, scratch, count);
+    if (rc) return rc;
+    if (layer < 0 || layer >= model->layers) return H4B_EINVAL;
+    const h4b::PrefillRun r{model, state, scratch, count, static_cast<cudaStream_t>(stream)};
+    return r.attention_only(layer);
 }
 
 extern "C" int h4b_prefill_tp_stage(const h4b_model* model, const h4b_state* state, const h4b_prefill_scratch* scratch,

@@ -377,6 +377,13 @@ typedef struct h4b_prefill_scratch {
 int h4b_prefill(const h4b_model *model, const h4b_state *state, const h4b_prefill_scratch *scratch, int count,
                 void *stream);
 
+/* The prompt attention of one layer alone, for timing: the `count` q rows
+ * left in scratch->qkv by an h4b_prefill of `count` tokens (normalised and
+ * rotated; the last layer's) against the session's cache for `layer`, with
+ * scratch->positions and scratch->attn_kernel, into scratch->attended. */
+int h4b_prefill_attention(const h4b_model *model, const h4b_state *state, const h4b_prefill_scratch *scratch,
+                          int count, int layer, void *stream);
+
 /* One stage of a tensor-parallel prefill on this rank's slice of the model
  * (its q/k/v heads, its MLP units, K-slices of o_proj and down_proj, its
  * vocabulary rows; x replicated): the reference's prefill loop

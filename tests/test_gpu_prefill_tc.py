@@ -161,3 +161,28 @@ def test_unsupported_shapes_fall_back_to_the_exact_kernel():
     np.testing.assert_array_equal(out["tensor"], out["exact"])
     with pytest.raises(ValueError):
         model.prefill(prompt, model.new_state(64), attention="fast")
+
+
+@pytest.mark.parametrize("attention", ["tensor", "exact"])
+def test_prefill_attention_entry_repeats_the_layer(attention):
+    """h4b_prefill_attention (the timing entry) recomputes the last layer's
+    prompt attention from what the prefill left: the same bits."""
+    import ctypes
+
+    from harsh4b_b200._lib import check, lib
+
+    model = _one_layer_model(56)
+    prompt = synthetic_prompt(model.config, 97, seed=7)
+    state = model.new_state(128)
+    model.prefill(prompt, state, attention=attention)
+    scratch = model._prefill_scratch
+    first = scratch.attended[:97].clone()
+    scratch.attended.zero_()
+    check(lib().h4b_prefill_attention(ctypes.byref(model.desc), ctypes.byref(state.desc), ctypes.byref(scratch.desc),
+                                      97, 0, state.stream.cuda_stream), "h4b_prefill_attention")
+    torch.cuda.synchronize()
+    assert torch.equal(scratch.attended[:97], first)
+    assert lib().h4b_prefill_attention(ctypes.byref(model.desc), ctypes.byref(state.desc), ctypes.byref(scratch.desc),
+                                       97, 1, state.stream.cuda_stream) != 0  # no layer 1
+    assert model.status() == 0
+    state.close()
