@@ -4,22 +4,29 @@
 //
 // Per layer the prompt rows go through the same operations as a decode
 // token, M rows at a time: RMSNorm + per-token quantisation, the tensor-core
-// int4 GEMM (gemm_tc.cu) for qkv / o / gate-up / down, residual adds and
-// SwiGLU. Attention runs in two launches so no query reads a key that
+// int4 GEMM (gemm_tc.cu) for qkv / o / gate-up / down (o and down add into
+// x in their epilogue), SwiGLU fused into the quantisation of the down
+// input. Attention runs in two launches so no query reads a key that
 // another CTA of the same launch is writing:
 //   1. prefill_rope_append_kernel: q/k RMSNorm and RoPE for every prompt
 //      token and head (the decode kernel's norm_rope), q written back in
 //      place, k and v appended to the session's cache at their positions;
-//   2. gqa_split_kernel with one batch entry per query, all on the one
-//      cache (batch stride 0), positions p0 + i, and no append.
-// The second launch reads back the cache values the first one stored, in
+//   2. the prompt queries' attention over the cache, by the scratch's
+//      attn_kernel and attn_splits:
+//      - H4B_PREFILL_ATTN_TENSOR, one split (the default for an fp16 cache,
+//        head_dim 128, 4 q heads per kv head): prefill_attention_tc_kernel
+//        (prefill_tc.cu), tcgen05 MMAs with split-fp16 operands -- within
+//        the fp32 tolerance, not the decode's bits;
+//      - otherwise with one split: prefill_attention_block_kernel, blocks of
+//        16 queries sharing their K/V sub-tiles, each (query, head) in the
+//        decode kernel's order;
+//      - more splits: gqa_split_kernel with one batch entry per query on the
+//        one cache (batch stride 0), positions p0 + i, no append.
+// The exact kernels read back the cache values the first launch stored, in
 // the cache precision, exactly as the decode kernel stages its own new key
 // and value, so every prompt row equals a chain decode step with the same
-// attention splits bit for bit. The split count is the scratch's own: one
-// split (the default) lets each query's CTA walk its whole context, which
-// stays in L2 for the layer, with no partials and no merge. Only the last
-// row goes through the LM head (its logits and greedy token are what
-// forward_token returns).
+// attention splits bit for bit. Only the last row goes through the LM head
+// (its logits and greedy token are what forward_token returns).
 
 namespace h4b {
 
