@@ -201,7 +201,7 @@ def test_two_gpu_tensor_parallel_matches_oracle(config_name, graph, comm):
     assert status == 0
 
 
-def _tp_prefill_rank(rank, world, port, results):
+def _tp_prefill_rank(rank, world, port, results, attention="exact"):
     import datetime
 
     from harsh4b_b200.synthetic import qwen3_4b_config
@@ -216,7 +216,7 @@ def _tp_prefill_rank(rank, world, port, results):
         model = TensorParallelQwen(ck, kv_dtype="float16", attn_splits=16, comm="nccl")
         prompt = synthetic_prompt(config, PREFILL, seed=SEED)
         state = model.new_state(PREFILL + STEPS)
-        token, local = model.prefill(prompt, state, max_tokens=PREFILL_CHUNK, attention="exact")
+        token, local = model.prefill(prompt, state, max_tokens=PREFILL_CHUNK, attention=attention)
         rows, greedy = [], [token]
 
         def gather(local):
@@ -276,3 +276,46 @@ def test_two_gpu_tensor_parallel_prefill_matches_oracle():
     np.testing.assert_array_equal(rows, np.stack(want))
     assert greedy == want_greedy
     assert status == 0
+
+
+@pytest.mark.gpu
+def test_two_gpu_tensor_parallel_prefill_with_tensor_core_attention():
+    """The sharded prefill with the tcgen05 prompt attention equals the
+    single-GPU tcgen05 prefill bit for bit: each kv head's attention is the
+    same kernel on the same rows, the attended rows are quantised with the
+    global absmax and the o / down sums are exact int32 all-reduces; the
+    decode after it is the oracle-exact one."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from harsh4b_b200.model import CudaQwen
+    from harsh4b_b200.synthetic import qwen3_4b_config
+
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_prefill_rank, args=(r, 2, port, results, "tensor")) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        rows, greedy, status = results.get(timeout=600)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.exitcode is None:
+                p.kill()
+    assert all(p.exitcode == 0 for p in procs)
+    assert status == 0
+    config = qwen3_4b_config(num_hidden_layers=2)
+    ck = synthetic_checkpoint(config, seed=SEED)
+    model = CudaQwen.from_checkpoint(ck, kv_dtype="float16", mode="chain", attn_splits=16)
+    state = model.new_state(PREFILL + STEPS)
+    prompt = synthetic_prompt(config, PREFILL, seed=SEED)
+    want = [model.prefill(prompt, state, max_tokens=PREFILL_CHUNK, attention="tensor").cpu().numpy().copy()]
+    want_greedy = [int(np.argmax(want[-1]))]
+    for _ in range(STEPS - 1):
+        want.append(model.forward_token(want_greedy[-1], state).cpu().numpy().copy())
+        want_greedy.append(int(np.argmax(want[-1])))
+    np.testing.assert_array_equal(rows, np.stack(want))
+    assert greedy == want_greedy
+    assert model.status() == 0
+    state.close()
