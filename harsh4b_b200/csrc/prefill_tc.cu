@@ -21,22 +21,24 @@
 //
 // Operands: q (hi, lo) and the probability tiles P (hi, lo) live in tensor
 // memory, the A operands of the MMAs (row = lane, two fp16 per 32-bit
-// column); only the K and V tiles are read from shared memory, which keeps
-// the MMAs' shared-memory traffic to the tiles the TMA brings in.
+// column); only the K and V tiles are read from shared memory. A tile's P is
+// written over its own S columns once the row warps hold S in registers.
 //
 // Warps: 0-3 are the row warps (thread = query row; TMEM lane quarter =
 // warp), 4 loads K tiles and owns the tensor memory, 5 loads V tiles, 6
-// issues the MMAs (one elected thread). Per key tile j, with the score
-// accumulator S and the probability tile P double-buffered (b = j % 2), K and
-// V in kStages stages and one output accumulator O in tensor memory:
+// issues the MMAs (one elected thread). Per key tile j (128 keys), with the
+// score accumulator S (and P over it) double-buffered (b = j % 2), K and V in
+// kStages stages and one output accumulator O in tensor memory:
 //   MMA:   S[b] = Qhi K_j^T + Qlo K_j^T                  -> s_full[b], k_empty
-//   rows:  load S[b] (-> s_free[b]); masked maximum, p; P[b] = (phi, plo)
+//   rows:  load S[b]; masked maximum, p; P[b] = (phi, plo) over S[b]
 //                                                         -> p_full[b]
 //   MMA:   O += Phi V_j + Plo V_j                        -> o_full, v_empty
-// The MMA thread issues P.V for tile j, then S for tile j + 2: the tensor
-// cores compute the next scores while the row warps work on the softmax, and
-// s_full for tile j also stands for the completion of P.V j - 2 (a commit
-// tracks every earlier MMA of its thread).
+// The MMA thread issues P.V for tile j, then S for tile j + 2 into the same
+// columns: the tensor cores run a CTA's MMAs in issue order, so the P.V has
+// read P before the S overwrites it; and s_full for tile j also stands for
+// the completion of P.V j - 2 (a commit tracks every earlier MMA of its
+// thread). The tile is 128 keys so that each MMA does more work: the MMA
+// thread's issue of the many small MMAs of 64-key tiles was the bound.
 // O is scaled lazily: each row keeps a reference maximum m_ref and forms
 // p = 2^(s - m_ref + 8); only when a tile's maximum passes m_ref + 7 (p would
 // leave fp16's range) does the row move m_ref up, and the warp then rescales
@@ -53,28 +55,29 @@ namespace h4b {
 constexpr int kPtcPositions = 32;                          // prompt positions per CTA
 constexpr int kPtcGroups = 4;                              // q heads per kv head
 constexpr int kPtcRows = kPtcPositions * kPtcGroups;       // MMA M = 128
-constexpr int kPtcKeys = 64;                               // keys per tile (the S MMA's N)
+constexpr int kPtcKeys = 128;                              // keys per tile (the S MMA's N)
 constexpr int kPtcDim = 128;                               // head_dim (the P.V MMA's N)
 constexpr int kPtcStages = 3;                              // K and V tile stages
 constexpr int kPtcRowWarps = 4, kPtcKWarp = 4, kPtcVWarp = 5, kPtcMmaWarp = 6;
 constexpr int kPtcThreads = 32 * 7;
 
 // Shared memory, every tile 1024-byte aligned (the 128-byte swizzle atom):
-//   K: [stage][d half][64 keys x 128 B]                   kPtcStages x 16 KB
-//   V: [stage][d half][64 keys x 128 B]                   kPtcStages x 16 KB
-constexpr int kPtcHalfTile = kPtcKeys * 128;               // 8 KB: 64 keys x 64 dims of fp16
+//   K: [stage][d half][128 keys x 128 B]                  kPtcStages x 32 KB
+//   V: [stage][d half][128 keys x 128 B]                  kPtcStages x 32 KB
+constexpr int kPtcHalfTile = kPtcKeys * 128;               // 16 KB: 128 keys x 64 dims of fp16
 constexpr int kPtcKOff = 0;
 constexpr int kPtcVOff = kPtcKOff + kPtcStages * 2 * kPtcHalfTile;
 constexpr int kPtcBarOff = kPtcVOff + kPtcStages * 2 * kPtcHalfTile;
 constexpr int kPtcBarBytes = 256;
 constexpr int kPtcSmem = kPtcBarOff + kPtcBarBytes + 1024;  // + alignment slack
 static_assert(kPtcSmem <= 232448, "shared memory per CTA");
-static_assert((4 * kPtcStages + 9) * 8 + 8 <= kPtcBarBytes, "barrier area");
+static_assert((4 * kPtcStages + 7) * 8 + 8 <= kPtcBarBytes, "barrier area");
 
 // Tensor memory columns (32-bit): q hi, q lo (64 each: 128 fp16), S[0], S[1]
-// (64 fp32 each), P[0], P[1] (hi then lo, 32 each: 64 fp16), O (128 fp32).
+// (128 fp32 each; P[b] over S[b]: hi then lo, 64 columns each = 128 fp16),
+// O (128 fp32).
 constexpr uint32_t kPtcTmemCols = 512;
-constexpr uint32_t kPtcQCol = 0, kPtcSCol = 128, kPtcPCol = 256, kPtcOCol = 384;
+constexpr uint32_t kPtcQCol = 0, kPtcSCol = 128, kPtcOCol = 384;
 // Lazy rescaling: p = 2^(s - m_ref + kPtcOffset), m_ref moves when a score
 // passes m_ref + kPtcSlack, so p < 2^(kPtcOffset + kPtcSlack) = 2^15 < fp16 max.
 constexpr float kPtcOffset = 8.f, kPtcSlack = 7.f;
@@ -199,8 +202,7 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
     uint64_t* v_full = k_empty + kPtcStages;
     uint64_t* v_empty = v_full + kPtcStages;
     uint64_t* s_full = v_empty + kPtcStages;  // [2]
-    uint64_t* s_free = s_full + 2;             // [2]
-    uint64_t* p_full = s_free + 2;             // [2]
+    uint64_t* p_full = s_full + 2;             // [2]
     uint64_t* o_full = p_full + 2;             // one phase per P.V tile
     uint64_t* q_ready = o_full + 1;
     uint64_t* mma_done = q_ready + 1;
@@ -224,7 +226,6 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&s_full[b], 1);
-            mbar_init(&s_free[b], kPtcRowWarps);
             mbar_init(&p_full[b], kPtcRowWarps);
         }
         mbar_init(o_full, 1);
@@ -280,7 +281,6 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
             auto issue_s = [&](int j) -> bool {
                 const int s = j % kPtcStages, b = j & 1;
                 if (*failed) return false;
-                if (j >= 2 && !mbar_wait(&s_free[b], ((j - 2) >> 1) & 1)) return false;
                 if (!mbar_wait(&k_full[s], (j / kPtcStages) & 1)) return false;
                 tc_fence_after();
 #pragma unroll
@@ -307,7 +307,7 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < kPtcKeys / 16; ++kk) {
                         // A: 16 keys = 8 columns of P; B: 16 keys = 2 groups of 8 rows = 2048 bytes
-                        const uint32_t a = tmem + kPtcPCol + 64 * b + 32 * part + 8 * kk;
+                        const uint32_t a = tmem + kPtcSCol + kPtcKeys * b + 64 * part + 8 * kk;
                         const uint64_t bd = sw128_mn_desc(v_half(s, 0) + kk * 2048, kPtcHalfTile);
                         tc_mma_f16_ts(tmem + kPtcOCol, a, bd, kPtcIdescPV, (j | part | kk) != 0);
                     }
@@ -365,9 +365,6 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
 #pragma unroll
             for (int c0 = 0; c0 < kPtcKeys; c0 += 16) tmem_ld16_nowait(lane_base + kPtcSCol + b * kPtcKeys + c0, sv, c0);
             tmem_wait_regs(sv);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[b]);
 
             // causal mask (only tiles that reach past some row's position) and
             // the tile maximum, in raw q.k units (the scale is positive)
@@ -431,8 +428,8 @@ __global__ void __launch_bounds__(kPtcThreads, 1)
 #pragma unroll
                     for (int k = 0; k < 8; k += 2) split_pair(pv[k], pv[k + 1], hi[(c + k) / 2], lo[(c + k) / 2]);
                 }
-                tmem_st16u(lane_base + kPtcPCol + 64 * b + c0 / 2, hi, 0);
-                tmem_st16u(lane_base + kPtcPCol + 64 * b + 32 + c0 / 2, lo, 0);
+                tmem_st16u(lane_base + kPtcSCol + kPtcKeys * b + c0 / 2, hi, 0);
+                tmem_st16u(lane_base + kPtcSCol + kPtcKeys * b + 64 + c0 / 2, lo, 0);
             }
             l += ((part[0] + part[4]) + (part[2] + part[6])) + ((part[1] + part[5]) + (part[3] + part[7]));
             if (j == tiles - 1 && max_ctx < kbase + kPtcKeys) {
