@@ -74,6 +74,10 @@ def parse_args():
     parser.add_argument("--prompt-len", type=int, default=2048, help="batch / prefill workloads: prompt tokens")
     parser.add_argument("--prefill-attention", choices=("tensor", "exact"), default="tensor",
                         help="prefill workload: tcgen05 attention (tolerance) or the decode-order fp32 kernel")
+    parser.add_argument("--batch-attention", choices=("tensor", "exact"), default="tensor",
+                        help="batch workload: the tcgen05 attention (tolerance) or the decode-order fp32 one")
+    parser.add_argument("--batch-splits", type=int, default=16,
+                        help="batch workload: attention splits per sequence (the tensor kernel: at most this)")
     parser.add_argument("--context", type=int, default=4096, help="tp workload: context before decoding")
     parser.add_argument("--layers", type=int, default=None,
                         help="override the layer count (a smaller model for profiling captures; not the headline)")
@@ -618,7 +622,8 @@ def run_batch(args, rank=0, world=1, local_rank=0, dist=None) -> int:
     rng = np.random.default_rng([args.seed, B, P, rank])
     prompts = rng.integers(0, model.vocab, size=(B, P))
     capacity = P + 2 * (args.warmup + args.steps) + 2
-    state = model.new_batch_state(B, capacity)
+    splits = args.batch_splits
+    state = model.new_batch_state(B, capacity, attn_splits=splits, attention=args.batch_attention)
     t0 = time.perf_counter()
     for i in range(P):
         model.forward_batch(prompts[:, i], state)
@@ -676,7 +681,8 @@ def run_batch(args, rank=0, world=1, local_rank=0, dist=None) -> int:
         "config": {"workload": f"config3: batch {B}, {P}-token random prompts, greedy decode, tcgen05 GEMM body",
                    "batch": B, "prompt": P, "kv_dtype": args.kv_dtype, "layers": model.n_layers,
                    "context": [ctx0, ctx0 + args.steps], "l2": "inputs larger than L2",
-                   "prompt_feed_s": round(prompt_s, 2), "parallelism": f"replicas x{world}"},
+                   "prompt_feed_s": round(prompt_s, 2), "parallelism": f"replicas x{world}",
+                   "attention": args.batch_attention, "attn_splits": splits},
         "e2e": {"value": round(world * B * args.steps / e2e_elapsed, 1), "unit": "tok/s",
                 "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
         "roofline": {"bound": "hbm", "kernel": "whole batched step (weights + every sequence's K/V)",
@@ -905,7 +911,7 @@ def run_attention(args) -> int:
                 check(lib().h4b_decode_stage(ctypes.byref(model.desc), ctypes.byref(st.desc), 2, 0,
                                              torch.cuda.current_stream().cuda_stream), "h4b_decode_stage")
         else:
-            st = model.new_batch_state(batch, ctx, attn_splits=splits)
+            st = model.new_batch_state(batch, ctx, attn_splits=splits, attention="exact")
             st.k_cache.normal_(); st.v_cache.normal_(); st.qkv.normal_()
             st.positions.fill_(ctx - 1)
 
@@ -914,11 +920,25 @@ def run_attention(args) -> int:
                                                 torch.cuda.current_stream().cuda_stream), "h4b_batch_attention")
         sec = _graph_time(torch, launch, reps=20)
         kv_bytes = batch * 2 * ctx * model.kv_size * 2
-        results.append({"batch": batch, "ctx": ctx, "splits": splits, "us": round(sec * 1e6, 2),
-                        "gbs": round(kv_bytes / sec / 1e9, 1), "frac": round(kv_bytes / sec / 1e9 / peaks["hbm_gbs"], 4),
-                        "kv_bytes": kv_bytes})
+        case_line = {"batch": batch, "ctx": ctx, "splits": splits, "us": round(sec * 1e6, 2),
+                     "gbs": round(kv_bytes / sec / 1e9, 1), "frac": round(kv_bytes / sec / 1e9 / peaks["hbm_gbs"], 4),
+                     "kv_bytes": kv_bytes}
         del st
         torch.cuda.empty_cache()
+        if batch > 1:  # the tcgen05 batched kernel on the same case (qk-norm / RoPE / append kernel + attention + merge)
+            st = model.new_batch_state(batch, ctx, attn_splits=64, attention="tensor")
+            st.k_cache.normal_(); st.v_cache.normal_(); st.qkv.normal_()
+            st.positions.fill_(ctx - 1)
+
+            def launch_tc(st=st):
+                check(lib().h4b_batch_attention(ctypes.byref(model.desc), ctypes.byref(st.desc), 0,
+                                                torch.cuda.current_stream().cuda_stream), "h4b_batch_attention")
+            sec_tc = _graph_time(torch, launch_tc, reps=20)
+            case_line["tensor"] = {"us": round(sec_tc * 1e6, 2), "gbs": round(kv_bytes / sec_tc / 1e9, 1),
+                                   "frac": round(kv_bytes / sec_tc / 1e9 / peaks["hbm_gbs"], 4)}
+            del st
+            torch.cuda.empty_cache()
+        results.append(case_line)
     line = {"metric": "GQA decode attention GB/s of K/V read (config 2)", "unit": "GB/s",
             "peak": peaks["hbm_gbs"], "peak_source": peaks["source"],
             "config": {"workload": "config2: 32 q / 8 kv heads, d 128, fp16 KV N(0,1), RoPE + qk-norm in kernel",

@@ -46,7 +46,7 @@ class BatchStateDesc(ctypes.Structure):
     _fields_ = [("batch", _i32), ("capacity", _i32), ("kv_dtype", _i32), ("attn_splits", _i32)] + [
         (n, _vp) for n in ("k_cache", "v_cache", "positions", "tokens", "next_tokens", "x", "x8", "act_scale",
                            "act_sum", "qkv", "attended", "proj", "gate_up", "act", "logits", "attn_partials",
-                           "attn_counters", "gemm_acc")]
+                           "attn_counters", "gemm_acc")] + [("attn_kernel", _i32)]
 
 
 class PrefillScratchDesc(ctypes.Structure):

@@ -231,6 +231,7 @@ int validate_batch(const h4b_model* m, const h4b_batch_state* s) {
     if (s->capacity < 1 || s->capacity > m->max_pos) return H4B_EINVAL;
     if (s->kv_dtype != 0 && s->kv_dtype != 1) return H4B_EINVAL;
     if (s->attn_splits < 1 || s->attn_splits > 64) return H4B_EINVAL;
+    if (s->attn_kernel != H4B_BATCH_ATTN_EXACT && s->attn_kernel != H4B_BATCH_ATTN_TENSOR) return H4B_EINVAL;
     const void* required[] = {m->w_qkv, m->s_qkv, m->w_o, m->s_o, m->w_gate_up, m->s_gate_up, m->w_down, m->s_down,
                               m->w_embed, m->s_embed, m->norm_in, m->norm_post, m->norm_q, m->norm_k, m->norm_final,
                               m->rope_cos, m->rope_sin, s->k_cache, s->v_cache, s->positions, s->tokens,
@@ -244,7 +245,13 @@ int validate_batch(const h4b_model* m, const h4b_batch_state* s) {
 
 // Layer l's attention for every sequence of the batch: qk-RMSNorm, RoPE,
 // append at each sequence's position, split-K GQA over its own cache.
+// decode_tc.cu
+int launch_batch_attention_tc(const h4b_model* m, const h4b_batch_state* s, int l, cudaStream_t stream);
+bool batch_tc_supported(int kv_dtype, int head_dim, int groups);
+
 int batch_attention(const h4b_model* m, const h4b_batch_state* s, int l, cudaStream_t stream) {
+    if (s->attn_kernel == H4B_BATCH_ATTN_TENSOR && batch_tc_supported(s->kv_dtype, m->head_dim, m->heads / m->kv_heads))
+        return launch_batch_attention_tc(m, s, l, stream);
     const int d = m->head_dim, q_size = m->heads * d, kv_size = m->kv_heads * d, qkv_rows = q_size + 2 * kv_size;
     const size_t kv_layer = static_cast<size_t>(m->kv_heads) * s->capacity * d;  // elements
     AttnArgs a = {};

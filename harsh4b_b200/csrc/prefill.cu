@@ -42,19 +42,25 @@ __global__ void prefill_setup_kernel(const int32_t* position, int count, int cap
 
 // One warp per (prompt token, head), eight to a CTA: heads [0, q_heads)
 // are queries, [q_heads, q_heads + kv_heads) keys (+ the matching value row).
+// Batched decode uses it with one row per sequence and row_stride = the
+// distance between the sequences' caches.
 constexpr int kRopeWarps = 8;
 
 template <typename KV>
 __global__ void __launch_bounds__(32 * kRopeWarps) prefill_rope_append_kernel(
     float* qkv, int qkv_stride, int q_heads, int kv_heads, const float* q_norm, const float* k_norm,
     const float* rope_cos, const float* rope_sin, float eps, const int32_t* positions, int count, KV* kcache,
-    KV* vcache, long long head_stride, long long time_stride) {
+    KV* vcache, long long head_stride, long long time_stride, int capacity, long long row_stride = 0) {
     const int heads = q_heads + kv_heads;
     const long long w = static_cast<long long>(blockIdx.x) * kRopeWarps + (threadIdx.x >> 5);
     if (w >= static_cast<long long>(count) * heads) return;
     const int i = static_cast<int>(w / heads), head = static_cast<int>(w % heads), lane = threadIdx.x & 31;
     const int pos = positions[i];
     if (pos < 0) return;
+    if (pos >= capacity) {  // a batch row past its cache (the prefill marks such rows -1)
+        if (lane == 0 && head == 0) report(kStatusBadPosition);
+        return;
+    }
     const float* cs = rope_cos + static_cast<long long>(pos) * (kHeadDim / 2);
     const float* sn = rope_sin + static_cast<long long>(pos) * (kHeadDim / 2);
     float* row = qkv + static_cast<long long>(i) * qkv_stride;
@@ -67,7 +73,8 @@ __global__ void __launch_bounds__(32 * kRopeWarps) prefill_rope_append_kernel(
     const float* k = row + static_cast<long long>(q_heads + kvh) * kHeadDim;
     const float* v = row + static_cast<long long>(q_heads + kv_heads + kvh) * kHeadDim;
     const float4 kn = norm_rope(*(reinterpret_cast<const float4*>(k) + lane), k_norm, cs, sn, eps, lane);
-    const long long at = kvh * head_stride + static_cast<long long>(pos) * time_stride + 4 * lane;
+    // row_stride: each row its own cache (batched decode), 0: one cache (prefill)
+    const long long at = i * row_stride + kvh * head_stride + static_cast<long long>(pos) * time_stride + 4 * lane;
     store4<KV>(kcache + at, kn);
     store4<KV>(vcache + at, *(reinterpret_cast<const float4*>(v) + lane));
 }
@@ -257,12 +264,12 @@ struct PrefillRun {
             prefill_rope_append_kernel<float><<<rope_grid, 32 * kRopeWarps, 0, stream>>>(
                 p->qkv, qkv_rows, m->heads, m->kv_heads, m->norm_q + static_cast<size_t>(l) * d,
                 m->norm_k + static_cast<size_t>(l) * d, m->rope_cos, m->rope_sin, m->eps, p->positions, count,
-                reinterpret_cast<float*>(kc), reinterpret_cast<float*>(vc), head_stride, d);
+                reinterpret_cast<float*>(kc), reinterpret_cast<float*>(vc), head_stride, d, s->capacity);
         else
             prefill_rope_append_kernel<__half><<<rope_grid, 32 * kRopeWarps, 0, stream>>>(
                 p->qkv, qkv_rows, m->heads, m->kv_heads, m->norm_q + static_cast<size_t>(l) * d,
                 m->norm_k + static_cast<size_t>(l) * d, m->rope_cos, m->rope_sin, m->eps, p->positions, count,
-                reinterpret_cast<__half*>(kc), reinterpret_cast<__half*>(vc), head_stride, d);
+                reinterpret_cast<__half*>(kc), reinterpret_cast<__half*>(vc), head_stride, d, s->capacity);
         H4B_CUDA_TRY(cudaGetLastError());
         return attention_only(l);
     }

@@ -25,6 +25,8 @@ KV_DTYPES = {"float32": (0, torch.float32), "float16": (1, torch.float16)}
 MODES = ("persistent", "chain")
 # prefill attention kernels (h4b_prefill_scratch.attn_kernel)
 PREFILL_ATTENTION = {"exact": 0, "tensor": 1}
+# batched-decode attention kernels (h4b_batch_state.attn_kernel)
+BATCH_ATTENTION = {"exact": 0, "tensor": 1}
 PERSISTENT_ATTN_CHUNK = 32  # tokens per attention split in the persistent step (persistent.cu)
 SWIGLU_BLOCK = 4  # rows per gate/up interleave block (matches the kernel)
 
@@ -181,11 +183,21 @@ class CudaDecodeState:
 class CudaBatchState:
     """B independent decode sessions advanced together (one token each per
     step). KV cache [B][L][kv_heads][capacity][head_dim]; every sequence keeps
-    its own position. Scratch sized for the batch; nothing allocates per step."""
+    its own position. Scratch sized for the batch; nothing allocates per step.
 
-    def __init__(self, model: "CudaQwen", batch: int, capacity: int, attn_splits: int = 16):
+    attention="exact": the fp32 split kernel with `attn_splits` splits, each
+    row bit-identical to a decode step. attention="tensor" (the default; fp16
+    cache, head_dim 128, 4 q heads per kv head, otherwise as "exact"): tcgen05
+    attention with split fp16 operands over whole 128-key tiles (about two
+    CTAs per SM, at most `attn_splits` splits), within the 1e-3 relative
+    tolerance of the fp32 path."""
+
+    def __init__(self, model: "CudaQwen", batch: int, capacity: int, attn_splits: int = 16,
+                 attention: str = "tensor"):
         if batch < 1 or capacity < 1:
             raise ValueError("batch and capacity must be positive")
+        if attention not in BATCH_ATTENTION:
+            raise ValueError(f"attention must be one of {sorted(BATCH_ATTENTION)}")
         if capacity > model.max_pos:
             raise ValueError(f"capacity {capacity} exceeds the model's {model.max_pos} positions")
         self.model, self.batch, self.capacity, self.splits = model, batch, capacity, int(attn_splits)
@@ -218,6 +230,7 @@ class CudaBatchState:
             self.k_cache, self.v_cache, self.positions, self.tokens, self.next_tokens, self.x, self.x8,
             self.act_scale, self.act_sum, self.qkv, self.attended, self.proj, self.gate_up, self.act, self.logits,
             self.partials, self.counters, self.gemm_acc)])
+        self.desc.attn_kernel = BATCH_ATTENTION[attention]
         check(lib().h4b_validate_batch(ctypes.byref(model.desc), ctypes.byref(self.desc)), "h4b_validate_batch")
         self.position = np.zeros(batch, dtype=np.int64)  # host copy of every sequence's position
 
@@ -430,8 +443,9 @@ class CudaQwen:
         current.wait_stream(state.stream)
         return state.logits
 
-    def new_batch_state(self, batch: int, capacity: int, attn_splits: int = 16) -> CudaBatchState:
-        return CudaBatchState(self, batch, capacity, attn_splits)
+    def new_batch_state(self, batch: int, capacity: int, attn_splits: int = 16,
+                        attention: str = "tensor") -> CudaBatchState:
+        return CudaBatchState(self, batch, capacity, attn_splits, attention)
 
     def forward_batch(self, token_ids, state: CudaBatchState) -> torch.Tensor:
         """One token for each of the state's B sequences; returns the [B, V]

@@ -56,14 +56,15 @@ class ContinuousBatcher:
 
     def __init__(self, model, slots: int = 8, capacity: int = 2048, attn_splits: int = 16, sampler=None,
                  stop_ids=(), seed: int | None = None, top_p: float = 0.9, top_k: int = 50,
-                 repetition_penalty: float = 1.15):
+                 repetition_penalty: float = 1.15, attention: str = "tensor"):
         import torch
 
         from .model import CudaDecodeState
 
         self.torch, self.model = torch, model
         self.slots, self.capacity = int(slots), int(capacity)
-        self.batch = model.new_batch_state(self.slots, self.capacity, attn_splits)
+        self.attention = attention  # the prompt and the batched-decode attention kernels
+        self.batch = model.new_batch_state(self.slots, self.capacity, attn_splits, attention)
         self.slot_states = [CudaDecodeState(model, self.capacity, kv=(self.batch.k_cache[b], self.batch.v_cache[b]))
                             for b in range(self.slots)]
         self.sampler = sampler or CudaBackend(model=model, seed=seed, top_p=top_p, top_k=top_k,
@@ -160,7 +161,7 @@ class ContinuousBatcher:
             state = self.slot_states[b]
             state.reset()
             t0 = time.perf_counter()
-            logits = self.model.prefill(request.prompt_ids, state)
+            logits = self.model.prefill(request.prompt_ids, state, attention=self.attention)
             token = self.sampler(logits, request.generated, request.temperature)
             request.prefill_s = time.perf_counter() - t0
             request.t_decode0 = time.perf_counter()

@@ -279,7 +279,17 @@ typedef struct h4b_batch_state {
     int *attn_counters;
     int32_t *gemm_acc;  /* optional: [batch][(heads + 2 kv_heads) * head_dim] int32 zeros for split-K GEMMs
                            (the o, down and qkv projections at small batch); left zero after every step */
+    /* H4B_BATCH_ATTN_EXACT (0): the fp32 split kernel, each row bit-identical
+     * to a decode step. H4B_BATCH_ATTN_TENSOR (1): tcgen05 attention with
+     * split-fp16 operands (fp32 outputs within the 1e-3 relative tolerance)
+     * over splits of whole 128-key tiles (about two CTAs per SM, at most
+     * attn_splits), where the cache is fp16, head_dim 128 and 4 q heads share
+     * a kv head; else as 0. */
+    int attn_kernel;
 } h4b_batch_state;
+
+#define H4B_BATCH_ATTN_EXACT 0
+#define H4B_BATCH_ATTN_TENSOR 1
 
 int h4b_validate_batch(const h4b_model *model, const h4b_batch_state *state);
 

@@ -14,7 +14,7 @@ from harsh4b_b200.synthetic import qwen3_4b_config, synthetic_checkpoint, synthe
 
 def _batch_decode(model, prompts, steps, splits):
     B, n = len(prompts), len(prompts[0])
-    state = model.new_batch_state(B, n + steps, attn_splits=splits)
+    state = model.new_batch_state(B, n + steps, attn_splits=splits, attention="exact")
     rows = []
     for i in range(n):
         rows.append(model.forward_batch([p[i] for p in prompts], state).cpu().numpy().copy())
@@ -64,7 +64,7 @@ def test_qwen_shaped_batch_matches_oracle_and_device_loop():
         np.testing.assert_array_equal(logits[b], want)
         assert list(greedy[b]) == want_greedy
     # device-side greedy loop from the same point: 2 more tokens
-    fresh = model.new_batch_state(4, 16, attn_splits=16)
+    fresh = model.new_batch_state(4, 16, attn_splits=16, attention="exact")
     for i in range(6):
         model.forward_batch([p[i] for p in prompts], fresh)
     model.generate_batch(fresh, 3)

@@ -57,7 +57,7 @@ def test_continuous_batching_matches_single_sessions():
     # a stop id that the greedy decode of job 2 emits part-way
     probe = _oracle_greedy(checkpoint, *jobs[2], stop_ids=set())
     stop_ids = {probe[6]}
-    engine = ContinuousBatcher(model, slots=3, capacity=64, stop_ids=stop_ids).start()
+    engine = ContinuousBatcher(model, slots=3, capacity=64, stop_ids=stop_ids, attention="exact").start()
     try:
         requests = [engine.submit(prompt, limit, 0.0) for prompt, limit in jobs]
         results = [_drain(r) for r in requests]
