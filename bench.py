@@ -862,9 +862,26 @@ def run_gemm(args) -> int:
                 ops_ = 2 * M * N * K
                 row[kern] = {"us": round(sec * 1e6, 2), "tops": round(ops_ / sec / 1e12, 1),
                              "gbs": round((N * K // 2 + 4 * N + M * K + 4 * M * N) / sec / 1e9, 1)}
+            if M <= 64:
+                # the batched decode's form: K split over one CTA per SM (stream-K)
+                # through a zeroed int32 buffer, finalised into out
+                acc = torch.zeros(M * N, dtype=torch.int32, device="cuda")
+                outs["split"] = torch.empty(M, N, device="cuda")
+                state = {"i": 0}
+
+                def launch_acc(state=state):
+                    ops.int4_gemm_acc(x8, act, sums, ws[state["i"] % copies], scales, acc, out=outs["split"])
+                    state["i"] += 1
+
+                sec = _graph_time(torch, launch_acc, reps=max(copies, 8))
+                row["tcgen05_acc"] = {"us": round(sec * 1e6, 2), "tops": round(2 * M * N * K / sec / 1e12, 1),
+                                      "gbs": round((N * K // 2 + 4 * N + M * K + 4 * M * N) / sec / 1e9, 1)}
+                row["equal_acc"] = bool(torch.equal(outs["split"], outs["tcgen05"]))
             row["equal"] = bool(torch.equal(outs["tcgen05"], outs["mma_sync"]))
             tc = row["tcgen05"]
             row["frac"] = (round(tc["gbs"] / peaks["hbm_gbs"], 4) if M <= 64 else round(tc["tops"] / int8_peak, 4))
+            if M <= 64:
+                row["frac_acc"] = round(row["tcgen05_acc"]["gbs"] / peaks["hbm_gbs"], 4)
             results.append(row)
             del ws
     line = {"metric": "batched int4 x int8 GEMM (a13): tcgen05 vs mma.sync", "unit": "us",

@@ -46,7 +46,7 @@ class BatchStateDesc(ctypes.Structure):
     _fields_ = [("batch", _i32), ("capacity", _i32), ("kv_dtype", _i32), ("attn_splits", _i32)] + [
         (n, _vp) for n in ("k_cache", "v_cache", "positions", "tokens", "next_tokens", "x", "x8", "act_scale",
                            "act_sum", "qkv", "attended", "proj", "gate_up", "act", "logits", "attn_partials",
-                           "attn_counters", "gemm_acc")] + [("attn_kernel", _i32)]
+                           "attn_counters", "gemm_acc")] + [("attn_kernel", _i32), ("gemm_acc_width", _i32)]
 
 
 class PrefillScratchDesc(ctypes.Structure):
@@ -102,6 +102,7 @@ _SIGNATURES = {
     "h4b_quantize_rows": [_vp, _vp, _vp, _vp, _i32, _i32, _vp],
     "h4b_int4_gemm": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp],
     "h4b_int4_gemm_ex": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
+    "h4b_int4_gemm_acc": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
     "h4b_validate_batch": [ctypes.POINTER(ModelDesc), ctypes.POINTER(BatchStateDesc)],
     "h4b_int4_gemv_absmax": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp],
     "h4b_residual_acc": [_vp, _vp, _vp, _vp, _i32, _vp],

@@ -232,6 +232,7 @@ int validate_batch(const h4b_model* m, const h4b_batch_state* s) {
     if (s->kv_dtype != 0 && s->kv_dtype != 1) return H4B_EINVAL;
     if (s->attn_splits < 1 || s->attn_splits > 64) return H4B_EINVAL;
     if (s->attn_kernel != H4B_BATCH_ATTN_EXACT && s->attn_kernel != H4B_BATCH_ATTN_TENSOR) return H4B_EINVAL;
+    if (s->gemm_acc_width < 0) return H4B_EINVAL;
     const void* required[] = {m->w_qkv, m->s_qkv, m->w_o, m->s_o, m->w_gate_up, m->s_gate_up, m->w_down, m->s_down,
                               m->w_embed, m->s_embed, m->norm_in, m->norm_post, m->norm_q, m->norm_k, m->norm_final,
                               m->rope_cos, m->rope_sin, s->k_cache, s->v_cache, s->positions, s->tokens,
@@ -278,8 +279,10 @@ int decode_batch(const h4b_model* m, const h4b_batch_state* s, cudaStream_t stre
     if (rc) return rc;
     const int B = s->batch, H = m->hidden, I = m->intermediate, d = m->head_dim;
     const int q_size = m->heads * d, kv_size = m->kv_heads * d, qkv_rows = q_size + 2 * kv_size;
-    // split-K room: gemm_acc holds B rows of max(qkv rows, hidden) int32
-    const int acc_rows = std::max(m->heads * m->head_dim + 2 * m->kv_heads * m->head_dim, m->hidden);
+    // split-K / stream-K room: gemm_acc holds B rows of gemm_acc_width int32
+    const int acc_rows = s->gemm_acc_width > 0
+                             ? s->gemm_acc_width
+                             : std::max(m->heads * m->head_dim + 2 * m->kv_heads * m->head_dim, m->hidden);
     auto gemm = [&](const uint8_t* w, const float* ws, float* out, int rows, int width, bool residual = false) {
         GemmArgs g{s->x8, s->act_scale, s->act_sum, w, ws, out, B, rows, width};
         g.split_acc = rows <= acc_rows ? s->gemm_acc : nullptr;

@@ -15,15 +15,16 @@
 //   warps 0 .. 4 G - 1: unpack groups of four warps, group g taking stages
 //           g, g + G, ...: thread = weight row (its warp's TMEM lane quarter),
 //           it reads the row's 64 packed bytes, expands them to 128 signed
-//           int8 codes and stores them with tcgen05.st into the group's
-//           unpacked tile in tensor memory (32 columns, four codes per
-//           column) -- the MMA's A operand -- then arrives on `aready`. After
+//           int8 codes and stores them with tcgen05.st into one of the
+//           group's unpacked tiles in tensor memory (32 columns, four codes
+//           per column; two tiles per group used in turn below TOK 256) --
+//           the MMA's A operand -- then arrives on the tile's `aready`. After
 //           the last stage the first sixteen warps are the epilogue, warp w
 //           reading TMEM lane quarter w % 4 (32 rows) for column slice w / 4;
 //   warp 4 G + 1 lane 0: issues tcgen05.mma kind::i8 (A s8 weights from
 //           tensor memory, B s8 activations from shared memory, D s32 in
 //           TMEM), 4 per stage (K = 32 each), and tcgen05.commit to the
-//           stage's `empty` and the group's `afree`; a final commit signals
+//           stage's `empty` and the tile's `afree`; a final commit signals
 //           the epilogue.
 // Every wait is bounded (mbar_wait). A role whose wait runs out reports
 // kStatusWaitTimeout, marks the CTA as failed and stops issuing; the
@@ -45,6 +46,12 @@ struct TcCfg {
     // unpacked weight tile in tensor memory. The stage count is a multiple of
     // the groups, so a group always revisits its own stages round by round.
     static constexpr int kGroups = TOK == 256 ? 5 : 4;
+    // Unpacked weight tiles in tensor memory: two per group below TOK 256, so
+    // a group expands its next stage while the MMAs still read its previous
+    // one (each tile is free again only when the MMA thread's commit lands);
+    // one per group at TOK 256, whose accumulator takes 256 columns.
+    static constexpr int kSlotsPerGroup = TOK == 256 ? 1 : 2;
+    static constexpr int kASlots = kGroups * kSlotsPerGroup;
     static constexpr int kStages = TOK == 256 ? 5 : (TOK == 128 ? 8 : 12);
     static constexpr int kUnpackWarps = kGroups * kTcGroupWarps;
     static constexpr int kProducerWarp = kUnpackWarps, kMmaWarp = kUnpackWarps + 1;
@@ -56,15 +63,17 @@ struct TcCfg {
     static constexpr int kBarrierOff = kStages * kStageBytes;
     static constexpr int kBarrierBytes = 512;
     static constexpr int kSmem = kBarrierOff + kBarrierBytes + 1024;  // + alignment slack
-    // tensor memory: the accumulator (TOK columns), then one unpacked weight
-    // tile per group (128 rows x 128 int8 = 32 columns)
-    static constexpr uint32_t kACol = TOK;
-    static constexpr uint32_t kTmemCols = TOK + 32 * kGroups <= 256 ? 256 : 512;
+    // tensor memory: the accumulator (TOK columns; at TOK 64 two of them, one
+    // per row tile of a stream-K range), then the unpacked weight tiles
+    // (128 rows x 128 int8 = 32 columns each)
+    static constexpr int kAccs = TOK == 64 ? 2 : 1;
+    static constexpr uint32_t kACol = kAccs * TOK;
+    static constexpr uint32_t kTmemCols = kACol + 32 * kASlots <= 256 ? 256 : 512;
     static_assert(kStageBytes % 1024 == 0, "tiles keep the 1024-byte swizzle alignment");
     static_assert(kStages % kGroups == 0, "each group must own whole stages");
     static_assert(kSmem <= 232448, "shared memory per CTA");
-    static_assert(TOK + 32 * kGroups <= kTmemCols, "tensor memory");
-    static_assert(2 * kStages * 8 + 2 * kGroups * 8 + 16 <= kBarrierBytes, "barrier area");
+    static_assert(kACol + 32 * kASlots <= kTmemCols, "tensor memory");
+    static_assert(2 * kStages * 8 + 2 * kASlots * 8 + 16 <= kBarrierBytes, "barrier area");
 };
 
 struct TcArgs {
@@ -75,6 +84,11 @@ struct TcArgs {
     int32_t* out_i32;        // when set: the exact int32 sums [M][N] instead of `out`
     int32_t* split_acc;      // split-K (gridDim.z > 1): K slices add their int32 sums here
     int residual;            // out[m][n] = out[m][n] + value instead of value
+    // stream-K (M <= TOK = 64, split_acc set): CTA c of gridDim.x takes units
+    // [c U / G, (c + 1) U / G) of the U = (N / 128) x (K / 128) (row tile,
+    // k-step) units in row-tile order -- at most two row tiles, whose sums it
+    // adds to split_acc
+    int stream;
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -162,27 +176,42 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
     uint8_t* smem = tc_smem_raw + ((1024u - (smem_addr(tc_smem_raw) & 1023u)) & 1023u);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarrierOff);  // TMA stage landed
     uint64_t* empty = full + C::kStages;                                   // TMA stage consumed by the MMAs
-    uint64_t* aready = empty + C::kStages;                                 // unpacked tile g written
-    uint64_t* afree = aready + C::kGroups;                                 // unpacked tile g read by the MMAs
-    uint64_t* accfull = afree + C::kGroups;
+    uint64_t* aready = empty + C::kStages;                                 // unpacked tile a written
+    uint64_t* afree = aready + C::kASlots;                                 // unpacked tile a read by the MMAs
+    uint64_t* accfull = afree + C::kASlots;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accfull + 1);
     volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // token tiles fastest: the CTAs running at once share weight tiles and
     // spread their reads of the larger activation tiles over several of them
-    const int n0 = blockIdx.y * kTcRows, m0 = blockIdx.x * TOK;
-    // this CTA's K slice (split-K over gridDim.z): steps [kbeg, kbeg + steps)
+    int n0 = blockIdx.y * kTcRows, m0 = blockIdx.x * TOK;
+    // this CTA's iterations: [0, len0) are k-steps kbeg, kbeg + 1, ... of row
+    // tile n0 (split-K over gridDim.z: one K slice), [len0, steps) k-steps
+    // 0, 1, ... of the next row tile (stream-K only)
     const int all_steps = g.K / kTcK;
-    const int kbeg = static_cast<int>(static_cast<long long>(blockIdx.z) * all_steps / gridDim.z);
-    const int steps = static_cast<int>(static_cast<long long>(blockIdx.z + 1) * all_steps / gridDim.z) - kbeg;
+    int kbeg, steps;
+    if (TOK == 64 && g.stream) {
+        const long long units = static_cast<long long>(g.N / kTcRows) * all_steps;
+        const long long u0 = blockIdx.x * units / gridDim.x, u1 = (blockIdx.x + 1) * units / gridDim.x;
+        const int tile = static_cast<int>(u0 / all_steps);
+        kbeg = static_cast<int>(u0 - static_cast<long long>(tile) * all_steps);
+        steps = static_cast<int>(u1 - u0);
+        n0 = tile * kTcRows;
+        m0 = 0;
+    } else {
+        kbeg = static_cast<int>(static_cast<long long>(blockIdx.z) * all_steps / gridDim.z);
+        steps = static_cast<int>(static_cast<long long>(blockIdx.z + 1) * all_steps / gridDim.z) - kbeg;
+    }
+    const int len0 = min(steps, all_steps - kbeg);
+    const int n1 = n0 + kTcRows;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int a = 0; a < C::kGroups; ++a) {
+        for (int a = 0; a < C::kASlots; ++a) {
             mbar_init(&aready[a], kTcGroupWarps);
             mbar_init(&afree[a], 1);
         }
@@ -205,7 +234,8 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
     // cannot tell a phase from the one two rounds later): the producer and
     // the MMA thread walk all iterations in order; unpack group g handles
     // iterations g, g + kGroups, ..., whose TMA stages (it % kStages, a
-    // multiple of kGroups apart) and unpacked tile (g) are its own.
+    // multiple of kGroups apart) and unpacked tiles (g, g + kGroups, used
+    // in turn) are its own.
     if (warp == C::kProducerWarp) {
         if (lane == 0) {  // TMA producer
             int issued = 0;
@@ -220,9 +250,11 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
                         *failed = 1;
                         break;
                     }
+                    const bool next = it >= len0;
+                    const int kstep = next ? it - len0 : kbeg + it;
                     mbar_arrive_expect_tx(&full[s], C::kPackedBytes + C::kBBytes);
-                    tma_load_2d(stage(s) + C::kPackedOff, &wmap, (kbeg + it) * (kTcK / 2), n0, &full[s]);
-                    tma_load_2d(stage(s) + C::kBOff, &xmap, (kbeg + it) * kTcK, m0, &full[s]);
+                    tma_load_2d(stage(s) + C::kPackedOff, &wmap, kstep * (kTcK / 2), next ? n1 : n0, &full[s]);
+                    tma_load_2d(stage(s) + C::kBOff, &xmap, kstep * kTcK, m0, &full[s]);
                     issued = it + 1;
                 }
             }
@@ -234,18 +266,23 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
         if (lane == 0) {  // MMA issuer
             constexpr uint32_t idesc = tc_idesc<TOK>();
             for (int it = 0; it < steps && !*failed; ++it) {
-                const int s = it % C::kStages, a = it % C::kGroups;
+                const int s = it % C::kStages, use = it / C::kGroups;
+                const int a = it % C::kGroups + C::kGroups * (use % C::kSlotsPerGroup);
                 if (!mbar_wait(&full[s], (it / C::kStages) & 1) ||
-                    !mbar_wait(&aready[a], (it / C::kGroups) & 1)) {
+                    !mbar_wait(&aready[a], (use / C::kSlotsPerGroup) & 1)) {
                     *failed = 1;
                     break;
                 }
                 tc_fence_after();
                 const uint64_t bdesc = sw128_desc(stage(s) + C::kBOff);
                 const uint32_t atmem = tmem + C::kACol + 32 * a;
+                // the second row tile of a stream-K range: the second accumulator
+                const bool next = it >= len0;
+                const uint32_t dtmem = tmem + (next ? TOK : 0);
+                const int first = next ? len0 : 0;
 #pragma unroll
                 for (int kk = 0; kk < kTcK / 32; ++kk)  // K = 32: 8 columns of A, +32 bytes (+2) along B
-                    tc_mma_i8_ts(tmem, atmem + 8 * kk, bdesc + 2 * kk, idesc, (it | kk) != 0);
+                    tc_mma_i8_ts(dtmem, atmem + 8 * kk, bdesc + 2 * kk, idesc, (it != first) || kk != 0);
                 tc_commit(&empty[s]);
                 tc_commit(&afree[a]);
             }
@@ -259,8 +296,10 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         for (int it = group; it < steps; it += C::kGroups) {
             const int s = it % C::kStages;
-            const int use = it / C::kGroups;  // this group's tile use count
-            const bool ok = __all_sync(0xffffffffu, !*failed && (use == 0 || mbar_wait(&afree[group], (use - 1) & 1)) &&
+            const int use = it / C::kGroups;  // this group's stage count
+            const int a = group + C::kGroups * (use % C::kSlotsPerGroup);
+            const int k = use / C::kSlotsPerGroup;  // tile a's use count
+            const bool ok = __all_sync(0xffffffffu, !*failed && (k == 0 || mbar_wait(&afree[a], (k - 1) & 1)) &&
                                                         mbar_wait(&full[s], (it / C::kStages) & 1));
             if (!ok) {
                 if (lane == 0) *failed = 1;
@@ -283,7 +322,7 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
                 codes[8 * c + 6] = nib_s8(w.w, 0x1100);
                 codes[8 * c + 7] = nib_s8(w.w, 0x3322);
             }
-            const uint32_t acol = lane_base + C::kACol + 32 * group;
+            const uint32_t acol = lane_base + C::kACol + 32 * a;
 #pragma unroll
             for (int h = 0; h < 2; ++h)
                 asm volatile(
@@ -298,16 +337,32 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();  // tensor-memory stores -> ordered before the MMAs that read them
             __syncwarp();
-            if (lane == 0) mbar_arrive(&aready[group]);
+            if (lane == 0) mbar_arrive(&aready[a]);
         }
         // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = weight rows n0 + 32 (w % 4) + lane,
         // columns (tokens) of slice w / 4
         const bool done = __all_sync(0xffffffffu, mbar_wait(accfull, 0) && !*failed);
         tc_fence_after();
-        if (done && warp < 16) {  // the first sixteen warps: four column slices per lane quarter
+        if (done && warp < 16 && steps > 0) {  // the first sixteen warps: four column slices per lane quarter
             constexpr int kSlices = 4, kCols = TOK / kSlices;
             static_assert(kCols % 16 == 0, "column slices of whole 16-column loads");
             const int quarter = warp & 3, slice = warp >> 2;
+            if (TOK == 64 && g.stream) {
+                // stream-K: each row tile's sums (1 or 2 accumulators) into split_acc
+                for (int t = 0; t < (steps > len0 ? 2 : 1); ++t) {
+                    const int row = (t ? n1 : n0) + quarter * 32 + lane;
+                    const uint32_t base = tmem + t * TOK + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+                    for (int c0 = slice * kCols; c0 < (slice + 1) * kCols; c0 += 16) {
+                        uint32_t v[16];
+                        tmem_ld16(base + c0, v);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (c0 + j < g.M)
+                                atomicAdd(g.split_acc + static_cast<size_t>(c0 + j) * g.N + row, static_cast<int>(v[j]));
+                    }
+                }
+            } else {
             const int row = n0 + quarter * 32 + lane;
             const float ws = g.w_scale[row];
             const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -343,6 +398,7 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
                     const float value = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(v[j])), as), ws);
                     g.out[static_cast<size_t>(m) * g.N + row] = g.residual ? __fadd_rn(prev[j], value) : value;
                 }
+            }
             }
         }
     }
@@ -463,20 +519,32 @@ int launch_tc(const GemmArgs& g, cudaStream_t stream) {
     if (!byte_matrix_map(&wmap, g.w, static_cast<uint64_t>(g.K) / 2, g.N, kTcK / 2, kTcRows, 64) ||
         !byte_matrix_map(&xmap, g.x, g.K, g.M, kTcK, TOK, 128))
         return H4B_EUNSUPPORTED;
-    // Few output tiles (o / down / qkv at M <= 64 give 20-48 of them): split K
-    // so the grid fills the SMs, each slice at least 4 k-steps, the int32
-    // sums added in the caller's zeroed buffer and finalised below.
+    // With the caller's zeroed int32 buffer (split_acc) the int32 sums are
+    // added there (exact in any order) and finalised below:
+    // * M <= 64: stream-K, one CTA per SM over the (row tile, k-step) units,
+    //   when that gives every CTA at most K / 128 + 1 units (two row tiles):
+    //   all SMs busy for the same number of k-steps whatever the tile count
+    //   (gate_up's 152 row tiles are two waves of one CTA per SM otherwise);
+    // * else few output tiles (under half the SMs): split K so the grid fills
+    //   the SMs, each slice at least 4 k-steps.
     const int tiles = (g.N / kTcRows) * ((g.M + TOK - 1) / TOK);
     const int steps = g.K / kTcK;
-    int ksplit = 1;
-    if (g.split_acc && !g.out_i32 && tiles < sm_count() / 2)
-        ksplit = std::max(1, std::min(sm_count() / tiles, steps / 4));
-    const TcArgs a{g.act_scale, g.w_scale, g.out, g.M, g.N, g.K, g.out_i32, ksplit > 1 ? g.split_acc : nullptr,
-                   g.residual ? 1 : 0};
-    const dim3 grid((g.M + TOK - 1) / TOK, g.N / kTcRows, ksplit);
+    int ksplit = 1, stream_ctas = 0;
+    if (g.split_acc && !g.out_i32) {
+        const long long units = static_cast<long long>(tiles) * steps;
+        const long long ctas = std::min<long long>(sm_count(), units);
+        if (TOK == 64 && g.M <= TOK && (units + ctas - 1) / ctas <= steps + 1)
+            stream_ctas = static_cast<int>(ctas);
+        else if (tiles < sm_count() / 2)
+            ksplit = std::max(1, std::min(sm_count() / tiles, steps / 4));
+    }
+    const bool accumulate = stream_ctas > 0 || ksplit > 1;
+    const TcArgs a{g.act_scale, g.w_scale, g.out, g.M, g.N, g.K, g.out_i32, accumulate ? g.split_acc : nullptr,
+                   g.residual ? 1 : 0, stream_ctas > 0 ? 1 : 0};
+    const dim3 grid = stream_ctas > 0 ? dim3(stream_ctas, 1, 1) : dim3((g.M + TOK - 1) / TOK, g.N / kTcRows, ksplit);
     int4_gemm_tc_kernel<TOK><<<grid, C::kThreads, C::kSmem, stream>>>(wmap, xmap, a);
     H4B_CUDA_TRY(cudaGetLastError());
-    if (ksplit > 1) {
+    if (accumulate) {
         const long long n = static_cast<long long>(g.M) * g.N;
         split_finalize_kernel<<<static_cast<int>(std::min<long long>((n + 255) / 256, 8ll * sm_count())), 256, 0,
                                 stream>>>(g.split_acc, g.act_scale, g.w_scale, g.out, g.M, g.N,
@@ -520,4 +588,15 @@ extern "C" int h4b_int4_gemm_ex(const int8_t* x8, const float* act_scales, const
 extern "C" int h4b_int4_gemm(const int8_t* x8, const float* act_scales, const int32_t* act_sums, const uint8_t* weights,
                              const float* scales, float* output, int tokens, int rows, int width, void* stream) {
     return h4b_int4_gemm_ex(x8, act_scales, act_sums, weights, scales, output, tokens, rows, width, 0, stream);
+}
+
+extern "C" int h4b_int4_gemm_acc(const int8_t* x8, const float* act_scales, const int32_t* act_sums,
+                                 const uint8_t* weights, const float* scales, float* output, int32_t* acc, int tokens,
+                                 int rows, int width, int residual, void* stream) {
+    if (!x8 || !act_scales || !act_sums || !weights || !scales || !output || !acc) return H4B_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(acc) & 3) != 0) return H4B_EINVAL;
+    h4b::GemmArgs g{x8, act_scales, act_sums, weights, scales, output, tokens, rows, width};
+    g.split_acc = acc;
+    g.residual = residual != 0;
+    return h4b::launch_int4_gemm(g, static_cast<cudaStream_t>(stream), 0);
 }

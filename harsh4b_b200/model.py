@@ -224,13 +224,16 @@ class CudaBatchState:
         self.logits = torch.zeros(batch, model.vocab, **f32)
         self.partials = torch.zeros(batch * model.kv_heads * self.splits * model.groups * (model.head_dim + 4), **f32)
         self.counters = torch.zeros(batch * model.kv_heads, **i32)
-        # split-K sums of the few-tile GEMMs (o, down, qkv), zero between GEMMs
-        self.gemm_acc = torch.zeros(batch * max(Q + 2 * KV, H), **i32)
+        # int32 sums of the split-K / stream-K GEMMs (every body projection),
+        # zero between GEMMs
+        acc_width = max(Q + 2 * KV, H, 2 * I)
+        self.gemm_acc = torch.zeros(batch * acc_width, **i32)
         self.desc = BatchStateDesc(batch, capacity, code, self.splits, *[t.data_ptr() for t in (
             self.k_cache, self.v_cache, self.positions, self.tokens, self.next_tokens, self.x, self.x8,
             self.act_scale, self.act_sum, self.qkv, self.attended, self.proj, self.gate_up, self.act, self.logits,
             self.partials, self.counters, self.gemm_acc)])
         self.desc.attn_kernel = BATCH_ATTENTION[attention]
+        self.desc.gemm_acc_width = acc_width
         check(lib().h4b_validate_batch(ctypes.byref(model.desc), ctypes.byref(self.desc)), "h4b_validate_batch")
         self.position = np.zeros(batch, dtype=np.int64)  # host copy of every sequence's position
 

@@ -180,6 +180,26 @@ def int4_gemm(x8: torch.Tensor, act_scales: torch.Tensor, act_sums: torch.Tensor
     return out
 
 
+def int4_gemm_acc(x8: torch.Tensor, act_scales: torch.Tensor, act_sums: torch.Tensor, weights: torch.Tensor,
+                  scales: torch.Tensor, acc: torch.Tensor, out: torch.Tensor | None = None,
+                  residual: bool = False) -> torch.Tensor:
+    """h4b_int4_gemm_acc: int4_gemm with the K sum split over CTAs through the
+    zeroed int32 buffer `acc` [M, N] (left zero); `residual` adds into `out`."""
+    tokens, width = x8.shape
+    rows = weights.shape[0]
+    if residual and out is None:
+        raise ValueError("residual needs out")
+    if acc.numel() < tokens * rows:
+        raise ValueError(f"acc holds {acc.numel()} int32, needs {tokens * rows}")
+    out = torch.empty(tokens, rows, dtype=torch.float32, device=x8.device) if out is None else out
+    check(lib().h4b_int4_gemm_acc(_dev(x8, torch.int8, "x8"), _dev(act_scales, torch.float32, "act_scales"),
+                                  _dev(act_sums, torch.int32, "act_sums"), _dev(weights, torch.uint8, "weights"),
+                                  _dev(scales, torch.float32, "scales"), _dev(out, torch.float32, "out"),
+                                  _dev(acc, torch.int32, "acc"), tokens, rows, width, 1 if residual else 0,
+                                  stream_handle()), "h4b_int4_gemm_acc")
+    return out
+
+
 def int4_gemm_rows(values: torch.Tensor, weights: torch.Tensor, scales: torch.Tensor,
                    kernel: str = "auto") -> torch.Tensor:
     """fp32 [M, K] -> fp32 [M, N]: per-token quantisation, then the batched GEMM."""

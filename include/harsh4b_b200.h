@@ -168,6 +168,17 @@ int h4b_int4_gemm(const int8_t *x8, const float *act_scales, const int32_t *act_
 int h4b_int4_gemm_ex(const int8_t *x8, const float *act_scales, const int32_t *act_sums, const uint8_t *weights,
                      const float *scales, float *output, int tokens, int rows, int width, int kernel, void *stream);
 
+/* h4b_int4_gemm through a caller's int32 buffer acc [tokens][rows], zero on
+ * entry and left zero: the kernel may split the K sum over several CTAs
+ * (few tokens: one CTA per SM over the (128-row tile, 128-k step) units, or
+ * K slices when the row tiles are few), adding the exact int32 partial sums
+ * in acc, then applies the same epilogue -- the same bits as h4b_int4_gemm.
+ * residual != 0: output[m][n] = output[m][n] + value (x + proj) instead of
+ * value. The batched decode runs its projections this way. */
+int h4b_int4_gemm_acc(const int8_t *x8, const float *act_scales, const int32_t *act_sums, const uint8_t *weights,
+                      const float *scales, float *output, int32_t *acc, int tokens, int rows, int width, int residual,
+                      void *stream);
+
 /* ---- model level ----------------------------------------------------------- */
 
 /* Device-resident Qwen3 model. Every weight kind is one buffer covering all
@@ -277,8 +288,9 @@ typedef struct h4b_batch_state {
     float *qkv, *attended, *proj, *gate_up, *act, *logits;
     float *attn_partials;
     int *attn_counters;
-    int32_t *gemm_acc;  /* optional: [batch][(heads + 2 kv_heads) * head_dim] int32 zeros for split-K GEMMs
-                           (the o, down and qkv projections at small batch); left zero after every step */
+    int32_t *gemm_acc;  /* optional: [batch][gemm_acc_width] int32 zeros for split-K / stream-K GEMMs
+                           (every projection with at most gemm_acc_width rows, at small batch); left zero
+                           after every step */
     /* H4B_BATCH_ATTN_EXACT (0): the fp32 split kernel, each row bit-identical
      * to a decode step. H4B_BATCH_ATTN_TENSOR (1): tcgen05 attention with
      * split-fp16 operands (fp32 outputs within the 1e-3 relative tolerance)
@@ -286,6 +298,9 @@ typedef struct h4b_batch_state {
      * attn_splits), where the cache is fp16, head_dim 128 and 4 q heads share
      * a kv head; else as 0. */
     int attn_kernel;
+    /* int32 row width of gemm_acc; 0 = max((heads + 2 kv_heads) * head_dim, hidden). 2 * intermediate
+     * lets the gate/up projection use it as well. */
+    int gemm_acc_width;
 } h4b_batch_state;
 
 #define H4B_BATCH_ATTN_EXACT 0

@@ -72,6 +72,48 @@ def test_tcgen05_equals_mma_sync_at_prefill_size(rows, width):
     assert torch.equal(a[:64], want[:64])
 
 
+# (tokens, rows, width): stream-K at M <= 64 (gate_up's 152 row tiles, qkv,
+# o, down, tiny), the LM head (too many tiles: no split, acc untouched),
+# split-K slices at M = 100, a prefill-sized M with no split
+ACC_SHAPES = [(64, 19456, 2560), (64, 6144, 2560), (64, 2560, 4096), (64, 2560, 9728), (33, 19456, 2560),
+              (1, 128, 128), (17, 384, 256), (64, 151936, 2560), (100, 2560, 2560), (2048, 2560, 2560)]
+
+
+@pytest.mark.parametrize("tokens,rows,width", ACC_SHAPES)
+def test_gemm_through_acc_buffer_same_bits(tokens, rows, width):
+    """h4b_int4_gemm_acc (K split over CTAs, exact int32 partial sums added in
+    a zeroed buffer): the same bits as h4b_int4_gemm and as exact integer
+    sums, the residual form equal to x + proj, the buffer left zero."""
+    g = torch.Generator(device="cuda").manual_seed(tokens * 131 + rows + width)
+    x8 = torch.randint(-127, 128, (tokens, width), dtype=torch.int8, device="cuda", generator=g)
+    act = torch.rand(tokens, device="cuda", generator=g) * 1e-2
+    sums = x8.to(torch.int32).sum(dim=1, dtype=torch.int32)
+    codes = torch.randint(-7, 8, (rows, width), dtype=torch.int16, device="cuda", generator=g)
+    w = ((codes[:, 0::2] & 0xF) | ((codes[:, 1::2] & 0xF) << 4)).to(torch.uint8)
+    scales = torch.rand(rows, device="cuda", generator=g) * 1e-2
+    acc = torch.zeros(tokens * rows, dtype=torch.int32, device="cuda")
+    plain = ops.int4_gemm(x8, act, sums, w, scales)
+    split = ops.int4_gemm_acc(x8, act, sums, w, scales, acc)
+    prev = torch.randn(tokens, rows, device="cuda", generator=g)
+    res = ops.int4_gemm_acc(x8, act, sums, w, scales, acc, out=prev.clone(), residual=True)
+    torch.cuda.synchronize()
+    assert torch.equal(split, plain)
+    assert torch.equal(res, prev + plain)
+    assert int(acc.abs().max()) == 0
+    m = min(tokens, 64)
+    dense = (codes.to(torch.float64) @ x8[:m].to(torch.float64).T).T  # exact integers in float64
+    assert torch.equal(split[:m], (dense.to(torch.float32) * act[:m, None]) * scales[None, :])
+
+
+def test_gemm_acc_rejects_short_buffer():
+    x8 = torch.zeros(4, 256, dtype=torch.int8, device="cuda")
+    w = torch.zeros(128, 128, dtype=torch.uint8, device="cuda")
+    one = torch.ones(4, device="cuda")
+    with pytest.raises(ValueError):
+        ops.int4_gemm_acc(x8, one, torch.zeros(4, dtype=torch.int32, device="cuda"), w, torch.ones(128, device="cuda"),
+                          torch.zeros(10, dtype=torch.int32, device="cuda"))
+
+
 def test_tcgen05_rejects_width_not_multiple_of_128():
     x8 = torch.zeros(4, 64, dtype=torch.int8, device="cuda")
     act = torch.ones(4, device="cuda")
