@@ -496,6 +496,28 @@ __global__ void split_finalize_kernel(int32_t* acc, const float* act_scale, cons
     }
 }
 
+// The same, four columns per thread, row m = blockIdx.y (N % 4 == 0 and
+// acc, w_scale, out 16-byte aligned).
+__global__ void split_finalize_vec_kernel(int32_t* acc, const float* act_scale, const float* w_scale, float* out,
+                                          int N, int residual) {
+    const int m = blockIdx.y;
+    const int n = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (n >= N) return;
+    const size_t i = static_cast<size_t>(m) * N + n;
+    const int4 sum = *reinterpret_cast<const int4*>(acc + i);
+    const float4 ws = *reinterpret_cast<const float4*>(w_scale + n);
+    const float as = act_scale[m];
+    const float4 prev = residual ? *reinterpret_cast<const float4*>(out + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    auto value = [&](int v, float w, float p) {
+        const float x = __fmul_rn(__fmul_rn(static_cast<float>(v), as), w);
+        return residual ? __fadd_rn(p, x) : x;
+    };
+    *reinterpret_cast<float4*>(out + i) =
+        make_float4(value(sum.x, ws.x, prev.x), value(sum.y, ws.y, prev.y), value(sum.z, ws.z, prev.z),
+                    value(sum.w, ws.w, prev.w));
+    *reinterpret_cast<int4*>(acc + i) = make_int4(0, 0, 0, 0);
+}
+
 bool tc_gemm_supported(const GemmArgs& g) {
     return g.N % kTcRows == 0 && g.K % kTcK == 0 && (reinterpret_cast<uintptr_t>(g.w) & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(g.x) & 15) == 0 && tensor_map_encoder() != nullptr;
@@ -546,9 +568,15 @@ int launch_tc(const GemmArgs& g, cudaStream_t stream) {
     H4B_CUDA_TRY(cudaGetLastError());
     if (accumulate) {
         const long long n = static_cast<long long>(g.M) * g.N;
-        split_finalize_kernel<<<static_cast<int>(std::min<long long>((n + 255) / 256, 8ll * sm_count())), 256, 0,
-                                stream>>>(g.split_acc, g.act_scale, g.w_scale, g.out, g.M, g.N,
-                                         g.residual ? 1 : 0);
+        const bool aligned = ((reinterpret_cast<uintptr_t>(g.split_acc) | reinterpret_cast<uintptr_t>(g.w_scale) |
+                               reinterpret_cast<uintptr_t>(g.out)) & 15) == 0;
+        if (aligned && g.N % 4 == 0 && g.M <= 65535)
+            split_finalize_vec_kernel<<<dim3((g.N / 4 + 255) / 256, g.M), 256, 0, stream>>>(
+                g.split_acc, g.act_scale, g.w_scale, g.out, g.N, g.residual ? 1 : 0);
+        else
+            split_finalize_kernel<<<static_cast<int>(std::min<long long>((n + 255) / 256, 8ll * sm_count())), 256, 0,
+                                    stream>>>(g.split_acc, g.act_scale, g.w_scale, g.out, g.M, g.N,
+                                             g.residual ? 1 : 0);
         H4B_CUDA_TRY(cudaGetLastError());
     }
     return 0;

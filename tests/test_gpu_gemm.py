@@ -105,6 +105,26 @@ def test_gemm_through_acc_buffer_same_bits(tokens, rows, width):
     assert torch.equal(split[:m], (dense.to(torch.float32) * act[:m, None]) * scales[None, :])
 
 
+def test_gemm_acc_unaligned_output_same_bits():
+    """An output that is not 16-byte aligned takes the scalar finalize: the
+    same bits as the vectorised one."""
+    g = torch.Generator(device="cuda").manual_seed(7)
+    tokens, rows, width = 64, 2560, 4096
+    x8 = torch.randint(-127, 128, (tokens, width), dtype=torch.int8, device="cuda", generator=g)
+    act = torch.rand(tokens, device="cuda", generator=g) * 1e-2
+    sums = x8.to(torch.int32).sum(dim=1, dtype=torch.int32)
+    w = torch.randint(0, 256, (rows, width // 2), dtype=torch.uint8, device="cuda", generator=g)
+    scales = torch.rand(rows, device="cuda", generator=g) * 1e-2
+    acc = torch.zeros(tokens * rows, dtype=torch.int32, device="cuda")
+    base = torch.randn(tokens * rows + 1, device="cuda", generator=g)
+    shifted = base[1:].view(tokens, rows)  # 4 bytes past a 16-byte boundary
+    want = shifted + ops.int4_gemm(x8, act, sums, w, scales)
+    ops.int4_gemm_acc(x8, act, sums, w, scales, acc, out=shifted, residual=True)
+    torch.cuda.synchronize()
+    assert torch.equal(shifted, want)
+    assert int(acc.abs().max()) == 0
+
+
 def test_gemm_acc_rejects_short_buffer():
     x8 = torch.zeros(4, 256, dtype=torch.int8, device="cuda")
     w = torch.zeros(128, 128, dtype=torch.uint8, device="cuda")
