@@ -9,24 +9,27 @@
 // too few rows for an MMA. So the keys are the MMA's M and the heads its N:
 //   S^T [128 keys x 16] = K_tile [128 keys x 128 d] . q^T [128 d x 16]
 //   O^T [128 d x 16]   += V_tile^T [128 d x 128 keys] . P^T [128 keys x 16]
-// (heads 4..15 are zero rows). K is read K-major as the A operand; V, laid
-// out [key][d] in the cache, is the A operand read MN-major; q^T and P^T are
-// K-major B operands in shared memory.
+// K is read K-major as the A operand; V, laid out [key][d] in the cache, is
+// the A operand read MN-major; q^T and P^T are K-major B operands in shared
+// memory.
 //
 // Precision (the tolerance contract, as the prefill's tensor-core path): the
 // fp16 K and V are the cache's own values; q and p enter as (hi, lo) fp16
-// pairs, each product the sum of two MMAs with fp32 accumulation. Softmax in
-// base 2 with a lazily moved reference maximum (p <= 2^15).
+// pairs. The (hi, lo) halves share one MMA: B rows 0-3 carry the 4 heads' hi
+// parts, rows 4-7 their lo parts (8-15 zero), so S^T columns h and 4 + h and
+// O^T columns h and 4 + h hold the two fp32 partial products of head h, added
+// by the key warps. Softmax in base 2 with a lazily moved reference maximum
+// (p <= 2^15).
 //
 // Work split: one CTA per (split, kv head, sequence); a split takes whole
 // 128-key tiles of its sequence's context. Warps 0-3 are the key warps:
 // thread = TMEM lane = key row of S^T (and d row of O^T), 4 loads K tiles and
 // owns the tensor memory, 5 loads V tiles, 6 issues the MMAs. Per tile j
 // (S^T and P^T double-buffered, b = j % 2):
-//   MMA:  S^T[b] = K_j (qhi^T + qlo^T)                   -> s_full[b], k_empty
+//   MMA:  S^T[b] = K_j [qhi qlo]^T (8 MMAs)              -> s_full[b], k_empty
 //   keys: load S^T row; per-head maxima over the tile (warp maxima exchanged
 //         through shared memory, mx_full[b]); p; P^T[b] (hi, lo) -> p_full[b]
-//   MMA:  O^T += V_j^T (Phi^T + Plo^T)                   -> o_full, v_empty
+//   MMA:  O^T += V_j^T [Phi Plo]^T (8 MMAs)              -> o_full, v_empty
 // The MMA thread issues P.V for tile j then S for tile j + 2 (S^T[b] was read
 // before p_full[b]; s_full for tile j implies P.V j - 2 completed).
 // The split's result is written as a partial (unnormalised o, m, l) in the
@@ -49,15 +52,15 @@ constexpr int kDtcThreads = 32 * 7;
 
 // Shared memory (1024-byte aligned regions):
 //   K, V: [stage][d half][128 keys x 128 B]     kDtcStages x 32 KB each
-//   q^T:  [part][d half][16 rows x 128 B]        4 x 2 KB
-//   P^T:  [buffer][part][key half][16 x 128 B]  8 x 2 KB
+//   q^T:  [d half][16 rows x 128 B]              2 x 2 KB (rows: 4 hi, 4 lo, 8 zero)
+//   P^T:  [buffer][key half][16 x 128 B]        4 x 2 KB (the same rows)
 constexpr int kDtcHalfTile = kDtcKeys * 128;         // 16 KB
 constexpr int kDtcSmallTile = kDtcN * 128;           // 2 KB
 constexpr int kDtcKOff = 0;
 constexpr int kDtcVOff = kDtcKOff + kDtcStages * 2 * kDtcHalfTile;
 constexpr int kDtcQOff = kDtcVOff + kDtcStages * 2 * kDtcHalfTile;
-constexpr int kDtcPOff = kDtcQOff + 4 * kDtcSmallTile;
-constexpr int kDtcMxOff = kDtcPOff + 8 * kDtcSmallTile;  // [2][4 warps][16] floats, then [4][16] row sums
+constexpr int kDtcPOff = kDtcQOff + 2 * kDtcSmallTile;
+constexpr int kDtcMxOff = kDtcPOff + 4 * kDtcSmallTile;  // [2][4 warps][16] floats, then [4][16] row sums
 constexpr int kDtcBarOff = kDtcMxOff + 2 * kDtcKeyWarps * kDtcN * 4 + kDtcKeyWarps * kDtcN * 4;
 constexpr int kDtcBarBytes = 256;
 constexpr int kDtcSmem = kDtcBarOff + kDtcBarBytes + 1024;
@@ -162,10 +165,8 @@ __global__ void __launch_bounds__(kDtcThreads, 1)
     const uint32_t tmem = *tmem_slot;
     auto k_half = [&](int s, int half) { return smem + kDtcKOff + (s * 2 + half) * kDtcHalfTile; };
     auto v_half = [&](int s, int half) { return smem + kDtcVOff + (s * 2 + half) * kDtcHalfTile; };
-    auto q_tile = [&](int part, int half) { return smem + kDtcQOff + (part * 2 + half) * kDtcSmallTile; };
-    auto p_tile = [&](int buf, int part, int half) {
-        return smem + kDtcPOff + ((buf * 2 + part) * 2 + half) * kDtcSmallTile;
-    };
+    auto q_tile = [&](int half) { return smem + kDtcQOff + half * kDtcSmallTile; };
+    auto p_tile = [&](int buf, int half) { return smem + kDtcPOff + (buf * 2 + half) * kDtcSmallTile; };
 
     if (warp == kDtcKWarp || warp == kDtcVWarp) {
         if (lane == 0) {  // TMA producer of the K (or V) tiles of this split
@@ -202,13 +203,11 @@ __global__ void __launch_bounds__(kDtcThreads, 1)
                 if (!mbar_wait(&k_full[s], (j / kDtcStages) & 1)) return false;
                 tc_fence_after();
 #pragma unroll
-                for (int part = 0; part < 2; ++part)
-#pragma unroll
-                    for (int kk = 0; kk < kDtcDim / 16; ++kk) {  // 16 dims = 32 bytes = +2 in the address field
-                        const uint64_t ad = sw128_desc(k_half(s, kk >> 2)) + 2 * (kk & 3);
-                        const uint64_t bd = sw128_desc(q_tile(part, kk >> 2)) + 2 * (kk & 3);
-                        tc_mma_f16(tmem + kDtcSCol + bb * kDtcN, ad, bd, kDtcIdescS, (part | kk) != 0);
-                    }
+                for (int kk = 0; kk < kDtcDim / 16; ++kk) {  // 16 dims = 32 bytes = +2 in the address field
+                    const uint64_t ad = sw128_desc(k_half(s, kk >> 2)) + 2 * (kk & 3);
+                    const uint64_t bd = sw128_desc(q_tile(kk >> 2)) + 2 * (kk & 3);
+                    tc_mma_f16(tmem + kDtcSCol + bb * kDtcN, ad, bd, kDtcIdescS, kk != 0);
+                }
                 tc_commit(&k_empty[s]);
                 tc_commit(&s_full[bb]);
                 return true;
@@ -220,15 +219,13 @@ __global__ void __launch_bounds__(kDtcThreads, 1)
                 if (!mbar_wait(&v_full[s], (j / kDtcStages) & 1)) return false;
                 tc_fence_after();
 #pragma unroll
-                for (int part = 0; part < 2; ++part)
-#pragma unroll
-                    for (int kk = 0; kk < kDtcKeys / 16; ++kk) {
-                        // A: V^T, 16 keys = 2 groups of 8 key rows = 2048 bytes on, the other
-                        // 64 dims one half tile on; B: P^T, 16 keys = 32 bytes along its rows
-                        const uint64_t ad = sw128_mn_desc(v_half(s, 0) + (kk & 7) * 2048, kDtcHalfTile);
-                        const uint64_t bd = sw128_desc(p_tile(bb, part, kk >> 2)) + 2 * (kk & 3);
-                        tc_mma_f16(tmem + kDtcOCol, ad, bd, kDtcIdescPV, (j | part | kk) != 0);
-                    }
+                for (int kk = 0; kk < kDtcKeys / 16; ++kk) {
+                    // A: V^T, 16 keys = 2 groups of 8 key rows = 2048 bytes on, the other
+                    // 64 dims one half tile on; B: P^T, 16 keys = 32 bytes along its rows
+                    const uint64_t ad = sw128_mn_desc(v_half(s, 0) + (kk & 7) * 2048, kDtcHalfTile);
+                    const uint64_t bd = sw128_desc(p_tile(bb, kk >> 2)) + 2 * (kk & 3);
+                    tc_mma_f16(tmem + kDtcOCol, ad, bd, kDtcIdescPV, (j | kk) != 0);
+                }
                 tc_commit(&v_empty[s]);
                 tc_commit(o_full);
                 return true;
@@ -245,22 +242,25 @@ __global__ void __launch_bounds__(kDtcThreads, 1)
     } else {  // key warps: thread = TMEM lane 32 warp + lane (key row of S^T, d row of O^T)
         const int row = 32 * warp + lane;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * warp) << 16);
-        // q^T (hi, lo) for the group's heads, zero rows 4..15; P^T's zero rows
+        // q^T: rows h = hi, 4 + h = lo of the group's heads, rows 8..15 zero;
+        // P^T's zero rows 8..15
         {
             const float* qh = a.q + static_cast<long long>(b) * a.q_stride + static_cast<long long>(kvh) * kDtcGroups * kDtcDim;
-            for (int e = threadIdx.x; e < kDtcN * kDtcDim / 2; e += 32 * kDtcKeyWarps) {
+            for (int e = threadIdx.x; e < kDtcGroups * kDtcDim / 2; e += 32 * kDtcKeyWarps) {
                 const int h = e / (kDtcDim / 2), d = 2 * (e % (kDtcDim / 2));
                 float2 x = make_float2(0.f, 0.f);
-                if (h < kDtcGroups && ctx > 0) x = *reinterpret_cast<const float2*>(qh + h * kDtcDim + d);
+                if (ctx > 0) x = *reinterpret_cast<const float2*>(qh + h * kDtcDim + d);
                 uint32_t hi, lo;
                 split_pair(x.x, x.y, hi, lo);
-                const int off = sw128_elem(h, d & 63);
-                *reinterpret_cast<uint32_t*>(q_tile(0, d >> 6) + off) = hi;
-                *reinterpret_cast<uint32_t*>(q_tile(1, d >> 6) + off) = lo;
+                *reinterpret_cast<uint32_t*>(q_tile(d >> 6) + sw128_elem(h, d & 63)) = hi;
+                *reinterpret_cast<uint32_t*>(q_tile(d >> 6) + sw128_elem(kDtcGroups + h, d & 63)) = lo;
             }
-            for (int e = threadIdx.x; e < 2 * 2 * 2 * (kDtcN - kDtcGroups) * 64; e += 32 * kDtcKeyWarps) {
-                const int c = e % 64, r = kDtcGroups + (e / 64) % (kDtcN - kDtcGroups), t = e / (64 * (kDtcN - kDtcGroups));
-                *reinterpret_cast<__half*>(p_tile(t >> 2, (t >> 1) & 1, t & 1) + sw128_elem(r, c)) = __float2half(0.f);
+            constexpr int kZeroRows = kDtcN - 2 * kDtcGroups;
+            for (int e = threadIdx.x; e < 6 * kZeroRows * 32; e += 32 * kDtcKeyWarps) {
+                // 6 tiles (q^T halves, P^T buffers x halves), rows 8..15, 32 column pairs each
+                const int c = 2 * (e % 32), r = 2 * kDtcGroups + (e / 32) % kZeroRows, t = e / (32 * kZeroRows);
+                uint8_t* tile = t < 2 ? q_tile(t) : p_tile((t - 2) >> 1, (t - 2) & 1);
+                *reinterpret_cast<uint32_t*>(tile + sw128_elem(r, c)) = 0u;
             }
         }
         fence_proxy_async_smem();
@@ -283,6 +283,8 @@ __global__ void __launch_bounds__(kDtcThreads, 1)
             float sv[kDtcN];
             tmem_ld16_nowait(lane_base + kDtcSCol + bb * kDtcN, sv, 0);
             tmem_wait_regs(sv);
+#pragma unroll
+            for (int h = 0; h < kDtcGroups; ++h) sv[h] = __fadd_rn(sv[h], sv[kDtcGroups + h]);  // q hi + q lo parts
             const bool in = kbase + row < t1;
             // the tile's per-head maxima: warp maxima, exchanged
             float wm[kDtcGroups];
@@ -319,7 +321,10 @@ __global__ void __launch_bounds__(kDtcThreads, 1)
                 tmem_ld16_nowait(lane_base + kDtcOCol, o, 0);
                 tmem_wait_regs(o);
 #pragma unroll
-                for (int h = 0; h < kDtcGroups; ++h) o[h] *= alpha[h];
+                for (int h = 0; h < kDtcGroups; ++h) {
+                    o[h] *= alpha[h];
+                    o[kDtcGroups + h] *= alpha[h];
+                }
                 tmem_st16(lane_base + kDtcOCol, o, 0);
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 #pragma unroll
@@ -334,9 +339,8 @@ __global__ void __launch_bounds__(kDtcThreads, 1)
                 lt[h] += p;
                 const __half hi = __float2half_rn(p);
                 const __half lo = __float2half_rn(p - __half2float(hi));
-                const int off = sw128_elem(h, row & 63);
-                *reinterpret_cast<__half*>(p_tile(bb, 0, row >> 6) + off) = hi;
-                *reinterpret_cast<__half*>(p_tile(bb, 1, row >> 6) + off) = lo;
+                *reinterpret_cast<__half*>(p_tile(bb, row >> 6) + sw128_elem(h, row & 63)) = hi;
+                *reinterpret_cast<__half*>(p_tile(bb, row >> 6) + sw128_elem(kDtcGroups + h, row & 63)) = lo;
             }
             if (j == tiles - 1 && t1 < kbase + kDtcKeys) {
                 // keys past the context: p = 0, and their V rows zeroed (a
@@ -379,7 +383,7 @@ __global__ void __launch_bounds__(kDtcThreads, 1)
 #pragma unroll
             for (int h = 0; h < kDtcGroups; ++h) {
                 const float l = ((lsum[h] + lsum[kDtcN + h]) + (lsum[2 * kDtcN + h] + lsum[3 * kDtcN + h]));
-                const float ov = tiles > 0 ? o[h] : 0.f;
+                const float ov = tiles > 0 ? __fadd_rn(o[h], o[kDtcGroups + h]) : 0.f;  // P hi + P lo parts
                 const int qh = kvh * kDtcGroups + h;
                 if (a.splits == 1) {
                     if (ctx > 0) a.out[b * a.out_stride + static_cast<long long>(qh) * kDtcDim + d] = ov * __fdiv_rn(1.0f, l);
