@@ -236,6 +236,29 @@ class CudaBatchState:
         self.desc.gemm_acc_width = acc_width
         check(lib().h4b_validate_batch(ctypes.byref(model.desc), ctypes.byref(self.desc)), "h4b_validate_batch")
         self.position = np.zeros(batch, dtype=np.int64)  # host copy of every sequence's position
+        self._steps = 0
+        self._graph = None
+
+    def step(self) -> None:
+        """One h4b_decode_batch step on the current stream. The first runs
+        eagerly (it does the once-per-device kernel set-up); later ones replay
+        a CUDA graph of the step captured on the second call: every input the
+        step reads (tokens, positions, caches, scratch) is a device buffer of
+        this state, so the one capture serves every later step."""
+        model = self.model
+        if self._steps == 0:
+            check(lib().h4b_decode_batch(ctypes.byref(model.desc), ctypes.byref(self.desc),
+                                         torch.cuda.current_stream(model.device).cuda_stream), "h4b_decode_batch")
+        else:
+            if self._graph is None:
+                graph, stream = torch.cuda.CUDAGraph(), torch.cuda.Stream(model.device)
+                stream.wait_stream(torch.cuda.current_stream(model.device))
+                with torch.cuda.graph(graph, stream=stream):
+                    check(lib().h4b_decode_batch(ctypes.byref(model.desc), ctypes.byref(self.desc),
+                                                 stream.cuda_stream), "h4b_decode_batch")
+                self._graph = graph
+            self._graph.replay()
+        self._steps += 1
 
 
 class PrefillScratch:
@@ -462,8 +485,7 @@ class CudaQwen:
         if int(state.position.max()) >= state.capacity:
             raise ValueError("decode state capacity exhausted")
         state.tokens.copy_(torch.tensor(ids, dtype=torch.int32), non_blocking=False)
-        check(lib().h4b_decode_batch(ctypes.byref(self.desc), ctypes.byref(state.desc),
-                                     torch.cuda.current_stream(self.device).cuda_stream), "h4b_decode_batch")
+        state.step()
         state.position += 1
         return state.logits
 
@@ -472,10 +494,8 @@ class CudaQwen:
         (state.tokens holds the last tokens; call forward_batch first)."""
         if int(state.position.max()) + steps > state.capacity:
             raise ValueError("decode state capacity exhausted")
-        stream = torch.cuda.current_stream(self.device).cuda_stream
         for _ in range(steps):
-            check(lib().h4b_decode_batch(ctypes.byref(self.desc), ctypes.byref(state.desc), stream),
-                  "h4b_decode_batch")
+            state.step()
         state.position += steps
 
     def generate_greedy(self, token_id: int, state: CudaDecodeState, steps: int) -> None:

@@ -72,3 +72,33 @@ def test_qwen_shaped_batch_matches_oracle_and_device_loop():
     np.testing.assert_array_equal(fresh.positions.cpu().numpy(), np.full(4, 9))
     with pytest.raises(ValueError):
         model.forward_batch([0, 1], fresh)
+
+
+@pytest.mark.parametrize("attention", ["exact", "tensor"])
+def test_graph_replayed_steps_equal_eager_launches(attention):
+    """CudaBatchState.step replays a CUDA graph from the second step on: the
+    same kernels as launching h4b_decode_batch eagerly, so the same bits."""
+    import ctypes
+
+    from harsh4b_b200._lib import check, lib
+
+    config = tiny_config(num_hidden_layers=2)
+    model = CudaQwen.from_checkpoint(synthetic_checkpoint(config, seed=71), kv_dtype="float16")
+    prompts = [synthetic_prompt(config, 9, seed=s) for s in range(3)]
+    graphed = model.new_batch_state(3, 32, attn_splits=2, attention=attention)
+    eager = model.new_batch_state(3, 32, attn_splits=2, attention=attention)
+    stream = torch.cuda.current_stream().cuda_stream
+    for i in range(len(prompts[0])):
+        ids = [p[i] for p in prompts]
+        a = model.forward_batch(ids, graphed).cpu().numpy().copy()
+        eager.tokens.copy_(torch.tensor(ids, dtype=torch.int32))
+        check(lib().h4b_decode_batch(ctypes.byref(model.desc), ctypes.byref(eager.desc), stream), "h4b_decode_batch")
+        np.testing.assert_array_equal(a, eager.logits.cpu().numpy())
+    assert graphed._graph is not None
+    model.generate_batch(graphed, 4)
+    for _ in range(4):
+        check(lib().h4b_decode_batch(ctypes.byref(model.desc), ctypes.byref(eager.desc), stream), "h4b_decode_batch")
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(graphed.logits.cpu().numpy(), eager.logits.cpu().numpy())
+    np.testing.assert_array_equal(graphed.next_tokens.cpu().numpy(), eager.next_tokens.cpu().numpy())
+    assert model.status() == 0
