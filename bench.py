@@ -899,7 +899,10 @@ def run_attention(args) -> int:
     split-K GQA over an fp16 cache) for 32 q / 8 kv heads at contexts 512,
     4096, 32768 and batch 1 and 32; the cache is filled with N(0,1) values.
     Batch 1 is the decode stage (h4b_decode_stage 2) of a session at the
-    given position, batch 32 the batched kernel (h4b_batch_attention)."""
+    given position, batch 32 the batched kernel (h4b_batch_attention), both
+    the exact fp32 kernels; every case also carries a `tensor` record, the
+    tcgen05 batched kernel (h4b_batch_attention with attention="tensor") on
+    the same shapes, batch 1 as a one-sequence batch."""
     import ctypes
 
     import torch
@@ -942,19 +945,20 @@ def run_attention(args) -> int:
                      "kv_bytes": kv_bytes}
         del st
         torch.cuda.empty_cache()
-        if batch > 1:  # the tcgen05 batched kernel on the same case (qk-norm / RoPE / append kernel + attention + merge)
-            st = model.new_batch_state(batch, ctx, attn_splits=64, attention="tensor")
-            st.k_cache.normal_(); st.v_cache.normal_(); st.qkv.normal_()
-            st.positions.fill_(ctx - 1)
+        # the tcgen05 batched kernel on the same case (qk-norm / RoPE / append kernel + attention + merge;
+        # batch 1 as a one-sequence batch)
+        st = model.new_batch_state(batch, ctx, attn_splits=64, attention="tensor")
+        st.k_cache.normal_(); st.v_cache.normal_(); st.qkv.normal_()
+        st.positions.fill_(ctx - 1)
 
-            def launch_tc(st=st):
-                check(lib().h4b_batch_attention(ctypes.byref(model.desc), ctypes.byref(st.desc), 0,
-                                                torch.cuda.current_stream().cuda_stream), "h4b_batch_attention")
-            sec_tc = _graph_time(torch, launch_tc, reps=20)
-            case_line["tensor"] = {"us": round(sec_tc * 1e6, 2), "gbs": round(kv_bytes / sec_tc / 1e9, 1),
-                                   "frac": round(kv_bytes / sec_tc / 1e9 / peaks["hbm_gbs"], 4)}
-            del st
-            torch.cuda.empty_cache()
+        def launch_tc(st=st):
+            check(lib().h4b_batch_attention(ctypes.byref(model.desc), ctypes.byref(st.desc), 0,
+                                            torch.cuda.current_stream().cuda_stream), "h4b_batch_attention")
+        sec_tc = _graph_time(torch, launch_tc, reps=20)
+        case_line["tensor"] = {"us": round(sec_tc * 1e6, 2), "gbs": round(kv_bytes / sec_tc / 1e9, 1),
+                               "frac": round(kv_bytes / sec_tc / 1e9 / peaks["hbm_gbs"], 4)}
+        del st
+        torch.cuda.empty_cache()
         results.append(case_line)
     line = {"metric": "GQA decode attention GB/s of K/V read (config 2)", "unit": "GB/s",
             "peak": peaks["hbm_gbs"], "peak_source": peaks["source"],
