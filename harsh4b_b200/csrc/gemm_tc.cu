@@ -11,20 +11,23 @@
 //           (TOK rows x 128 bytes, 128-byte swizzle) land on the stage's
 //           `full` mbarrier; the warp also allocates and frees the tensor
 //           memory. Shared memory holds only this ring (5 stages at TOK
-//           256, 8 at 128, 12 at 64);
+//           256, else 8: one per unpacked tile);
 //   warps 0 .. 4 G - 1: unpack groups of four warps, group g taking stages
 //           g, g + G, ...: thread = weight row (its warp's TMEM lane quarter),
 //           it reads the row's 64 packed bytes, expands them to 128 signed
 //           int8 codes and stores them with tcgen05.st into one of the
 //           group's unpacked tiles in tensor memory (32 columns, four codes
 //           per column; two tiles per group used in turn below TOK 256) --
-//           the MMA's A operand -- then arrives on the tile's `aready`. After
+//           the MMA's A operand (tile s for stage s) -- then arrives on the
+//           tile's `aready`. After
 //           the last stage the first sixteen warps are the epilogue, warp w
 //           reading TMEM lane quarter w % 4 (32 rows) for column slice w / 4;
 //   warp 4 G + 1 lane 0: issues tcgen05.mma kind::i8 (A s8 weights from
 //           tensor memory, B s8 activations from shared memory, D s32 in
 //           TMEM), 4 per stage (K = 32 each), and tcgen05.commit to the
-//           stage's `empty` and the tile's `afree`; a final commit signals
+//           stage's `empty`, which frees the stage and its tile (the MMA
+//           thread waits only on `aready`: its group saw the stage land before
+//           arriving); a final commit signals
 //           the epilogue.
 // Every wait is bounded (mbar_wait). A role whose wait runs out reports
 // kStatusWaitTimeout, marks the CTA as failed and stops issuing; the
@@ -52,7 +55,9 @@ struct TcCfg {
     // one per group at TOK 256, whose accumulator takes 256 columns.
     static constexpr int kSlotsPerGroup = TOK == 256 ? 1 : 2;
     static constexpr int kASlots = kGroups * kSlotsPerGroup;
-    static constexpr int kStages = TOK == 256 ? 5 : (TOK == 128 ? 8 : 12);
+    // One TMA stage per unpacked tile: stage s and tile s are used by the
+    // same iterations, so a single commit per stage frees both.
+    static constexpr int kStages = TOK == 256 ? 5 : 8;
     static constexpr int kUnpackWarps = kGroups * kTcGroupWarps;
     static constexpr int kProducerWarp = kUnpackWarps, kMmaWarp = kUnpackWarps + 1;
     static constexpr int kThreads = 32 * (kUnpackWarps + 2);
@@ -71,9 +76,10 @@ struct TcCfg {
     static constexpr uint32_t kTmemCols = kACol + 32 * kASlots <= 256 ? 256 : 512;
     static_assert(kStageBytes % 1024 == 0, "tiles keep the 1024-byte swizzle alignment");
     static_assert(kStages % kGroups == 0, "each group must own whole stages");
+    static_assert(kStages == kGroups * kSlotsPerGroup, "stage s is unpacked into tile s");
     static_assert(kSmem <= 232448, "shared memory per CTA");
     static_assert(kACol + 32 * kASlots <= kTmemCols, "tensor memory");
-    static_assert(2 * kStages * 8 + 2 * kASlots * 8 + 16 <= kBarrierBytes, "barrier area");
+    static_assert(2 * kStages * 8 + kASlots * 8 + 16 <= kBarrierBytes, "barrier area");
 };
 
 struct TcArgs {
@@ -175,10 +181,9 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
     // access into a generic load or store)
     uint8_t* smem = tc_smem_raw + ((1024u - (smem_addr(tc_smem_raw) & 1023u)) & 1023u);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarrierOff);  // TMA stage landed
-    uint64_t* empty = full + C::kStages;                                   // TMA stage consumed by the MMAs
-    uint64_t* aready = empty + C::kStages;                                 // unpacked tile a written
-    uint64_t* afree = aready + C::kASlots;                                 // unpacked tile a read by the MMAs
-    uint64_t* accfull = afree + C::kASlots;
+    uint64_t* empty = full + C::kStages;  // stage s and unpacked tile s consumed by the MMAs
+    uint64_t* aready = empty + C::kStages;                                 // unpacked tile s written
+    uint64_t* accfull = aready + C::kASlots;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accfull + 1);
     volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -211,10 +216,7 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int a = 0; a < C::kASlots; ++a) {
-            mbar_init(&aready[a], kTcGroupWarps);
-            mbar_init(&afree[a], 1);
-        }
+        for (int a = 0; a < C::kASlots; ++a) mbar_init(&aready[a], kTcGroupWarps);
         mbar_init(accfull, 1);
         *failed = wait_failed_before() ? 1 : 0;
         fence_mbar_init();
@@ -266,16 +268,17 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
         if (lane == 0) {  // MMA issuer
             constexpr uint32_t idesc = tc_idesc<TOK>();
             for (int it = 0; it < steps && !*failed; ++it) {
-                const int s = it % C::kStages, use = it / C::kGroups;
-                const int a = it % C::kGroups + C::kGroups * (use % C::kSlotsPerGroup);
-                if (!mbar_wait(&full[s], (it / C::kStages) & 1) ||
-                    !mbar_wait(&aready[a], (use / C::kSlotsPerGroup) & 1)) {
+                // tile s is unpacked by a group that waited for stage s to
+                // land, so its aready (acquired here) covers the TMA's
+                // activation tile as well
+                const int s = it % C::kStages;
+                if (!mbar_wait(&aready[s], (it / C::kStages) & 1)) {
                     *failed = 1;
                     break;
                 }
                 tc_fence_after();
                 const uint64_t bdesc = sw128_desc(stage(s) + C::kBOff);
-                const uint32_t atmem = tmem + C::kACol + 32 * a;
+                const uint32_t atmem = tmem + C::kACol + 32 * s;
                 // the second row tile of a stream-K range: the second accumulator
                 const bool next = it >= len0;
                 const uint32_t dtmem = tmem + (next ? TOK : 0);
@@ -283,8 +286,7 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
 #pragma unroll
                 for (int kk = 0; kk < kTcK / 32; ++kk)  // K = 32: 8 columns of A, +32 bytes (+2) along B
                     tc_mma_i8_ts(dtmem, atmem + 8 * kk, bdesc + 2 * kk, idesc, (it != first) || kk != 0);
-                tc_commit(&empty[s]);
-                tc_commit(&afree[a]);
+                tc_commit(&empty[s]);  // stage s and tile s free again
             }
             tc_commit(accfull);  // arrives once every MMA issued above has completed
         }
@@ -295,12 +297,10 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
         const int row = quarter * 32 + lane;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         for (int it = group; it < steps; it += C::kGroups) {
-            const int s = it % C::kStages;
-            const int use = it / C::kGroups;  // this group's stage count
-            const int a = group + C::kGroups * (use % C::kSlotsPerGroup);
-            const int k = use / C::kSlotsPerGroup;  // tile a's use count
-            const bool ok = __all_sync(0xffffffffu, !*failed && (k == 0 || mbar_wait(&afree[a], (k - 1) & 1)) &&
-                                                        mbar_wait(&full[s], (it / C::kStages) & 1));
+            const int s = it % C::kStages;  // the TMA stage and the unpacked tile
+            const int k = it / C::kStages;  // their use count
+            const bool ok = __all_sync(0xffffffffu, !*failed && (k == 0 || mbar_wait(&empty[s], (k - 1) & 1)) &&
+                                                        mbar_wait(&full[s], k & 1));
             if (!ok) {
                 if (lane == 0) *failed = 1;
                 break;
@@ -322,7 +322,7 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
                 codes[8 * c + 6] = nib_s8(w.w, 0x1100);
                 codes[8 * c + 7] = nib_s8(w.w, 0x3322);
             }
-            const uint32_t acol = lane_base + C::kACol + 32 * a;
+            const uint32_t acol = lane_base + C::kACol + 32 * s;
 #pragma unroll
             for (int h = 0; h < 2; ++h)
                 asm volatile(
@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(TcCfg<TOK>::kThreads, 1)
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();  // tensor-memory stores -> ordered before the MMAs that read them
             __syncwarp();
-            if (lane == 0) mbar_arrive(&aready[a]);
+            if (lane == 0) mbar_arrive(&aready[s]);
         }
         // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = weight rows n0 + 32 (w % 4) + lane,
         // columns (tokens) of slice w / 4
