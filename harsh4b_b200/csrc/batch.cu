@@ -90,16 +90,21 @@ __global__ void __launch_bounds__(256) batch_rmsnorm_quant_kernel(const float* x
 // batch_rmsnorm_quant_kernel's result, bit for bit (each thread keeps the
 // same groups in the same order, and the block reductions are the same), with
 // the thread's kG groups of 8 held in registers: one read of the row instead
-// of three.
+// of three. With pending residual sums (the o / down GEMM's split-K sums left
+// in pend.acc), it first does the finalize kernel's residual step on its row,
+// x = x + float(acc) * as * ws in that order, stores x and zeroes acc.
 template <int kG>
-__global__ void __launch_bounds__(256) batch_rmsnorm_quant_reg_kernel(const float* x, const float* gamma, float eps,
+__global__ void __launch_bounds__(256) batch_rmsnorm_quant_reg_kernel(float* x, const float* gamma, float eps,
                                                                       int H, int8_t* x8, float* act_scale,
-                                                                      int32_t* act_sum) {
+                                                                      int32_t* act_sum, PendingSums pend) {
     __shared__ float red[32];
     __shared__ int ired[8];
     const int b = blockIdx.x, tid = threadIdx.x;
-    const float* row = x + static_cast<size_t>(b) * H;
+    float* row = x + static_cast<size_t>(b) * H;
     const int groups = H >> 3;
+    // read before this row's scale is overwritten at the end (after the barriers)
+    int32_t* prow = pend.acc ? pend.acc + static_cast<size_t>(b) * pend.stride : nullptr;
+    const float pas = pend.acc ? pend.as[b] : 0.f;
     float v[kG][8], gm[kG][8];
     float ss = 0.f;
 #pragma unroll
@@ -108,6 +113,20 @@ __global__ void __launch_bounds__(256) batch_rmsnorm_quant_reg_kernel(const floa
         if (g < groups) {
             load8(row + 8 * g, v[k]);
             load8(gamma + 8 * g, gm[k]);
+            if (prow) {
+                int4* cell = reinterpret_cast<int4*>(prow + 8 * g);
+                const int4 s0 = cell[0], s1 = cell[1];
+                float w[8];
+                load8(pend.ws + 8 * g, w);
+                const int sum[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[k][e] = __fadd_rn(v[k][e], pending_value(sum[e], pas, w[e]));
+                float4* out = reinterpret_cast<float4*>(row + 8 * g);
+                out[0] = make_float4(v[k][0], v[k][1], v[k][2], v[k][3]);
+                out[1] = make_float4(v[k][4], v[k][5], v[k][6], v[k][7]);
+                cell[0] = make_int4(0, 0, 0, 0);
+                cell[1] = make_int4(0, 0, 0, 0);
+            }
 #pragma unroll
             for (int e = 0; e < 8; ++e) ss = __fmaf_rn(v[k][e], v[k][e], ss);
         }
@@ -159,15 +178,23 @@ __global__ void __launch_bounds__(256) batch_rmsnorm_quant_reg_kernel(const floa
 
 // RMSNorm + per-row quantisation of `rows` rows of H (the register kernel
 // when a thread's share fits, else the three-pass kernel).
-int launch_rmsnorm_quant(const float* x, const float* gamma, float eps, int H, int rows, int8_t* x8,
-                         float* act_scale, int32_t* act_sum, cudaStream_t stream) {
+inline bool rmsnorm_quant_reg_fits(int H) { return H % 8 == 0 && (H / 8 + 255) / 256 <= 4; }
+
+// `pend` (the register kernel only): the pending residual sums of the
+// projection that produced x, applied to x first.
+int launch_rmsnorm_quant(float* x, const float* gamma, float eps, int H, int rows, int8_t* x8,
+                         float* act_scale, int32_t* act_sum, cudaStream_t stream, PendingSums pend = {}) {
     const int per = (H / 8 + 255) / 256;
+    if (pend.acc && (!rmsnorm_quant_reg_fits(H) || pend.stride % 4 != 0 ||
+                     ((reinterpret_cast<uintptr_t>(pend.acc) | reinterpret_cast<uintptr_t>(pend.ws) |
+                       reinterpret_cast<uintptr_t>(x)) & 15) != 0))
+        return H4B_EUNSUPPORTED;
     if (H % 8 == 0 && per <= 1)
-        batch_rmsnorm_quant_reg_kernel<1><<<rows, 256, 0, stream>>>(x, gamma, eps, H, x8, act_scale, act_sum);
+        batch_rmsnorm_quant_reg_kernel<1><<<rows, 256, 0, stream>>>(x, gamma, eps, H, x8, act_scale, act_sum, pend);
     else if (H % 8 == 0 && per == 2)
-        batch_rmsnorm_quant_reg_kernel<2><<<rows, 256, 0, stream>>>(x, gamma, eps, H, x8, act_scale, act_sum);
+        batch_rmsnorm_quant_reg_kernel<2><<<rows, 256, 0, stream>>>(x, gamma, eps, H, x8, act_scale, act_sum, pend);
     else if (H % 8 == 0 && per <= 4)
-        batch_rmsnorm_quant_reg_kernel<4><<<rows, 256, 0, stream>>>(x, gamma, eps, H, x8, act_scale, act_sum);
+        batch_rmsnorm_quant_reg_kernel<4><<<rows, 256, 0, stream>>>(x, gamma, eps, H, x8, act_scale, act_sum, pend);
     else
         batch_rmsnorm_quant_kernel<<<rows, 256, 0, stream>>>(x, gamma, eps, H, x8, act_scale, act_sum);
     H4B_CUDA_TRY(cudaGetLastError());
@@ -283,14 +310,30 @@ int decode_batch(const h4b_model* m, const h4b_batch_state* s, cudaStream_t stre
     const int acc_rows = s->gemm_acc_width > 0
                              ? s->gemm_acc_width
                              : std::max(m->heads * m->head_dim + 2 * m->kv_heads * m->head_dim, m->hidden);
-    auto gemm = [&](const uint8_t* w, const float* ws, float* out, int rows, int width, bool residual = false) {
+    // `deferred` (o, down, gate/up): a split GEMM leaves its int32 sums
+    // pending in gemm_acc instead of running the finalize kernel, and the
+    // next kernel -- the RMSNorm quantisation after o / down, the SwiGLU
+    // quantisation after gate/up -- applies them with the same arithmetic
+    auto gemm = [&](const uint8_t* w, const float* ws, float* out, int rows, int width, bool residual = false,
+                    bool* deferred = nullptr) {
         GemmArgs g{s->x8, s->act_scale, s->act_sum, w, ws, out, B, rows, width};
         g.split_acc = rows <= acc_rows ? s->gemm_acc : nullptr;
         g.residual = residual;
+        if (deferred) *deferred = false;
+        g.finalize_deferred = g.split_acc ? deferred : nullptr;
         return launch_int4_gemm(g, stream);
     };
+    auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const bool defer_x = rmsnorm_quant_reg_fits(H) && aligned16(s->x) && aligned16(s->gemm_acc) &&
+                         aligned16(m->s_o) && aligned16(m->s_down) && H % 4 == 0;
+    const bool defer_gu = quantize_rows_reg_fits(I) && aligned16(s->gate_up) && aligned16(s->gemm_acc) &&
+                          aligned16(m->s_gate_up) && (reinterpret_cast<uintptr_t>(s->x8) & 3) == 0;
+    PendingSums pend_x;  // o / down sums pending on x, applied by the next RMSNorm quantisation
     auto norm_quant = [&](const float* gamma) {
-        return launch_rmsnorm_quant(s->x, gamma, m->eps, H, B, s->x8, s->act_scale, s->act_sum, stream);
+        const int r = launch_rmsnorm_quant(s->x, gamma, m->eps, H, B, s->x8, s->act_scale, s->act_sum, stream,
+                                           pend_x);
+        pend_x = PendingSums{};
+        return r;
     };
     batch_embed_kernel<<<B, 256, 0, stream>>>(s->tokens, m->w_embed, m->s_embed, m->vocab, H, s->x);
     H4B_CUDA_TRY(cudaGetLastError());
@@ -305,18 +348,28 @@ int decode_batch(const h4b_model* m, const h4b_batch_state* s, cudaStream_t stre
         if ((rc = launch_quantize_rows<false>(s->attended, q_size, B, s->x8, s->act_scale, s->act_sum, nullptr,
                                               stream)))
             return rc;
-        if ((rc = gemm(m->w_o + static_cast<size_t>(l) * H * (q_size / 2), m->s_o + static_cast<size_t>(l) * H, s->x,
-                       H, q_size, true)))
+        bool deferred = false;
+        const float* s_o = m->s_o + static_cast<size_t>(l) * H;
+        if ((rc = gemm(m->w_o + static_cast<size_t>(l) * H * (q_size / 2), s_o, s->x, H, q_size, true,
+                       defer_x ? &deferred : nullptr)))
             return rc;
+        if (deferred) pend_x = PendingSums{s->gemm_acc, s->act_scale, s_o, H};
         if ((rc = norm_quant(m->norm_post + static_cast<size_t>(l) * H))) return rc;
-        if ((rc = gemm(m->w_gate_up + static_cast<size_t>(l) * 2 * I * (H / 2),
-                       m->s_gate_up + static_cast<size_t>(l) * 2 * I, s->gate_up, 2 * I, H)))
+        const float* s_gu = m->s_gate_up + static_cast<size_t>(l) * 2 * I;
+        deferred = false;
+        if ((rc = gemm(m->w_gate_up + static_cast<size_t>(l) * 2 * I * (H / 2), s_gu, s->gate_up, 2 * I, H, false,
+                       defer_gu ? &deferred : nullptr)))
             return rc;
-        if ((rc = launch_quantize_rows<true>(s->gate_up, I, B, s->x8, s->act_scale, s->act_sum, s->act, stream)))
+        const PendingSums pend_gu = deferred ? PendingSums{s->gemm_acc, s->act_scale, s_gu, 2 * I} : PendingSums{};
+        if ((rc = launch_quantize_rows<true>(s->gate_up, I, B, s->x8, s->act_scale, s->act_sum, s->act, stream,
+                                             pend_gu)))
             return rc;
-        if ((rc = gemm(m->w_down + static_cast<size_t>(l) * H * (I / 2), m->s_down + static_cast<size_t>(l) * H, s->x,
-                       H, I, true)))
+        const float* s_down = m->s_down + static_cast<size_t>(l) * H;
+        deferred = false;
+        if ((rc = gemm(m->w_down + static_cast<size_t>(l) * H * (I / 2), s_down, s->x, H, I, true,
+                       defer_x ? &deferred : nullptr)))
             return rc;
+        if (deferred) pend_x = PendingSums{s->gemm_acc, s->act_scale, s_down, H};  // the next RMSNorm applies it
     }
     if ((rc = norm_quant(m->norm_final))) return rc;
     if ((rc = gemm(m->w_embed, m->s_embed, s->logits, m->vocab, H))) return rc;

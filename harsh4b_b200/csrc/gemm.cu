@@ -40,7 +40,24 @@ struct GemmArgs {
     // with a float `out`: out[m][n] = out[m][n] + value (the residual add,
     // x + proj in that order) instead of out[m][n] = value
     bool residual = false;
+    // when set and the K sum is split through split_acc: no finalize kernel;
+    // *finalize_deferred says whether the sums were left pending in split_acc
+    // (for the consumer to apply, see PendingSums), else it is set false
+    bool* finalize_deferred = nullptr;
 };
+
+// GEMM results left as exact int32 sums: value[m][n] = float(acc[m][n]) *
+// as[m] * ws[n] (the GEMM epilogue's order), which the consumer applies -- and
+// then zeroes acc -- instead of a finalize kernel. acc rows are `stride` wide.
+struct PendingSums {
+    int32_t* acc = nullptr;
+    const float* as = nullptr;
+    const float* ws = nullptr;
+    int stride = 0;
+};
+__device__ __forceinline__ float pending_value(int sum, float as, float ws) {
+    return __fmul_rn(__fmul_rn(static_cast<float>(sum), as), ws);
+}
 
 // cp.async with a source size: bytes past src_bytes are zero-filled.
 __device__ __forceinline__ void async_copy16_zfill(void* dst, const void* src, int src_bytes) {
@@ -202,11 +219,16 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const float* v, int 
 // itself is never stored. The maximum and the code sum are order-free.
 template <int kThreads, int kGroups, bool kSwiglu>
 __global__ void __launch_bounds__(kThreads) quantize_rows_reg_kernel(const float* v, int K, int8_t* q,
-                                                                    float* scales, int32_t* sums) {
+                                                                    float* scales, int32_t* sums, PendingSums pend) {
     __shared__ float red[kThreads / 32];
     __shared__ int ired[kThreads / 32];
     const int groups = K / 4;
     const float4* row = reinterpret_cast<const float4*>(v + static_cast<size_t>(blockIdx.x) * (kSwiglu ? 2 : 1) * K);
+    // pending GEMM sums instead of v (SwiGLU rows only): read before this
+    // row's scale is overwritten below (after the barriers)
+    int4* prow = pend.acc ? reinterpret_cast<int4*>(pend.acc + static_cast<size_t>(blockIdx.x) * pend.stride) : nullptr;
+    const float pas = pend.acc ? pend.as[blockIdx.x] : 0.f;
+    const float4* pws = reinterpret_cast<const float4*>(pend.ws);
     float4 a[kGroups];
     float mx = 0.f;
 #pragma unroll
@@ -215,7 +237,20 @@ __global__ void __launch_bounds__(kThreads) quantize_rows_reg_kernel(const float
         a[k] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (gi < groups) {
             if constexpr (kSwiglu) {
-                const float4 g = row[2 * gi], u = row[2 * gi + 1];
+                float4 g, u;
+                if (prow) {
+                    const int4 sg = prow[2 * gi], su = prow[2 * gi + 1];
+                    const float4 wg = pws[2 * gi], wu = pws[2 * gi + 1];
+                    g = make_float4(pending_value(sg.x, pas, wg.x), pending_value(sg.y, pas, wg.y),
+                                    pending_value(sg.z, pas, wg.z), pending_value(sg.w, pas, wg.w));
+                    u = make_float4(pending_value(su.x, pas, wu.x), pending_value(su.y, pas, wu.y),
+                                    pending_value(su.z, pas, wu.z), pending_value(su.w, pas, wu.w));
+                    prow[2 * gi] = make_int4(0, 0, 0, 0);
+                    prow[2 * gi + 1] = make_int4(0, 0, 0, 0);
+                } else {
+                    g = row[2 * gi];
+                    u = row[2 * gi + 1];
+                }
                 a[k] = make_float4(swiglu_one(g.x, u.x), swiglu_one(g.y, u.y), swiglu_one(g.z, u.z),
                                    swiglu_one(g.w, u.w));
             } else {
@@ -262,8 +297,15 @@ __global__ void batch_swiglu_kernel(const float* gate_up, int I, int B, float* a
 
 template <bool kSwiglu, int G>
 void launch_quantize_reg(const float* v, int K, int rows, int8_t* q, float* scales, int32_t* sums,
-                         cudaStream_t stream) {
-    quantize_rows_reg_kernel<kQuantThreads, G, kSwiglu><<<rows, kQuantThreads, 0, stream>>>(v, K, q, scales, sums);
+                         cudaStream_t stream, PendingSums pend) {
+    quantize_rows_reg_kernel<kQuantThreads, G, kSwiglu><<<rows, kQuantThreads, 0, stream>>>(v, K, q, scales, sums,
+                                                                                           pend);
+}
+
+// Whether launch_quantize_rows takes its register kernel (the only one that
+// applies pending GEMM sums) for rows of K values.
+inline bool quantize_rows_reg_fits(int K) {
+    return K % 4 == 0 && (K / 4 + kQuantThreads - 1) / kQuantThreads <= kQuantMaxGroups;
 }
 
 // Per-row quantisation of `rows` rows of K values (kSwiglu: of the SwiGLU of
@@ -272,23 +314,27 @@ void launch_quantize_reg(const float* v, int K, int rows, int8_t* q, float* scal
 // needs `act`, [rows][K], for the intermediate values).
 template <bool kSwiglu>
 int launch_quantize_rows(const float* v, int K, int rows, int8_t* q, float* scales, int32_t* sums, float* act,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, PendingSums pend = {}) {
     const int per = (K / 4 + kQuantThreads - 1) / kQuantThreads;
-    if (K % 4 == 0 && per <= kQuantMaxGroups && (reinterpret_cast<uintptr_t>(v) & 15) == 0 &&
+    if (pend.acc && (!kSwiglu || !quantize_rows_reg_fits(K) || pend.stride % 4 != 0 ||
+                     ((reinterpret_cast<uintptr_t>(pend.acc) | reinterpret_cast<uintptr_t>(pend.ws)) & 15) != 0))
+        return H4B_EUNSUPPORTED;
+    if (quantize_rows_reg_fits(K) && (reinterpret_cast<uintptr_t>(v) & 15) == 0 &&
         (reinterpret_cast<uintptr_t>(q) & 3) == 0) {
         switch (per) {
             case 0:
-            case 1: launch_quantize_reg<kSwiglu, 1>(v, K, rows, q, scales, sums, stream); break;
-            case 2: launch_quantize_reg<kSwiglu, 2>(v, K, rows, q, scales, sums, stream); break;
-            case 3: launch_quantize_reg<kSwiglu, 3>(v, K, rows, q, scales, sums, stream); break;
-            case 4: launch_quantize_reg<kSwiglu, 4>(v, K, rows, q, scales, sums, stream); break;
-            case 5: launch_quantize_reg<kSwiglu, 5>(v, K, rows, q, scales, sums, stream); break;
-            case 6: launch_quantize_reg<kSwiglu, 6>(v, K, rows, q, scales, sums, stream); break;
-            default: launch_quantize_reg<kSwiglu, 8>(v, K, rows, q, scales, sums, stream); break;
+            case 1: launch_quantize_reg<kSwiglu, 1>(v, K, rows, q, scales, sums, stream, pend); break;
+            case 2: launch_quantize_reg<kSwiglu, 2>(v, K, rows, q, scales, sums, stream, pend); break;
+            case 3: launch_quantize_reg<kSwiglu, 3>(v, K, rows, q, scales, sums, stream, pend); break;
+            case 4: launch_quantize_reg<kSwiglu, 4>(v, K, rows, q, scales, sums, stream, pend); break;
+            case 5: launch_quantize_reg<kSwiglu, 5>(v, K, rows, q, scales, sums, stream, pend); break;
+            case 6: launch_quantize_reg<kSwiglu, 6>(v, K, rows, q, scales, sums, stream, pend); break;
+            default: launch_quantize_reg<kSwiglu, 8>(v, K, rows, q, scales, sums, stream, pend); break;
         }
         H4B_CUDA_TRY(cudaGetLastError());
         return 0;
     }
+    if (pend.acc) return H4B_EUNSUPPORTED;
     const float* src = v;
     if constexpr (kSwiglu) {
         if (!act) return H4B_EUNSUPPORTED;

@@ -566,7 +566,8 @@ int launch_tc(const GemmArgs& g, cudaStream_t stream) {
     const dim3 grid = stream_ctas > 0 ? dim3(stream_ctas, 1, 1) : dim3((g.M + TOK - 1) / TOK, g.N / kTcRows, ksplit);
     int4_gemm_tc_kernel<TOK><<<grid, C::kThreads, C::kSmem, stream>>>(wmap, xmap, a);
     H4B_CUDA_TRY(cudaGetLastError());
-    if (accumulate) {
+    if (g.finalize_deferred) *g.finalize_deferred = accumulate;
+    if (accumulate && !g.finalize_deferred) {
         const long long n = static_cast<long long>(g.M) * g.N;
         const bool aligned = ((reinterpret_cast<uintptr_t>(g.split_acc) | reinterpret_cast<uintptr_t>(g.w_scale) |
                                reinterpret_cast<uintptr_t>(g.out)) & 15) == 0;
@@ -587,6 +588,7 @@ int launch_tc(const GemmArgs& g, cudaStream_t stream) {
 int launch_int4_gemm(const GemmArgs& g, cudaStream_t stream, int kernel = 0) {
     if (g.M < 1 || g.N < 1 || g.K < 1) return H4B_EINVAL;
     if (kernel < 0 || kernel > 2) return H4B_EINVAL;
+    if (g.finalize_deferred) *g.finalize_deferred = false;  // the mma.sync kernel writes out directly
     if (kernel == 2 || (kernel == 0 && !tc_gemm_supported(g))) return launch_int4_gemm_mma(g, stream);
     if (!tc_gemm_supported(g)) return H4B_EUNSUPPORTED;
     if (g.M <= 64) return launch_tc<64>(g, stream);
