@@ -305,21 +305,20 @@ def run_ours(args, rank, world, local_rank, dist) -> int:
     last_token = state.next_token_host()
     status = model.status()
 
-    # ---- e2e: host round trip per token through forward_token ----
+    # ---- e2e: host round trip per token (token id in from pinned host memory,
+    # greedy id out) through CudaQwen.decode_greedy ----
     e2e_state = model.new_state(capacity)
     for token_id in prompt:
         model.forward_token(token_id, e2e_state)
     token = e2e_state.next_token_host()
     for _ in range(args.warmup):
-        model.forward_token(token, e2e_state)
-        token = e2e_state.next_token_host()
+        token = model.decode_greedy(token, e2e_state)
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     e_start.record(e2e_state.stream)
     for _ in range(args.steps):
-        model.forward_token(token, e2e_state)
-        token = e2e_state.next_token_host()
+        token = model.decode_greedy(token, e2e_state)
     e_end.record(e2e_state.stream)
     torch.cuda.synchronize()
     barrier()

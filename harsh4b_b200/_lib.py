@@ -102,6 +102,7 @@ _SIGNATURES = {
     "h4b_quantize_rows": [_vp, _vp, _vp, _vp, _i32, _i32, _vp],
     "h4b_int4_gemm": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp],
     "h4b_int4_gemm_ex": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
+    "h4b_graph_token": [_vp, _vp, _vp, _vp, _vp, _vp],
     "h4b_int4_gemm_acc": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp],
     "h4b_validate_batch": [ctypes.POINTER(ModelDesc), ctypes.POINTER(BatchStateDesc)],
     "h4b_int4_gemv_absmax": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp],

@@ -386,6 +386,17 @@ extern "C" int h4b_graph_launch(void* graph, void* stream) {
                                             static_cast<cudaStream_t>(stream)));
 }
 
+extern "C" int h4b_graph_token(void* graph, const int32_t* token_host, int32_t* token_dev, const int32_t* next_dev,
+                               int32_t* next_host, void* stream) {
+    if (!graph || !token_host || !token_dev || !next_dev || !next_host) return H4B_EINVAL;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    H4B_CUDA_TRY(cudaMemcpyAsync(token_dev, token_host, sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    H4B_CUDA_TRY(cudaGraphLaunch(static_cast<h4b::GraphHandle*>(graph)->exec, s));
+    H4B_CUDA_TRY(cudaMemcpyAsync(next_host, next_dev, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    H4B_CUDA_TRY(cudaStreamSynchronize(s));
+    return 0;
+}
+
 extern "C" int h4b_graph_destroy(void* graph) {
     if (!graph) return 0;
     h4b::GraphHandle* h = static_cast<h4b::GraphHandle*>(graph);

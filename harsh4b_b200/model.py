@@ -164,6 +164,19 @@ class CudaDecodeState:
             check(lib().h4b_graph_launch(self._graph, self.stream.cuda_stream), "h4b_graph_launch")
         self.position += steps
 
+    def greedy_token(self, token_id: int) -> int:
+        """One decode step fed `token_id` from the host, returning its greedy
+        token to the host (h4b_graph_token: one call for the pinned copy in,
+        the graph launch, the copy out and the wait)."""
+        self._ensure_graph()
+        self._copied.synchronize()  # a set_token copy may still read the pinned slot
+        self._token_host[0] = int(token_id)
+        check(lib().h4b_graph_token(self._graph, self._token_host.data_ptr(), self.token_dev.data_ptr(),
+                                    self.next_token_dev.data_ptr(), self._next_host.data_ptr(),
+                                    self.stream.cuda_stream), "h4b_graph_token")
+        self.position += 1
+        return int(self._next_host[0])
+
     def next_token_host(self) -> int:
         """Device -> host read of the greedy token of the last step."""
         with torch.cuda.stream(self.stream):
@@ -428,6 +441,14 @@ class CudaQwen:
         state.replay()
         current.wait_stream(state.stream)
         return state.logits
+
+    def decode_greedy(self, token_id: int, state: CudaDecodeState) -> int:
+        """forward_token + argmax with the token ids on the host: consumes
+        `token_id` and returns the greedy next token (the logits stay in
+        state.logits), in one library call per token."""
+        self._check(token_id, state)
+        state.stream.wait_stream(torch.cuda.current_stream(self.device))
+        return state.greedy_token(token_id)
 
     def prefill(self, token_ids, state: CudaDecodeState, max_tokens: int = 2048,
                 attn_splits: int = 1, attention: str = "tensor") -> torch.Tensor:

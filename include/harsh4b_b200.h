@@ -265,6 +265,13 @@ int h4b_graph_create(const h4b_model *model, const h4b_state *state, void *strea
 int h4b_graph_create_persistent(const h4b_model *model, const h4b_state *state, void *stream,
                                 void **graph_out);
 int h4b_graph_launch(void *graph, void *stream);
+/* One greedy token with a host round trip, for a caller that feeds each
+ * token from the host (forward_token + argmax, cpu_lightspark.py:424-468,
+ * 704-705): copies the token id from token_host (pinned) to token_dev, launches
+ * the graph, copies the graph's greedy token from next_dev to next_host
+ * (pinned) and waits for the stream. */
+int h4b_graph_token(void *graph, const int32_t *token_host, int32_t *token_dev, const int32_t *next_dev,
+                    int32_t *next_host, void *stream);
 int h4b_graph_destroy(void *graph);
 
 /* ---- batched decode (B sequences, one token each per call) ----------------

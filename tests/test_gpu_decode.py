@@ -87,6 +87,31 @@ def test_device_side_greedy_loop_matches_host_loop(tiny):
     assert state.position == len(prompt) + 11
 
 
+def test_decode_greedy_host_round_trip_matches_forward_token(tiny):
+    """decode_greedy (one h4b_graph_token call per token: pinned copy in,
+    graph, copy out, wait) gives the greedy tokens and the logits of
+    forward_token + argmax."""
+    checkpoint, prompt = tiny
+    model = CudaQwen.from_checkpoint(checkpoint)
+    _, greedy = cuda_decode(model, prompt, 12)
+    state = model.new_state(len(prompt) + 12)
+    for token in prompt[:-1]:
+        model.forward_token(token, state)
+    tokens = [model.decode_greedy(prompt[-1], state)]
+    for _ in range(11):
+        tokens.append(model.decode_greedy(tokens[-1], state))
+    assert tokens == list(greedy[:12])
+    assert state.position == len(prompt) + 11
+    reference = model.new_state(len(prompt) + 12)
+    for token in prompt:
+        model.forward_token(token, reference)
+    for token in tokens[:11]:
+        logits = model.forward_token(token, reference)
+    np.testing.assert_array_equal(state.logits.cpu().numpy(), logits.cpu().numpy())
+    with pytest.raises(ValueError):
+        model.decode_greedy(model.vocab, state)
+
+
 def test_reference_golden_decode_on_device():
     """Logits recorded from the reference's own LiteSparkQwen.forward_token."""
     golden = np.load(GOLDEN)
