@@ -465,11 +465,14 @@ int launch_batch_attention_tc(const h4b_model* m, const h4b_batch_state* s, int 
     if (!batch_cache_map(&kmap, kc, m->kv_heads, B, s->capacity, batch_stride) ||
         !batch_cache_map(&vmap, vc, m->kv_heads, B, s->capacity, batch_stride))
         return H4B_EUNSUPPORTED;
-    // splits: enough CTAs for about two per SM, at most the state's count
-    // (its partials are sized for that); whole-sequence CTAs when the batch
-    // alone fills the GPU
+    // splits: one wave of CTAs (one fits per SM) when the batch's (sequence,
+    // kv head) pairs leave at least half the SMs idle, else about two CTAs per
+    // SM; at most the state's count (its partials are sized for that);
+    // whole-sequence CTAs when the batch alone fills the GPU
     const int units = B * m->kv_heads;
-    const int splits = std::max(1, std::min(s->attn_splits, (2 * sm_count() + units - 1) / units));
+    const int splits =
+        std::max(1, std::min(s->attn_splits, 2 * units <= sm_count() ? sm_count() / units
+                                                                       : (2 * sm_count() + units - 1) / units));
     const DtcArgs a{s->qkv, qkv_rows, s->positions, splits, m->kv_heads, s->capacity, s->attn_partials, s->attended,
                     q_size};
     decode_attention_tc_kernel<<<dim3(splits, m->kv_heads, B), kDtcThreads, kDtcSmem, stream>>>(kmap, vmap, a);

@@ -201,8 +201,9 @@ class CudaBatchState:
     attention="exact": the fp32 split kernel with `attn_splits` splits, each
     row bit-identical to a decode step. attention="tensor" (the default; fp16
     cache, head_dim 128, 4 q heads per kv head, otherwise as "exact"): tcgen05
-    attention with split fp16 operands over whole 128-key tiles (about two
-    CTAs per SM, at most `attn_splits` splits), within the 1e-3 relative
+    attention with split fp16 operands over whole 128-key tiles (one wave of
+    CTAs for small batches, about two per SM otherwise, at most `attn_splits`
+    splits), within the 1e-3 relative
     tolerance of the fp32 path."""
 
     def __init__(self, model: "CudaQwen", batch: int, capacity: int, attn_splits: int = 16,

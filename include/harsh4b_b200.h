@@ -301,7 +301,8 @@ typedef struct h4b_batch_state {
     /* H4B_BATCH_ATTN_EXACT (0): the fp32 split kernel, each row bit-identical
      * to a decode step. H4B_BATCH_ATTN_TENSOR (1): tcgen05 attention with
      * split-fp16 operands (fp32 outputs within the 1e-3 relative tolerance)
-     * over splits of whole 128-key tiles (about two CTAs per SM, at most
+     * over splits of whole 128-key tiles (one wave of CTAs for small batches,
+     * about two per SM otherwise, at most
      * attn_splits), where the cache is fp16, head_dim 128 and 4 q heads share
      * a kv head; else as 0. */
     int attn_kernel;
