@@ -45,9 +45,10 @@ constexpr int kTcGroupWarps = 4;  // an unpack group: one warp per TMEM lane qua
 
 template <int TOK>
 struct TcCfg {
-    // Unpack groups: group g owns the k-steps g, g + kGroups, ... and one
-    // unpacked weight tile in tensor memory. The stage count is a multiple of
-    // the groups, so a group always revisits its own stages round by round.
+    // Unpack groups: group g owns the k-steps g, g + kGroups, ... and with
+    // them the TMA stages and unpacked tiles g, g + kGroups, ... (the stage
+    // count is a multiple of the groups, so a group always revisits its own
+    // stages round by round).
     static constexpr int kGroups = TOK == 256 ? 5 : 4;
     // Unpacked weight tiles in tensor memory: two per group below TOK 256, so
     // a group expands its next stage while the MMAs still read its previous
