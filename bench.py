@@ -78,6 +78,9 @@ def parse_args():
                         help="batch workload: the tcgen05 attention (tolerance) or the decode-order fp32 one")
     parser.add_argument("--batch-splits", type=int, default=16,
                         help="batch workload: attention splits per sequence (the tensor kernel: at most this)")
+    parser.add_argument("--kernel-shares", action="store_true",
+                        help="batch workload: add the per-kernel device-time shares of 2 more steps (torch "
+                             "profiler, CUDA activity), taken after the timed regions")
     parser.add_argument("--context", type=int, default=4096, help="tp workload: context before decoding")
     parser.add_argument("--layers", type=int, default=None,
                         help="override the layer count (a smaller model for profiling captures; not the headline)")
@@ -620,7 +623,7 @@ def run_batch(args, rank=0, world=1, local_rank=0, dist=None) -> int:
                                      mode="chain")
     rng = np.random.default_rng([args.seed, B, P, rank])
     prompts = rng.integers(0, model.vocab, size=(B, P))
-    capacity = P + 2 * (args.warmup + args.steps) + 2
+    capacity = P + 2 * (args.warmup + args.steps) + 2 + (2 if args.kernel_shares else 0)
     splits = args.batch_splits
     state = model.new_batch_state(B, capacity, attn_splits=splits, attention=args.batch_attention)
     t0 = time.perf_counter()
@@ -666,6 +669,7 @@ def run_batch(args, rank=0, world=1, local_rank=0, dist=None) -> int:
     status = model.status()
     if rank != 0:
         return 0
+    shares = kernel_shares(torch, lambda: model.generate_batch(state, 2), 2) if args.kernel_shares else None
     kv_bytes = 2 if args.kv_dtype == "float16" else 4
     per_pos = model.n_layers * 2 * model.kv_size * kv_bytes
     mean_ctx = ctx0 + (args.steps + 1) / 2
@@ -690,8 +694,36 @@ def run_batch(args, rank=0, world=1, local_rank=0, dist=None) -> int:
                      "peak_source": peaks["source"]},
         "clocks": clocks.summary(), "device_status": status,
     }
+    if shares is not None:
+        line["kernel_shares"] = shares
     print(json.dumps(line), flush=True)
     return 0
+
+
+def kernel_shares(torch, fn, steps: int) -> dict:
+    """Per-kernel device time of `fn` (torch profiler, CUDA activity): per
+    kernel name its launches and microseconds per step and its share of all
+    the kernels' time. Taken under a profiler, so only the shares are read;
+    the bench's timings come from CUDA events."""
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    totals = {}
+    for event in prof.events():
+        if event.device_type != torch.autograd.DeviceType.CUDA:
+            continue
+        name = event.name.split("(")[0].replace("void ", "").strip()
+        if "int4_gemm_tc" not in name:
+            name = name.split("<")[0]
+        entry = totals.setdefault(name, [0, 0.0])
+        entry[0] += 1
+        entry[1] += event.device_time_total
+    whole = sum(t for _, t in totals.values()) or 1.0
+    return {name: {"launches_per_step": n / steps, "us_per_step": round(t / steps, 1), "share": round(t / whole, 4)}
+            for name, (n, t) in sorted(totals.items(), key=lambda kv: -kv[1][1])}
 
 
 def run_prefill(args) -> int:
